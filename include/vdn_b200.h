@@ -1,0 +1,183 @@
+/* vdn_b200: B200-native (sm_100a) kernels for the VDN-H3 hybrid-attention DiT
+ * block hot path, behind a plain C ABI.
+ *
+ * Every entry point takes raw device pointers, element counts and strides, and a
+ * cudaStream_t (pass the caller's current stream; 0 is the legacy default
+ * stream).  Nothing here allocates device memory: outputs and workspaces are
+ * owned by the caller.  Every function returns VDN_OK (0) or an error code; the
+ * message of the last error on the calling thread is vdn_last_error().  Bad
+ * metadata is reported before any launch.  Launches are asynchronous; a device
+ * fault surfaces at the caller's next synchronisation.
+ *
+ * Citations name the reference (ec-jt/vdn) interface each entry point replaces,
+ * as path:line within that project.
+ */
+#ifndef VDN_B200_H
+#define VDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VDN_ABI_VERSION 1
+
+/* Status codes.  The Python layer maps VALUE -> ValueError, TYPE -> TypeError,
+ * NONFINITE -> ValueError("nonfinite MXFP8 ..."), RUNTIME/TIMEOUT -> RuntimeError. */
+#define VDN_OK 0
+#define VDN_ERR_VALUE 1
+#define VDN_ERR_TYPE 2
+#define VDN_ERR_RUNTIME 3
+#define VDN_ERR_NONFINITE 4
+#define VDN_ERR_TIMEOUT 5
+
+/* Element types for the dtype arguments. */
+#define VDN_DTYPE_F32 0
+#define VDN_DTYPE_BF16 1
+#define VDN_DTYPE_F16 2
+
+/* Activations of vdn_mxfp8_act_quantize. */
+#define VDN_ACT_GELU_TANH 1
+#define VDN_ACT_GELU_ERF 2
+#define VDN_ACT_SWIGLU 3
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* vdn_last_error(void);
+int vdn_abi_version(void);
+/* *supported = 1 when `device` is an sm_100 part this library was built for. */
+int vdn_device_supported(int device, int* supported);
+
+/* ------------------------------------------------------------------ MXFP8 */
+
+/* Rows and K rounded up to multiples of 128.
+ * Replaces padded_shape / scale_numel, src/models/ops/mxfp8_quant.py:15-23. */
+int vdn_mxfp8_padded_shape(int64_t rows, int64_t k, int64_t* rows_padded, int64_t* k_padded);
+
+/* bf16 [rows, k] (row_stride elements, K contiguous) -> E4M3 codes q [RP, KP]
+ * (row-major, padding = exact zero) and E8M0 scales s [RP*KP/32] in the
+ * SWIZZLE_32_4_4 layout.  Bit-exact with the reference rule.  When `nonfinite`
+ * is not null, the count of 32-blocks holding a NaN/Inf input is ADDED to it.
+ * Replaces quantize_activation / launch_quantize,
+ * src/models/ops/mxfp8_quant.py:77-90, src/models/ops/mxfp8_kernels.py:30-58. */
+int vdn_mxfp8_quantize(const void* x, int64_t rows, int64_t k, int64_t row_stride,
+                       uint8_t* q, uint8_t* s, int* nonfinite, cudaStream_t stream);
+
+/* Fused activation producer: act(x) rounded to bf16, then quantised as above.
+ * act = VDN_ACT_GELU_TANH / VDN_ACT_GELU_ERF read x [rows, k]; VDN_ACT_SWIGLU
+ * reads x [rows, 2k] as (a | g) and produces a * silu(g).
+ * Replaces launch_swiglu_quantize, src/models/ops/mxfp8_kernels.py:61-124,
+ * 203-214 (the GELU forms are this build's analogue for a GELU FFN). */
+int vdn_mxfp8_act_quantize(int act, const void* x, int64_t rows, int64_t k, int64_t row_stride,
+                           uint8_t* q, uint8_t* s, int* nonfinite, cudaStream_t stream);
+
+/* RMSNorm(x) * weight * (1 + scale[idx]) + shift[idx] -> bf16 (optionally
+ * stored to y [rows, k] when y != NULL) -> MXFP8 codes/scales, plus a per-padded-
+ * row finite byte finite[RP].  x, scale, shift bf16; weight fp32 or bf16;
+ * indices int64 [rows].
+ * Replaces launch_prenorm_quantize, src/models/ops/mxfp8_kernels.py:86-139, 217-229. */
+int vdn_mxfp8_prenorm_quantize(const void* x, int64_t rows, int64_t k, int64_t x_stride,
+                               const void* weight, int weight_dtype, float eps,
+                               const void* scale, int64_t scale_stride, const void* shift,
+                               int64_t shift_stride, const int64_t* indices, void* y,
+                               uint8_t* q, uint8_t* s, uint8_t* finite, cudaStream_t stream);
+
+/* One finite byte per 4096 elements: mode 0 float (dtype), 1 E4M3 codes
+ * ((x & 127) != 127), 2 E8M0 bytes (x != 255).
+ * Replaces finite_parts, src/models/ops/mxfp8_kernels.py:142-162. */
+int vdn_finite_parts(const void* x, int64_t n, int dtype, int mode, uint8_t* parts,
+                     cudaStream_t stream);
+
+/* Host (CPU) weight quantiser, multithreaded; same outputs as the device
+ * quantiser.  Returns VDN_ERR_NONFINITE on a NaN/Inf weight.
+ * Replaces quantize_cpu, src/models/ops/mxfp8_quant.py:40-74. */
+int vdn_mxfp8_quantize_host(const void* x, int dtype, int64_t rows, int64_t k,
+                            int64_t row_stride, uint8_t* q, uint8_t* s, int num_threads);
+
+/* Block-scaled MXFP8 GEMM on tcgen05 (kind::mxf8f6f4, scale_vec::1X):
+ *   y[:rows_out, :n] = bf16(dequant(xq, xs) @ dequant(wq, ws)^T) (+ bias[n] bf16)
+ * xq [m_pad, k_pad] / wq [n_pad, k_pad] E4M3 codes, xs / ws swizzled E8M0
+ * scales, m_pad, n_pad, k_pad multiples of 128.  y bf16 with row stride ldy.
+ * Replaces MXFP8Linear.forward_quantized, src/models/ops/mxfp8_linear.py:60-93
+ * (F.scaled_mm BlockWise1x32 / SWIZZLE_32_4_4). */
+int vdn_mxfp8_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, const uint8_t* ws,
+                   const void* bias, int64_t m_pad, int64_t n, int64_t n_pad, int64_t k_pad,
+                   int64_t rows_out, void* y, int64_t ldy, cudaStream_t stream);
+
+/* -------------------------------------------------------------------- VDA */
+
+/* Per (frame, head) delta-rule factors, d in {64, 128}, n matrices:
+ *   T = diag(alpha) (I + A)^-1,  J = B (I + A)^-1    (alpha NULL = ones)
+ * A, B, T, J fp32 [n, d, d]; alpha fp32 [n, d].  I + A must be SPD.
+ * Replaces paper_delta_factors, src/models/linear_attention/paper_factor.py:133-186,
+ * and VdnDelta.factor_apply, src/models/linear_attention/delta_rule.py:45-60. */
+int vdn_delta_factors(const float* A, const float* B, const float* alpha, int64_t n, int d,
+                      float* T, float* J, cudaStream_t stream);
+
+/* Frame statistics from RAW projections (SiLU + L2 over d for k, SiLU for v,
+ * rounded to bf16 as the feature path does, then multiplied by beta):
+ *   A[f,h] = sym(sum_s (k beta)(k)^T) fp32,  B[f,h] = bf16(sum_s bf16(v beta) k^T)
+ * Element (f, s, h, :) of k / v / beta lives at f*stride_f + s*stride_s + h*stride_h
+ * (elements; d contiguous for k and v).  A, B fp32 [F, H, d, d].
+ * Replaces frame_statistics, src/models/linear_attention/scan.py:113-267, and
+ * paper_statistics, src/models/linear_attention/paper_stack.py:51-110. */
+int vdn_vda_statistics(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh,
+                       const void* v, int64_t v_sf, int64_t v_ss, int64_t v_sh,
+                       const void* beta, int64_t b_sf, int64_t b_ss, int64_t b_sh,
+                       int features_applied, int F, int S, int H, int d,
+                       float* A, float* B, cudaStream_t stream);
+
+/* Forward and reverse scans s_t = s_{t-1} T_t + J_t over F frames, started from
+ * seed [H, d, d] (NULL = zero).  prefix / suffix fp32 [F, H, d, d].
+ * Replaces _run_scans / _run_scans_inference, src/models/linear_attention/scan.py:270-355. */
+int vdn_vda_scan(const float* T, const float* J, const float* seed, int F, int H, int d,
+                 float* prefix, float* suffix, cudaStream_t stream);
+
+/* State outside each frame's inclusive window [lo, hi] (bounds: host int32
+ * [F][2], F <= 1024), decayed into the frame by prod(alpha) when bridge != 0:
+ *   out[t] = prefix[lo-1] * prod_{lo..t} alpha + suffix[hi+1] * prod_{t..hi} alpha
+ * with the seed (or zero) past the clip ends.  out [F, H, d, d], out_dtype
+ * VDN_DTYPE_F32 or VDN_DTYPE_BF16.
+ * Replaces gather_linear_state, src/models/linear_attention/scan.py:361-496, and
+ * paper_gather, src/models/linear_attention/paper_stack.py:239-263. */
+int vdn_vda_gather(const float* prefix, const float* suffix, const float* alpha,
+                   const int32_t* bounds, const float* seed, int bridge, int F, int H, int d,
+                   void* out, int out_dtype, cudaStream_t stream);
+
+/* Readout and epilogue: q features (SiLU + L2, bf16) times state^T (bf16
+ * [F, H, d, d]), RMSNorm over d (eps) times norm_weight (fp32 [d]) times gate,
+ * stored token-major out [F*S, H*d] bf16.  q and gate addressing as in
+ * vdn_vda_statistics.
+ * Replaces the readout + linear_epilogue of branch.py:470-482 / 560-563 and
+ * vdn_linear_epilogue, src/models/linear_attention/paper_sglang.py:377-437. */
+int vdn_vda_readout(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh,
+                    const void* state, const void* gate, int64_t g_sf, int64_t g_ss, int64_t g_sh,
+                    const float* norm_weight, float eps, int F, int S, int H, int d,
+                    void* out, cudaStream_t stream);
+
+/* Workspace bytes vdn_vda_forward needs for this geometry. */
+size_t vdn_vda_workspace_size(int F, int S, int H, int d);
+
+/* The whole VDA branch body over the frames it owns: statistics, factors,
+ * bidirectional scans, boundary gather, readout, RMSNorm and gate.
+ * q, k, v [F*S, H, d] bf16 with token stride qkv_ss and head stride qkv_sh
+ * (shared by the three), beta [F*S, H] bf16 (b_ss, b_sh), gate [F*S, H, d] bf16
+ * (g_ss, g_sh), alpha fp32 [F, H, d] contiguous, norm_weight fp32 [d], bounds
+ * host int32 [F][2], seed fp32 [H, d, d] or NULL, out bf16 [F*S, H*d].
+ * Replaces BidirectionalLinearBranch._readout / _readout_inference / paper_readout,
+ * src/models/linear_attention/branch.py:404-563, paper_stack.py:266-318. */
+int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss, int64_t qkv_sh,
+                    const void* beta, int64_t b_ss, int64_t b_sh,
+                    const void* gate, int64_t g_ss, int64_t g_sh,
+                    const float* alpha, const float* norm_weight, float eps,
+                    const int32_t* bounds, const float* seed, int bridge,
+                    int F, int S, int H, int d, void* out,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VDN_B200_H */

@@ -1,0 +1,154 @@
+"""Generate the golden fixtures under tests/golden/ from the REFERENCE's own CPU code.
+
+Run once, in a container where the reference checkout is importable:
+
+    python tests/golden/make_golden.py /path/to/vdn/checkout
+
+It imports the reference (ec-jt/vdn) and records, on seeded synthetic inputs:
+  * quantize_cpu codes/scales (src/models/ops/mxfp8_quant.py:40-74) for the
+    BASELINE config-0 256x256 matrix, odd shapes, an outlier matrix and the
+    exponent-boundary known-answer vector;
+  * the eager VDA body BidirectionalLinearBranch._readout
+    (src/models/linear_attention/branch.py:404-482) with alpha injected, at the
+    BASELINE config-0 geometry (F=4, S=64, H=4, d=64) and at d=128 with and
+    without the text seed and the anchor frames;
+  * the stage functions frame_statistics, VdnDelta.factor_apply, _run_scans and
+    gather_linear_state (scan.py, delta_rule.py) on one d=128 case.
+
+Nothing at test time reads the reference; the tests read only these .npz files.
+"""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    """bf16 tensor -> uint16 bit patterns."""
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def mxfp8_fixtures(quantize_cpu):
+    out = {}
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(256, 256, generator=g).bfloat16()
+    q, s = quantize_cpu(x)
+    out.update(cfg0_x=bits(x), cfg0_q=q.numpy(), cfg0_s=s.numpy())
+    for i, shape in enumerate([(1, 1), (3, 31), (127, 32), (129, 129), (9, 256), (130, 300)]):
+        x = torch.randn(shape, generator=g).bfloat16()
+        q, s = quantize_cpu(x, chunk_rows=7)
+        out[f"shape{i}_x"], out[f"shape{i}_q"], out[f"shape{i}_s"] = bits(x), q.numpy(), s.numpy()
+    # BASELINE config-1 activation distribution: N(0,1) with 1% of channels x50.
+    x = torch.randn(200, 640, generator=g)
+    idx = torch.randperm(640, generator=g)[:640 // 100]
+    x[:, idx] *= 50
+    x = x.bfloat16()
+    q, s = quantize_cpu(x)
+    out.update(outlier_x=bits(x), outlier_q=q.numpy(), outlier_s=s.numpy())
+    # Exponent boundaries (reference test_paper_stack_mxfp8_ops.py:67-78), plus
+    # subnormal, negative-zero and mixed-sign rows.
+    kat = torch.tensor([0., 224., 448., 449., 896., 1e-38, -3.0e-39, -0.0, 1.75, -1.7501],
+                       dtype=torch.float32)[:, None].expand(-1, 32).contiguous()
+    kat[8, ::2] *= -1
+    q, s = quantize_cpu(kat)
+    out.update(kat_x=kat.numpy(), kat_q=q.numpy(), kat_s=s.numpy())
+    np.savez_compressed(HERE / "mxfp8_golden.npz", **out)
+
+
+def vda_case(branch_cls, f, s, h, d, seed, text_len=0, skip_ends=False, radius=1):
+    g = torch.Generator().manual_seed(seed)
+    n = f * s
+
+    def raw_qk():
+        # BASELINE: q,k ~ N(0,1) bf16, L2-normalised per head, then given to the op.
+        return F.normalize(torch.randn(n, h, d, generator=g), dim=-1).bfloat16()
+
+    q, k = raw_qk(), raw_qk()
+    v = torch.randn(n, h, d, generator=g).bfloat16()
+    beta = torch.sigmoid(torch.randn(n, h, generator=g)).bfloat16()
+    gate = torch.rand(n, h, d, generator=g).bfloat16()
+    # log alpha = -softplus(N(0,1)) per (frame, head), broadcast over d_k.
+    alpha = torch.exp(-F.softplus(torch.randn(f, h, 1, generator=g))).expand(f, h, d).contiguous()
+    bounds = [(t - radius, t + radius) for t in range(f)]
+    text = {}
+    if text_len:
+        tq, tk = (F.normalize(torch.randn(text_len, h, d, generator=g), dim=-1).bfloat16()
+                  for _ in range(2))
+        tv = torch.randn(text_len, h, d, generator=g).bfloat16()
+        tb = torch.sigmoid(torch.randn(text_len, h, generator=g)).bfloat16()
+        text = dict(text_qkv_raw=(tq, tk, tv), text_beta=tb)
+    hidden = 16
+    branch = branch_cls(hidden, h, d, delta_rule="vdn_solve").eval()
+    branch.alpha.forward = lambda frame_mean, heads=None: alpha[1:-1] if (
+        skip_ends and frame_mean.shape[0] == f - 2) else alpha
+    with torch.no_grad():
+        out = branch(None, f, s, bounds, (q, k, v), skip_ends=skip_ends,
+                     heads=slice(0, h), beta=beta, gate=gate,
+                     frame_mean=torch.zeros(f, hidden), **text)
+    rec = dict(q=bits(q), k=bits(k), v=bits(v), beta=bits(beta), gate=bits(gate),
+               alpha=alpha.numpy(), bounds=np.array(bounds, np.int64),
+               geometry=np.array([f, s, h, d, int(skip_ends), text_len], np.int64),
+               out=bits(out))
+    if text_len:
+        rec.update(tk=bits(text["text_qkv_raw"][1]), tv=bits(text["text_qkv_raw"][2]),
+                   tbeta=bits(text["text_beta"]))
+    return rec
+
+
+def stage_fixtures(scan, delta):
+    g = torch.Generator().manual_seed(5)
+    f, h, s, d = 5, 1, 40, 128
+    k = F.normalize(F.silu(torch.randn(f, h, s, d, generator=g)), dim=-1).bfloat16()
+    v = F.silu(torch.randn(f, h, s, d, generator=g)).bfloat16()
+    beta = torch.sigmoid(torch.randn(f, h, s, generator=g)).bfloat16()
+    alpha = (torch.rand(f, h, d, generator=g) * 0.5 + 0.45).float()
+    with torch.no_grad():
+        a, b = scan.frame_statistics(k, v, beta, a_fp32=True)
+        t, j = delta.VdnDelta().factor_apply(alpha, a, b)
+        seed = torch.randn(h, d, d, generator=g) * 0.1
+        prefix, suffix = scan._run_scans(delta.VdnDelta(), alpha, a, b, text_state=seed)
+        bounds = [(t_ - 1, t_ + 2) for t_ in range(f)]
+        gathered = scan.gather_linear_state(prefix, suffix, alpha, bounds, text_state=seed)
+        gathered0 = scan.gather_linear_state(prefix, suffix, alpha, bounds, text_state=None)
+    np.savez_compressed(
+        HERE / "vda_stages_golden.npz", k=bits(k), v=bits(v), beta=bits(beta),
+        alpha=alpha.numpy(), a=a.numpy(), b=b.numpy(), t=t.numpy(), j=j.numpy(),
+        seed=seed.numpy(), prefix=prefix.numpy(), suffix=suffix.numpy(),
+        bounds=np.array(bounds, np.int64), gathered=gathered.numpy(),
+        gathered_noseed=gathered0.numpy())
+
+
+def main(ref_root: str):
+    sys.path.insert(0, ref_root)
+    from src.models.ops.mxfp8_quant import quantize_cpu
+    from src.models.linear_attention import scan, delta_rule
+    from src.models.linear_attention.branch import BidirectionalLinearBranch
+
+    torch.set_num_threads(8)
+    mxfp8_fixtures(quantize_cpu)
+    cases = {
+        "cfg0": dict(f=4, s=64, h=4, d=64, seed=10),
+        "d128": dict(f=5, s=40, h=2, d=128, seed=11),
+        "d128_text": dict(f=5, s=24, h=2, d=128, seed=12, text_len=7),
+        "d128_anchor": dict(f=6, s=16, h=2, d=128, seed=13, skip_ends=True),
+        "d128_wide": dict(f=7, s=20, h=3, d=128, seed=14, radius=2),
+    }
+    recs = {}
+    for name, kw in cases.items():
+        for key, val in vda_case(BidirectionalLinearBranch, **kw).items():
+            recs[f"{name}_{key}"] = val
+    np.savez_compressed(HERE / "vda_golden.npz", **recs)
+    stage_fixtures(scan, delta_rule)
+    print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py <path to the ec-jt/vdn checkout>")
+    main(sys.argv[1])

@@ -1,0 +1,459 @@
+// MXFP8 producers for sm_100a: block-32 E4M3 codes with one E8M0 scale per 32
+// K-elements, scales stored in the SWIZZLE_32_4_4 layout the tcgen05 block-scaled
+// MMA consumes directly (one 512-byte atom = 128 rows x 4 scale columns).
+//
+// Reference rule (ec-jt/vdn src/models/ops/mxfp8_quant.py:64-73,
+// src/models/ops/mxfp8_kernels.py:14-58):
+//   e0 = biased_exp(amax) - 135, thr = 1.75 * 2^(e0+8),
+//   e = max(e0 + (amax > thr), -127), code = e4m3_rne(x * 2^-e), byte = e + 127.
+// The multiply by 2^-e is exact and denormals are never flushed (this file is
+// compiled without -ftz), so the codes are bit-identical to the reference.
+//
+// Kernels here are HBM-bound; one thread owns one 32-element block (64 input
+// bytes, 32 code bytes) and lanes 4i..4i+3 pack their scale bytes into one
+// 32-bit store, because four consecutive K-blocks of a row are contiguous in
+// the swizzled layout.
+#include "common.cuh"
+
+#include <math.h>
+#include <string.h>
+#include <algorithm>
+#include <cmath>
+#include <thread>
+#include <vector>
+
+namespace vdn {
+
+// E8M0 exponent rule on the bit pattern of a non-negative fp32 amax.
+// Returns the scale byte and writes the exact multiplier 2^-e.
+__host__ __device__ __forceinline__ uint32_t e8m0_from_amax_bits(uint32_t ab, float* inv) {
+  const int biased = (int)((ab >> 23) & 255u);
+  const int e0 = biased - 135;
+  const uint32_t thr = ((uint32_t)biased << 23) | 0x600000u;
+  int e = e0 + (ab > thr ? 1 : 0);  // positive floats order like their bit patterns
+  if (e < -127) e = -127;
+  const uint32_t inv_bits = (uint32_t)(127 - e) << 23;
+  float f;
+  memcpy(&f, &inv_bits, 4);
+  *inv = f;
+  return (uint32_t)(e + 127);
+}
+
+// fp32 -> float8_e4m3fn, round to nearest even, two at a time (hi -> upper byte).
+__device__ __forceinline__ uint16_t e4m3x2(float hi, float lo) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+  // byte 0 = a, byte 1 = b, byte 2 = c, byte 3 = d (little-endian row order)
+  return (uint32_t)e4m3x2(b, a) | ((uint32_t)e4m3x2(d, c) << 16);
+}
+
+__device__ __forceinline__ int64_t scale_offset(int64_t r, int64_t c, int64_t kp) {
+  return ((r >> 7) * (kp >> 7) + (c >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (c & 3);
+}
+
+enum Act { ACT_NONE = 0, ACT_GELU_TANH = 1, ACT_GELU_ERF = 2, ACT_SWIGLU = 3 };
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float inner = k0 * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
+}
+
+// Loads the 32 inputs of block (r, c) as fp32, zero outside [rows, k).
+template <bool VEC>
+__device__ __forceinline__ void load_block(const uint16_t* __restrict__ x, int64_t row_stride,
+                                           int64_t r, int64_t c, int64_t rows, int64_t k,
+                                           float* v) {
+  const int64_t col0 = c * 32;
+  if (r < rows && VEC && col0 + 32 <= k) {
+    const uint4* p = reinterpret_cast<const uint4*>(x + r * row_stride + col0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) unpack8(__ldg(p + i), v + 8 * i);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int64_t col = col0 + i;
+      v[i] = (r < rows && col < k) ? bf16_bits_to_f32(x[r * row_stride + col]) : 0.0f;
+    }
+  }
+}
+
+// One 32-element block: activation, bf16 rounding (when an activation ran), scale,
+// codes, and the finite predicate of the inputs and the produced values.
+template <int ACT, bool VEC>
+__global__ void __launch_bounds__(256) act_quantize_kernel(
+    const uint16_t* __restrict__ x, int64_t row_stride, int64_t rows, int64_t k, int64_t rp,
+    int64_t kp, uint8_t* __restrict__ q, uint8_t* __restrict__ s, int* __restrict__ nonfinite) {
+  const int64_t nblk = kp >> 5;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool active = g < rp * nblk;
+  const int64_t r = active ? g / nblk : 0;
+  const int64_t c = active ? g - r * nblk : 0;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+  bool bad = false;
+  if (active) {
+    load_block<VEC>(x, row_stride, r, c, rows, k, v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) bad |= !isfinite(v[i]);
+    if (ACT == ACT_SWIGLU) {
+      float gte[32];
+      load_block<VEC>(x + k, row_stride, r, c, rows, k, gte);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        bad |= !isfinite(gte[i]);
+        // a * (g * sigmoid(g)) rounded to bf16, no contraction (reference
+        // src/models/ops/mxfp8_kernels.py:61-74).
+        const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gte[i])));
+        v[i] = round_bf16(__fmul_rn(v[i], __fmul_rn(gte[i], sg)));
+        bad |= !isfinite(v[i]);
+      }
+    } else if (ACT == ACT_GELU_TANH || ACT == ACT_GELU_ERF) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        v[i] = round_bf16(ACT == ACT_GELU_TANH ? gelu_tanh(v[i]) : gelu_erf(v[i]));
+        bad |= !isfinite(v[i]);
+      }
+    }
+  }
+  uint32_t amax_bits = 0;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint32_t b = __float_as_uint(v[i]) & 0x7FFFFFFFu;
+    amax_bits = b > amax_bits ? b : amax_bits;
+  }
+  float inv;
+  const uint32_t sbyte = e8m0_from_amax_bits(amax_bits, &inv);
+  // Pack four scale bytes of c..c+3 (same row: nblk % 4 == 0) into one word.
+  const unsigned lane = threadIdx.x & 31;
+  uint32_t word = sbyte << (8 * (lane & 3));
+  word |= __shfl_xor_sync(0xffffffffu, word, 1);
+  word |= __shfl_xor_sync(0xffffffffu, word, 2);
+  if (!active) return;
+  uint32_t packed[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    packed[i] = e4m3x4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv, v[4 * i + 3] * inv);
+  uint4* qp = reinterpret_cast<uint4*>(q + r * kp + c * 32);
+  qp[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  qp[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(s + scale_offset(r, c, kp)) = word;
+  if (bad && nonfinite) atomicAdd(nonfinite, 1);
+}
+
+// RMSNorm * w, AdaLN affine (1 + scale[idx]) and shift[idx], bf16 rounding, then
+// MXFP8 of that bf16 value. One CTA per padded row; rows past `rows` quantise
+// exact zeros (reference src/models/ops/mxfp8_kernels.py:86-139).
+template <typename WT>
+__global__ void __launch_bounds__(256) prenorm_quantize_kernel(
+    const uint16_t* __restrict__ x, int64_t xs, const WT* __restrict__ w,
+    const uint16_t* __restrict__ scale, int64_t ss, const uint16_t* __restrict__ shift,
+    int64_t ts, const int64_t* __restrict__ idx, int64_t rows, int64_t k, int64_t kp, float eps,
+    uint16_t* __restrict__ y, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
+    uint8_t* __restrict__ finite) {
+  const int64_t r = blockIdx.x;
+  const bool valid_row = r < rows;
+  __shared__ float red[8];
+  __shared__ int bad_any;
+  if (threadIdx.x == 0) bad_any = 0;
+  float sq = 0.f;
+  bool bad = false;
+  if (valid_row) {
+    for (int64_t col = threadIdx.x; col < k; col += blockDim.x) {
+      const float xv = bf16_bits_to_f32(x[r * xs + col]);
+      sq += xv * xv;
+      bad |= !isfinite(xv);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float inv_rms = rsqrtf(tot / (float)k + eps);
+  const int64_t t = valid_row ? idx[r] : 0;
+  const int64_t nblk = kp >> 5;
+  for (int64_t c0 = 0; c0 < nblk; c0 += blockDim.x) {
+    const int64_t c = c0 + threadIdx.x;
+    const bool active = c < nblk;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int64_t col = c * 32 + i;
+      float val = 0.f;
+      if (active && valid_row && col < k) {
+        const float xv = bf16_bits_to_f32(x[r * xs + col]);
+        const float wv = (float)w[col];
+        const float sc = bf16_bits_to_f32(scale[t * ss + col]);
+        const float sh = bf16_bits_to_f32(shift[t * ts + col]);
+        val = round_bf16(__fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(xv, inv_rms), wv),
+                                             __fadd_rn(1.0f, sc)), sh));
+        bad |= !isfinite(val);
+        if (y) y[r * k + col] = f32_to_bf16_bits(val);
+      }
+      v[i] = val;
+    }
+    uint32_t amax_bits = 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const uint32_t b = __float_as_uint(v[i]) & 0x7FFFFFFFu;
+      amax_bits = b > amax_bits ? b : amax_bits;
+    }
+    float inv;
+    const uint32_t sbyte = e8m0_from_amax_bits(amax_bits, &inv);
+    if (active) {
+      uint32_t packed[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        packed[i] = e4m3x4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv, v[4 * i + 3] * inv);
+      uint4* qp = reinterpret_cast<uint4*>(q + r * kp + c * 32);
+      qp[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      qp[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+      s[scale_offset(r, c, kp)] = (uint8_t)sbyte;
+    }
+  }
+  if (bad) bad_any = 1;
+  __syncthreads();
+  if (threadIdx.x == 0) finite[r] = bad_any ? 0 : 1;
+}
+
+// Per-4096-element finite predicate (reference src/models/ops/mxfp8_kernels.py:142-162).
+template <typename T, int MODE>
+__global__ void finite_parts_kernel(const T* __restrict__ x, int64_t n, uint8_t* __restrict__ parts) {
+  const int64_t base = (int64_t)blockIdx.x * 4096;
+  int good = 1;
+  for (int64_t i = base + threadIdx.x; i < base + 4096 && i < n; i += blockDim.x) {
+    if (MODE == 1) good &= ((uint32_t)x[i] & 127u) != 127u;
+    else if (MODE == 2) good &= (uint32_t)x[i] != 255u;
+    else good &= isfinite((float)x[i]);
+  }
+  good = __syncthreads_and(good);
+  if (threadIdx.x == 0) parts[blockIdx.x] = (uint8_t)good;
+}
+
+// ---------------------------------------------------------------- host quantiser
+static inline float host_half_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000) << 16;
+  uint32_t exp = (h >> 10) & 0x1F, man = h & 0x3FF, bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {  // renormalise the fp16 subnormal
+      int e = -1;
+      do { ++e; man <<= 1; } while (!(man & 0x400));
+      bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3FF) << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7F800000u | (man << 13);
+  } else {
+    bits = sign | ((exp + 112) << 23) | (man << 13);
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+static inline uint8_t host_e4m3(float x) {
+  uint32_t b;
+  memcpy(&b, &x, 4);
+  const uint32_t sign = b >> 31;
+  const uint32_t exp = (b >> 23) & 0xFF, man = b & 0x7FFFFF;
+  uint32_t code;
+  if ((int)exp - 120 >= 1) {
+    const uint32_t joined = ((exp - 120) << 23) | man;
+    code = (joined >> 20) + (((joined & 0xFFFFF) > 0x80000) ||
+                             (((joined & 0xFFFFF) == 0x80000) && ((joined >> 20) & 1)));
+  } else {
+    const uint64_t full = exp ? (man | (1u << 23)) : man;
+    const int shift = 141 - (exp ? (int)exp : 1);
+    if (shift >= 40) {
+      code = 0;
+    } else {
+      const uint64_t qv = full >> shift, rem = full & ((1ull << shift) - 1), half = 1ull << (shift - 1);
+      code = (uint32_t)(qv + ((rem > half) || (rem == half && (qv & 1))));
+    }
+  }
+  return (uint8_t)(code | (sign << 7));
+}
+
+static int host_quantize_rows(const void* x, int dtype, int64_t r0, int64_t r1, int64_t rows,
+                              int64_t k, int64_t row_stride, int64_t kp, uint8_t* q, uint8_t* s,
+                              int* bad) {
+  std::vector<float> v(32);
+  for (int64_t r = r0; r < r1; ++r) {
+    for (int64_t c = 0; c < kp / 32; ++c) {
+      uint32_t amax_bits = 0;
+      for (int i = 0; i < 32; ++i) {
+        const int64_t col = c * 32 + i;
+        float f = 0.f;
+        if (r < rows && col < k) {
+          const int64_t off = r * row_stride + col;
+          if (dtype == VDN_DTYPE_F32) {
+            f = static_cast<const float*>(x)[off];
+          } else if (dtype == VDN_DTYPE_BF16) {
+            const uint32_t bits = (uint32_t)static_cast<const uint16_t*>(x)[off] << 16;
+            memcpy(&f, &bits, 4);
+          } else {
+            f = host_half_to_f32(static_cast<const uint16_t*>(x)[off]);
+          }
+          if (!std::isfinite(f)) { *bad = 1; return 0; }
+        }
+        v[i] = f;
+        uint32_t ab;
+        memcpy(&ab, &f, 4);
+        ab &= 0x7FFFFFFFu;
+        amax_bits = ab > amax_bits ? ab : amax_bits;
+      }
+      float inv;
+      const uint32_t sbyte = e8m0_from_amax_bits(amax_bits, &inv);
+      for (int i = 0; i < 32; ++i) q[r * kp + c * 32 + i] = host_e4m3(v[i] * inv);
+      s[((r >> 7) * (kp >> 7) + (c >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (c & 3)] =
+          (uint8_t)sbyte;
+    }
+  }
+  return 0;
+}
+
+}  // namespace vdn
+
+using namespace vdn;
+
+extern "C" {
+
+int vdn_mxfp8_padded_shape(int64_t rows, int64_t k, int64_t* rows_padded, int64_t* k_padded) {
+  VDN_CHECK_ARG(rows >= 0 && k > 0, "rows must be nonnegative and K positive");
+  VDN_CHECK_ARG(rows_padded && k_padded, "output pointers must not be null");
+  *rows_padded = (rows + 127) / 128 * 128;
+  *k_padded = (k + 127) / 128 * 128;
+  return VDN_OK;
+}
+
+static int launch_act_quantize(int act, const void* x, int64_t rows, int64_t k, int64_t row_stride,
+                               uint8_t* q, uint8_t* s, int* nonfinite, cudaStream_t stream) {
+  VDN_CHECK_ARG(rows >= 0 && k > 0, "rows must be nonnegative and K positive");
+  VDN_CHECK_ARG(q && s, "q and s must not be null");
+  VDN_CHECK_ARG(rows == 0 || x, "x must not be null");
+  const int64_t width = act == ACT_SWIGLU ? 2 * k : k;
+  VDN_CHECK_ARG(rows <= 1 || row_stride >= width, "row_stride %lld shorter than the row width %lld",
+                (long long)row_stride, (long long)width);
+  VDN_CHECK_ARG(aligned16(q) && aligned16(s), "q and s must be 16-byte aligned");
+  const int64_t rp = (rows + 127) / 128 * 128, kp = (k + 127) / 128 * 128;
+  if (rp == 0) return VDN_OK;
+  const bool vec = aligned16(x) && (row_stride % 8 == 0) && (act != ACT_SWIGLU || k % 8 == 0);
+  const int64_t threads = rp * (kp / 32);
+  const dim3 grid((unsigned)((threads + 255) / 256)), block(256);
+  const uint16_t* xp = static_cast<const uint16_t*>(x);
+#define VDN_QLAUNCH(A)                                                                       \
+  if (vec) act_quantize_kernel<A, true><<<grid, block, 0, stream>>>(xp, row_stride, rows, k, rp, kp, q, s, nonfinite); \
+  else act_quantize_kernel<A, false><<<grid, block, 0, stream>>>(xp, row_stride, rows, k, rp, kp, q, s, nonfinite);
+  switch (act) {
+    case ACT_NONE: VDN_QLAUNCH(ACT_NONE); break;
+    case ACT_GELU_TANH: VDN_QLAUNCH(ACT_GELU_TANH); break;
+    case ACT_GELU_ERF: VDN_QLAUNCH(ACT_GELU_ERF); break;
+    case ACT_SWIGLU: VDN_QLAUNCH(ACT_SWIGLU); break;
+    default: return set_error(VDN_ERR_VALUE, "unknown activation %d", act);
+  }
+#undef VDN_QLAUNCH
+  VDN_LAUNCH_CHECK("mxfp8 quantize");
+  return VDN_OK;
+}
+
+int vdn_mxfp8_quantize(const void* x, int64_t rows, int64_t k, int64_t row_stride, uint8_t* q,
+                       uint8_t* s, int* nonfinite, cudaStream_t stream) {
+  return launch_act_quantize(ACT_NONE, x, rows, k, row_stride, q, s, nonfinite, stream);
+}
+
+int vdn_mxfp8_act_quantize(int act, const void* x, int64_t rows, int64_t k, int64_t row_stride,
+                           uint8_t* q, uint8_t* s, int* nonfinite, cudaStream_t stream) {
+  VDN_CHECK_ARG(act >= VDN_ACT_GELU_TANH && act <= VDN_ACT_SWIGLU, "unknown activation %d", act);
+  return launch_act_quantize(act, x, rows, k, row_stride, q, s, nonfinite, stream);
+}
+
+int vdn_mxfp8_prenorm_quantize(const void* x, int64_t rows, int64_t k, int64_t x_stride,
+                               const void* weight, int weight_dtype, float eps, const void* scale,
+                               int64_t scale_stride, const void* shift, int64_t shift_stride,
+                               const int64_t* indices, void* y, uint8_t* q, uint8_t* s,
+                               uint8_t* finite, cudaStream_t stream) {
+  VDN_CHECK_ARG(rows >= 0 && k > 0, "rows must be nonnegative and K positive");
+  VDN_CHECK_ARG(q && s && finite, "q, s and finite must not be null");
+  VDN_CHECK_ARG(rows == 0 || (x && weight && scale && shift && indices), "inputs must not be null");
+  VDN_CHECK_ARG(weight_dtype == VDN_DTYPE_F32 || weight_dtype == VDN_DTYPE_BF16,
+                "weight must be fp32 or bf16");
+  const int64_t rp = (rows + 127) / 128 * 128, kp = (k + 127) / 128 * 128;
+  if (rp == 0) return VDN_OK;
+  const uint16_t* xp = static_cast<const uint16_t*>(x);
+  if (weight_dtype == VDN_DTYPE_F32) {
+    prenorm_quantize_kernel<float><<<(unsigned)rp, 256, 0, stream>>>(
+        xp, x_stride, static_cast<const float*>(weight), static_cast<const uint16_t*>(scale),
+        scale_stride, static_cast<const uint16_t*>(shift), shift_stride, indices, rows, k, kp, eps,
+        static_cast<uint16_t*>(y), q, s, finite);
+  } else {
+    prenorm_quantize_kernel<__nv_bfloat16><<<(unsigned)rp, 256, 0, stream>>>(
+        xp, x_stride, static_cast<const __nv_bfloat16*>(weight), static_cast<const uint16_t*>(scale),
+        scale_stride, static_cast<const uint16_t*>(shift), shift_stride, indices, rows, k, kp, eps,
+        static_cast<uint16_t*>(y), q, s, finite);
+  }
+  VDN_LAUNCH_CHECK("mxfp8 prenorm quantize");
+  return VDN_OK;
+}
+
+int vdn_finite_parts(const void* x, int64_t n, int dtype, int mode, uint8_t* parts,
+                     cudaStream_t stream) {
+  VDN_CHECK_ARG(n >= 0 && parts, "bad finite_parts arguments");
+  VDN_CHECK_ARG(mode >= 0 && mode <= 2, "mode must be 0, 1 or 2");
+  if (n == 0) return VDN_OK;
+  const unsigned grid = (unsigned)((n + 4095) / 4096);
+  if (mode == 1) {
+    finite_parts_kernel<uint8_t, 1><<<grid, 256, 0, stream>>>(static_cast<const uint8_t*>(x), n, parts);
+  } else if (mode == 2) {
+    finite_parts_kernel<uint8_t, 2><<<grid, 256, 0, stream>>>(static_cast<const uint8_t*>(x), n, parts);
+  } else if (dtype == VDN_DTYPE_F32) {
+    finite_parts_kernel<float, 0><<<grid, 256, 0, stream>>>(static_cast<const float*>(x), n, parts);
+  } else if (dtype == VDN_DTYPE_BF16) {
+    finite_parts_kernel<__nv_bfloat16, 0><<<grid, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), n, parts);
+  } else if (dtype == VDN_DTYPE_F16) {
+    finite_parts_kernel<__half, 0><<<grid, 256, 0, stream>>>(static_cast<const __half*>(x), n, parts);
+  } else {
+    return set_error(VDN_ERR_TYPE, "unsupported dtype %d", dtype);
+  }
+  VDN_LAUNCH_CHECK("finite_parts");
+  return VDN_OK;
+}
+
+int vdn_mxfp8_quantize_host(const void* x, int dtype, int64_t rows, int64_t k, int64_t row_stride,
+                            uint8_t* q, uint8_t* s, int num_threads) {
+  VDN_CHECK_ARG(rows >= 0 && k > 0, "rows must be nonnegative and K positive");
+  VDN_CHECK_ARG(q && s && (rows == 0 || x), "null pointer");
+  if (dtype != VDN_DTYPE_F32 && dtype != VDN_DTYPE_BF16 && dtype != VDN_DTYPE_F16)
+    return set_error(VDN_ERR_TYPE, "expected a floating 2D weight");
+  const int64_t rp = (rows + 127) / 128 * 128, kp = (k + 127) / 128 * 128;
+  int nt = num_threads > 0 ? num_threads : (int)std::thread::hardware_concurrency();
+  if (nt < 1) nt = 1;
+  if (nt > rp / 128 + 1) nt = (int)(rp / 128 + 1);
+  std::vector<std::thread> pool;
+  std::vector<int> bad(nt, 0);
+  const int64_t chunk = ((rp + nt - 1) / nt + 127) / 128 * 128;
+  for (int t = 0; t < nt; ++t) {
+    const int64_t r0 = t * chunk, r1 = std::min<int64_t>(rp, r0 + chunk);
+    if (r0 >= r1) break;
+    pool.emplace_back([=, &bad] { host_quantize_rows(x, dtype, r0, r1, rows, k, row_stride, kp, q, s, &bad[t]); });
+  }
+  for (auto& th : pool) th.join();
+  for (int b : bad)
+    if (b) return set_error(VDN_ERR_NONFINITE, "nonfinite MXFP8 weight");
+  return VDN_OK;
+}
+
+}  // extern "C"

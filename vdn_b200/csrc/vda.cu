@@ -1,0 +1,633 @@
+// VDA (frame-wise bidirectional delta-rule linear attention) for sm_100a.
+//
+// Stage kernels, each a launch over the natural parallel unit of its stage:
+//   statistics  one CTA per (frame, head): SiLU(+L2) features of k / v in
+//               registers, A = sym((k*beta) k^T) fp32, B = bf16(bf16(v*beta) k^T)
+//   factors     one CTA per (frame, head): in-register Gauss-Jordan inverse of
+//               the SPD I + A, T = diag(alpha) inv, J = B inv
+//   scan        one CTA per (head, direction, 16 state rows): rows of the state
+//               evolve independently, s_t = s_{t-1} T_t + J_t, fp32
+//   gather      one CTA per (frame, head, 16 rows): window complement, decayed
+//   readout     one CTA per (frame, head, 256 tokens): q features, q state^T,
+//               RMSNorm * w * gate, token-major bf16 store
+// Reference: ec-jt/vdn src/models/linear_attention/{scan.py, delta_rule.py,
+// branch.py, paper_stack.py, paper_sglang.py}.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace vdn {
+
+constexpr int kMaxFrames = 1024;
+
+struct FrameBounds {
+  int32_t lo[kMaxFrames];
+  int32_t hi[kMaxFrames];
+};
+
+// Features of one token row (d = 32 * PER lanes' worth): SiLU, optional L2 over
+// d (sum clamped at 1e-12), rounded to bf16 once (paper_sglang.py:211-250).
+template <int PER>
+__device__ __forceinline__ void warp_features(const uint16_t* __restrict__ src, bool l2, float* out) {
+  const int lane = threadIdx.x & 31;
+  float y[PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const float x = bf16_bits_to_f32(src[lane * PER + i]);
+    y[i] = silu_f(x);
+    ss += y[i] * y[i];
+  }
+  if (l2) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.0f / sqrtf(fmaxf(ss, 1e-12f));
+#pragma unroll
+    for (int i = 0; i < PER; ++i) y[i] *= inv;
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) out[i] = round_bf16(y[i]);
+}
+
+// ----------------------------------------------------------------- statistics
+template <int D>
+__global__ void __launch_bounds__(256) stats_kernel(
+    const uint16_t* __restrict__ k, int64_t k_sf, int64_t k_ss, int64_t k_sh,
+    const uint16_t* __restrict__ v, int64_t v_sf, int64_t v_ss, int64_t v_sh,
+    const uint16_t* __restrict__ beta, int64_t b_sf, int64_t b_ss, int64_t b_sh,
+    int features_applied, int S, int H, float* __restrict__ A, float* __restrict__ B) {
+  constexpr int T = D / 16;      // each thread owns a T x T tile of A and of B
+  constexpr int CS = 32;         // tokens per chunk
+  constexpr int PER = D / 32;    // elements per lane in a token row
+  extern __shared__ float smem[];
+  float* kb = smem;              // [CS][D] k * beta (fp32)
+  float* kk = kb + CS * D;       // [CS][D] k features
+  float* vb = kk + CS * D;       // [CS][D] bf16(v * beta)
+  const int fh = blockIdx.x;
+  const int f = fh / H, h = fh % H;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float acc_a[T][T], acc_b[T][T];
+#pragma unroll
+  for (int i = 0; i < T; ++i)
+#pragma unroll
+    for (int j = 0; j < T; ++j) acc_a[i][j] = acc_b[i][j] = 0.f;
+
+  for (int s0 = 0; s0 < S; s0 += CS) {
+    __syncthreads();
+    for (int t = warp; t < CS; t += 8) {
+      const int s = s0 + t;
+      float kf[PER], vf[PER];
+      float bt = 0.f;
+      if (s < S) {
+        const uint16_t* kr = k + (int64_t)f * k_sf + (int64_t)s * k_ss + (int64_t)h * k_sh;
+        const uint16_t* vr = v + (int64_t)f * v_sf + (int64_t)s * v_ss + (int64_t)h * v_sh;
+        if (features_applied) {
+#pragma unroll
+          for (int i = 0; i < PER; ++i) {
+            kf[i] = bf16_bits_to_f32(kr[lane * PER + i]);
+            vf[i] = bf16_bits_to_f32(vr[lane * PER + i]);
+          }
+        } else {
+          warp_features<PER>(kr, true, kf);
+          warp_features<PER>(vr, false, vf);
+        }
+        bt = bf16_bits_to_f32(beta[(int64_t)f * b_sf + (int64_t)s * b_ss + (int64_t)h * b_sh]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) kf[i] = vf[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        kk[t * D + lane * PER + i] = kf[i];
+        kb[t * D + lane * PER + i] = kf[i] * bt;
+        vb[t * D + lane * PER + i] = round_bf16(vf[i] * bt);
+      }
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int t = 0; t < CS; ++t) {
+      float a[T], b[T], c[T];
+#pragma unroll
+      for (int i = 0; i < T; ++i) {
+        a[i] = kb[t * D + ty * T + i];
+        c[i] = vb[t * D + ty * T + i];
+        b[i] = kk[t * D + tx * T + i];
+      }
+#pragma unroll
+      for (int i = 0; i < T; ++i)
+#pragma unroll
+        for (int j = 0; j < T; ++j) {
+          acc_a[i][j] = fmaf(a[i], b[j], acc_a[i][j]);
+          acc_b[i][j] = fmaf(c[i], b[j], acc_b[i][j]);
+        }
+    }
+  }
+  // Symmetrise A through shared memory; round B to bf16 (reference scan.py:262-266).
+  __syncthreads();
+  float* as = smem;  // [D][D]
+#pragma unroll
+  for (int i = 0; i < T; ++i)
+#pragma unroll
+    for (int j = 0; j < T; ++j) as[(ty * T + i) * D + tx * T + j] = acc_a[i][j];
+  __syncthreads();
+  float* a_out = A + (int64_t)fh * D * D;
+  float* b_out = B + (int64_t)fh * D * D;
+#pragma unroll
+  for (int i = 0; i < T; ++i)
+#pragma unroll
+    for (int j = 0; j < T; ++j) {
+      const int r = ty * T + i, c = tx * T + j;
+      a_out[r * D + c] = 0.5f * (acc_a[i][j] + as[c * D + r]);
+      b_out[r * D + c] = round_bf16(acc_b[i][j]);
+    }
+}
+
+// -------------------------------------------------------------------- factors
+// One CTA per matrix; thread (ty, tx) holds rows ty*T.., cols tx*T.. of the
+// working matrix in registers. T may alias A and J may alias B (each CTA reads
+// its whole matrix before the first store), so those pointers are not restrict.
+// Non-pivoting in-place Gauss-Jordan inversion of the SPD M = I + A: at pivot p the owners publish row p and column p through
+// double-buffered shared vectors, then every thread applies the rank-1 update.
+template <int D>
+__global__ void __launch_bounds__(256) factor_kernel(const float* A, const float* B,
+                                                     const float* __restrict__ alpha,
+                                                     float* Tout, float* Jout) {
+  constexpr int T = D / 16;
+  extern __shared__ float smem[];
+  float* rowbuf = smem;            // [2][D]
+  float* colbuf = smem + 2 * D;    // [2][D]
+  float* inv_s = smem + 4 * D;     // [D][D] inverse, then reused
+  float* b_s = inv_s + D * D;      // [D][D] B
+  const int64_t mat = blockIdx.x;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const float* a_in = A + mat * D * D;
+  float m[T][T];
+#pragma unroll
+  for (int i = 0; i < T; ++i)
+#pragma unroll
+    for (int j = 0; j < T; ++j) {
+      const int r = ty * T + i, c = tx * T + j;
+      m[i][j] = a_in[r * D + c] + (r == c ? 1.0f : 0.0f);
+    }
+  // Stage B while the inversion runs (read-only until the product).
+  const float* b_in = B + mat * D * D;
+  for (int e = threadIdx.x * 4; e < D * D; e += 256 * 4)
+    *reinterpret_cast<float4*>(b_s + e) = *reinterpret_cast<const float4*>(b_in + e);
+
+  // Outer loop over pivot blocks, inner loop unrolled so the pivot's position
+  // inside a thread's tile is a compile-time index (m stays in registers).
+  for (int pb = 0; pb < D / T; ++pb) {
+#pragma unroll
+    for (int pi = 0; pi < T; ++pi) {
+      const int p = pb * T + pi;
+      float* rb = rowbuf + (p & 1) * D;
+      float* cb = colbuf + (p & 1) * D;
+      if (ty == pb) {
+#pragma unroll
+        for (int j = 0; j < T; ++j) rb[tx * T + j] = m[pi][j];
+      }
+      if (tx == pb) {
+#pragma unroll
+        for (int i = 0; i < T; ++i) cb[ty * T + i] = m[i][pi];
+      }
+      __syncthreads();
+      const float piv = rb[p];
+      const float ip = __fdiv_rn(1.0f, piv);
+      float prow[T], pcol[T];
+#pragma unroll
+      for (int j = 0; j < T; ++j) prow[j] = rb[tx * T + j] * ip;
+#pragma unroll
+      for (int i = 0; i < T; ++i) pcol[i] = cb[ty * T + i];
+#pragma unroll
+      for (int i = 0; i < T; ++i) {
+        const bool row_is_p = (ty == pb) && (i == pi);
+#pragma unroll
+        for (int j = 0; j < T; ++j) {
+          const bool col_is_p = (tx == pb) && (j == pi);
+          float val;
+          if (row_is_p) val = col_is_p ? ip : prow[j];
+          else if (col_is_p) val = -pcol[i] * ip;
+          else val = fmaf(-pcol[i], prow[j], m[i][j]);
+          m[i][j] = val;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const float* al = alpha ? alpha + mat * D : nullptr;
+  float* t_out = Tout + mat * D * D;
+#pragma unroll
+  for (int i = 0; i < T; ++i)
+#pragma unroll
+    for (int j = 0; j < T; ++j) {
+      const int r = ty * T + i, c = tx * T + j;
+      inv_s[r * D + c] = m[i][j];
+      t_out[r * D + c] = al ? al[r] * m[i][j] : m[i][j];
+    }
+  __syncthreads();
+  // J = B inv
+  float acc[T][T];
+#pragma unroll
+  for (int i = 0; i < T; ++i)
+#pragma unroll
+    for (int j = 0; j < T; ++j) acc[i][j] = 0.f;
+  for (int kk = 0; kk < D; ++kk) {
+    float bv[T], iv[T];
+#pragma unroll
+    for (int i = 0; i < T; ++i) bv[i] = b_s[(ty * T + i) * D + kk];
+#pragma unroll
+    for (int j = 0; j < T; ++j) iv[j] = inv_s[kk * D + tx * T + j];
+#pragma unroll
+    for (int i = 0; i < T; ++i)
+#pragma unroll
+      for (int j = 0; j < T; ++j) acc[i][j] = fmaf(bv[i], iv[j], acc[i][j]);
+  }
+  float* j_out = Jout + mat * D * D;
+#pragma unroll
+  for (int i = 0; i < T; ++i)
+#pragma unroll
+    for (int j = 0; j < T; ++j) j_out[(ty * T + i) * D + tx * T + j] = acc[i][j];
+}
+
+// ----------------------------------------------------------------------- scan
+// grid (H, 2, D/16); 256 threads; thread owns row t/16 of the CTA's 16 rows and
+// D/16 consecutive columns.
+template <int D>
+__global__ void __launch_bounds__(256) scan_kernel(const float* __restrict__ Tm,
+                                                   const float* __restrict__ Jm,
+                                                   const float* __restrict__ seed, int F, int H,
+                                                   float* __restrict__ prefix,
+                                                   float* __restrict__ suffix) {
+  constexpr int R = 16, C = D / 16;
+  __shared__ float st[R][D];
+  const int h = blockIdx.x, dir = blockIdx.y, rb = blockIdx.z;
+  const int r = threadIdx.x / 16, c0 = (threadIdx.x % 16) * C;
+  const int row = rb * R + r;
+  float cur[C];
+#pragma unroll
+  for (int j = 0; j < C; ++j) cur[j] = seed ? seed[((int64_t)h * D + row) * D + c0 + j] : 0.f;
+  float* bank = dir == 0 ? prefix : suffix;
+  for (int step = 0; step < F; ++step) {
+    const int f = dir == 0 ? step : F - 1 - step;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < C; ++j) st[r][c0 + j] = cur[j];
+    __syncthreads();
+    const int64_t base = ((int64_t)f * H + h) * D * D;
+    const float* tm = Tm + base;
+    float acc[C];
+#pragma unroll
+    for (int j = 0; j < C; ++j) acc[j] = Jm[base + (int64_t)row * D + c0 + j];
+#pragma unroll 4
+    for (int kk = 0; kk < D; ++kk) {
+      const float sv = st[r][kk];
+      const float* trow = tm + (int64_t)kk * D + c0;
+#pragma unroll
+      for (int j = 0; j < C; ++j) acc[j] = fmaf(sv, __ldg(trow + j), acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      cur[j] = acc[j];
+      bank[base + (int64_t)row * D + c0 + j] = acc[j];
+    }
+  }
+}
+
+// --------------------------------------------------------------------- gather
+template <int D, typename OutT>
+__global__ void __launch_bounds__(256) gather_kernel(const float* __restrict__ prefix,
+                                                     const float* __restrict__ suffix,
+                                                     const float* __restrict__ alpha,
+                                                     const float* __restrict__ seed, int bridge,
+                                                     int F, int H, const FrameBounds bounds,
+                                                     OutT* __restrict__ out) {
+  constexpr int R = 16;
+  __shared__ float dec_b[D], dec_a[D];
+  const int t = blockIdx.x, h = blockIdx.y, rb = blockIdx.z;
+  const int lo = bounds.lo[t], hi = bounds.hi[t];
+  const bool has_b = lo > 0, has_a = hi + 1 < F;
+  if (threadIdx.x < D) {
+    const int kk = threadIdx.x;
+    float pb = 1.f, pa = 1.f;
+    if (bridge) {
+      for (int u = max(lo, 0); u <= t; ++u) pb *= fmaxf(alpha[((int64_t)u * H + h) * D + kk], 1e-12f);
+      for (int u = t; u <= min(hi, F - 1); ++u) pa *= fmaxf(alpha[((int64_t)u * H + h) * D + kk], 1e-12f);
+    }
+    dec_b[kk] = pb;
+    dec_a[kk] = pa;
+  }
+  __syncthreads();
+  const int64_t plane = (int64_t)D * D;
+  for (int e = threadIdx.x; e < R * D; e += blockDim.x) {
+    const int r = rb * R + e / D, kk = e % D;
+    const int64_t off = (int64_t)r * D + kk;
+    const float sd = seed ? seed[h * plane + off] : 0.f;
+    const float left = has_b ? prefix[((int64_t)(lo - 1) * H + h) * plane + off] : sd;
+    const float right = has_a ? suffix[((int64_t)(hi + 1) * H + h) * plane + off] : sd;
+    const float val = left * dec_b[kk] + right * dec_a[kk];
+    const int64_t o = ((int64_t)t * H + h) * plane + off;
+    if constexpr (sizeof(OutT) == 2) reinterpret_cast<uint16_t*>(out)[o] = f32_to_bf16_bits(val);
+    else out[o] = val;
+  }
+}
+
+// -------------------------------------------------------------------- readout
+// grid (F*H, ceil(S/256)); 256 threads = 8 warps; a warp owns 8 tokens at a time,
+// lane l the output channels 4l..4l+3 (d = 128) or 2l..2l+1 (d = 64).
+template <int D>
+__global__ void __launch_bounds__(256) readout_kernel(
+    const uint16_t* __restrict__ q, int64_t q_sf, int64_t q_ss, int64_t q_sh,
+    const uint16_t* __restrict__ state, const uint16_t* __restrict__ gate, int64_t g_sf,
+    int64_t g_ss, int64_t g_sh, const float* __restrict__ norm_w, float eps, int S, int H,
+    uint16_t* __restrict__ out) {
+  constexpr int PER = D / 32;   // channels per lane
+  constexpr int TOK = 8;        // tokens per warp pass
+  extern __shared__ float smem[];
+  float* stT = smem;            // [D(k)][D(v)] state transposed, fp32
+  float* qs = stT + D * D;      // [8 warps][D(k)][TOK]
+  const int fh = blockIdx.x;
+  const int f = fh / H, h = fh % H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint16_t* st = state + (int64_t)fh * D * D;
+  for (int e = threadIdx.x; e < D * D; e += blockDim.x) {
+    const int vv = e / D, kk = e % D;
+    stT[kk * D + vv] = bf16_bits_to_f32(st[e]);
+  }
+  float w[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) w[i] = norm_w[lane * PER + i];
+  __syncthreads();
+  float* myq = qs + warp * D * TOK;
+  const int s_begin = blockIdx.y * 256;
+  const int s_end = min(S, s_begin + 256);
+  for (int s0 = s_begin + warp * TOK; s0 < s_end; s0 += 8 * TOK) {
+    __syncwarp();
+    for (int t = 0; t < TOK; ++t) {
+      const int s = s0 + t;
+      float qf[PER];
+      if (s < s_end) {
+        warp_features<PER>(q + (int64_t)f * q_sf + (int64_t)s * q_ss + (int64_t)h * q_sh, true, qf);
+      } else {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) qf[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) myq[(lane * PER + i) * TOK + t] = qf[i];
+    }
+    __syncwarp();
+    float acc[TOK][PER];
+#pragma unroll
+    for (int t = 0; t < TOK; ++t)
+#pragma unroll
+      for (int i = 0; i < PER; ++i) acc[t][i] = 0.f;
+#pragma unroll 2
+    for (int kk = 0; kk < D; ++kk) {
+      float sv[PER], qv[TOK];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) sv[i] = stT[kk * D + lane * PER + i];
+#pragma unroll
+      for (int t = 0; t < TOK; ++t) qv[t] = myq[kk * TOK + t];
+#pragma unroll
+      for (int t = 0; t < TOK; ++t)
+#pragma unroll
+        for (int i = 0; i < PER; ++i) acc[t][i] = fmaf(qv[t], sv[i], acc[t][i]);
+    }
+#pragma unroll
+    for (int t = 0; t < TOK; ++t) {
+      const int s = s0 + t;
+      float r[PER];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        r[i] = round_bf16(acc[t][i]);  // the readout matmul stores bf16
+        ss += r[i] * r[i];
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (s >= s_end) continue;
+      const float inv = 1.0f / sqrtf(ss / (float)D + eps);
+      const uint16_t* gr = gate + (int64_t)f * g_sf + (int64_t)s * g_ss + (int64_t)h * g_sh;
+      uint16_t* orow = out + ((int64_t)f * S + s) * ((int64_t)H * D) + (int64_t)h * D;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int c = lane * PER + i;
+        orow[c] = f32_to_bf16_bits(r[i] * inv * w[i] * bf16_bits_to_f32(gr[c]));
+      }
+    }
+  }
+}
+
+static int check_d(int d) {
+  if (d != 64 && d != 128) return set_error(VDN_ERR_VALUE, "head_dim must be 64 or 128, got %d", d);
+  return VDN_OK;
+}
+
+template <typename K>
+static int set_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024)
+    VDN_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return VDN_OK;
+}
+
+static int fill_bounds(const int32_t* bounds, int F, FrameBounds* fb) {
+  VDN_CHECK_ARG(bounds, "bounds must not be null");
+  VDN_CHECK_ARG(F >= 1 && F <= kMaxFrames, "frames must lie in [1, %d], got %d", kMaxFrames, F);
+  for (int t = 0; t < F; ++t) {
+    const int lo = bounds[2 * t], hi = bounds[2 * t + 1];
+    VDN_CHECK_ARG(lo <= t && t <= hi, "each inclusive window must contain its query frame");
+    fb->lo[t] = lo;
+    fb->hi[t] = hi;
+  }
+  return VDN_OK;
+}
+
+int launch_stats(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, const void* v,
+                 int64_t v_sf, int64_t v_ss, int64_t v_sh, const void* beta, int64_t b_sf,
+                 int64_t b_ss, int64_t b_sh, int features_applied, int F, int S, int H, int d,
+                 float* A, float* B, cudaStream_t stream) {
+  if (int rc = check_d(d)) return rc;
+  VDN_CHECK_ARG(F >= 1 && S >= 1 && H >= 1, "positive F, S, H required");
+  VDN_CHECK_ARG(k && v && beta && A && B, "null pointer");
+  const size_t smem = std::max<size_t>(3 * 32 * d, (size_t)d * d) * sizeof(float);
+  const auto* kp = static_cast<const uint16_t*>(k);
+  const auto* vp = static_cast<const uint16_t*>(v);
+  const auto* bp = static_cast<const uint16_t*>(beta);
+  if (d == 128) {
+    if (int rc = set_smem(stats_kernel<128>, smem)) return rc;
+    stats_kernel<128><<<F * H, 256, smem, stream>>>(kp, k_sf, k_ss, k_sh, vp, v_sf, v_ss, v_sh, bp,
+                                                     b_sf, b_ss, b_sh, features_applied, S, H, A, B);
+  } else {
+    if (int rc = set_smem(stats_kernel<64>, smem)) return rc;
+    stats_kernel<64><<<F * H, 256, smem, stream>>>(kp, k_sf, k_ss, k_sh, vp, v_sf, v_ss, v_sh, bp,
+                                                    b_sf, b_ss, b_sh, features_applied, S, H, A, B);
+  }
+  VDN_LAUNCH_CHECK("vda statistics");
+  return VDN_OK;
+}
+
+int launch_factors(const float* A, const float* B, const float* alpha, int64_t n, int d, float* T,
+                   float* J, cudaStream_t stream) {
+  if (int rc = check_d(d)) return rc;
+  VDN_CHECK_ARG(n >= 0, "n must be nonnegative");
+  if (n == 0) return VDN_OK;
+  VDN_CHECK_ARG(A && B && T && J, "null pointer");
+  VDN_CHECK_ARG(aligned16(A) && aligned16(B), "A and B must be 16-byte aligned");
+  VDN_CHECK_ARG(n < (1ll << 31), "too many matrices");
+  const size_t smem = (4 * d + 2 * d * d) * sizeof(float);
+  if (d == 128) {
+    if (int rc = set_smem(factor_kernel<128>, smem)) return rc;
+    factor_kernel<128><<<(unsigned)n, 256, smem, stream>>>(A, B, alpha, T, J);
+  } else {
+    if (int rc = set_smem(factor_kernel<64>, smem)) return rc;
+    factor_kernel<64><<<(unsigned)n, 256, smem, stream>>>(A, B, alpha, T, J);
+  }
+  VDN_LAUNCH_CHECK("delta factors");
+  return VDN_OK;
+}
+
+int launch_scan(const float* T, const float* J, const float* seed, int F, int H, int d,
+                float* prefix, float* suffix, cudaStream_t stream) {
+  if (int rc = check_d(d)) return rc;
+  VDN_CHECK_ARG(F >= 1 && H >= 1, "positive F and H required");
+  VDN_CHECK_ARG(T && J && prefix && suffix, "null pointer");
+  const dim3 grid(H, 2, d / 16);
+  if (d == 128) scan_kernel<128><<<grid, 256, 0, stream>>>(T, J, seed, F, H, prefix, suffix);
+  else scan_kernel<64><<<grid, 256, 0, stream>>>(T, J, seed, F, H, prefix, suffix);
+  VDN_LAUNCH_CHECK("vda scan");
+  return VDN_OK;
+}
+
+int launch_gather(const float* prefix, const float* suffix, const float* alpha,
+                  const int32_t* bounds, const float* seed, int bridge, int F, int H, int d,
+                  void* out, int out_dtype, cudaStream_t stream) {
+  if (int rc = check_d(d)) return rc;
+  VDN_CHECK_ARG(H >= 1, "positive H required");
+  VDN_CHECK_ARG(prefix && suffix && alpha && out, "null pointer");
+  FrameBounds fb;
+  if (int rc = fill_bounds(bounds, F, &fb)) return rc;
+  const dim3 grid(F, H, d / 16);
+  if (out_dtype == VDN_DTYPE_BF16) {
+    auto* o = static_cast<__nv_bfloat16*>(out);
+    if (d == 128) gather_kernel<128, __nv_bfloat16><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o);
+    else gather_kernel<64, __nv_bfloat16><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o);
+  } else if (out_dtype == VDN_DTYPE_F32) {
+    auto* o = static_cast<float*>(out);
+    if (d == 128) gather_kernel<128, float><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o);
+    else gather_kernel<64, float><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o);
+  } else {
+    return set_error(VDN_ERR_TYPE, "out_dtype must be fp32 or bf16");
+  }
+  VDN_LAUNCH_CHECK("vda gather");
+  return VDN_OK;
+}
+
+int launch_readout(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, const void* state,
+                   const void* gate, int64_t g_sf, int64_t g_ss, int64_t g_sh,
+                   const float* norm_weight, float eps, int F, int S, int H, int d, void* out,
+                   cudaStream_t stream) {
+  if (int rc = check_d(d)) return rc;
+  VDN_CHECK_ARG(F >= 1 && S >= 1 && H >= 1, "positive F, S, H required");
+  VDN_CHECK_ARG(q && state && gate && norm_weight && out, "null pointer");
+  const size_t smem = ((size_t)d * d + 8 * d * 8) * sizeof(float);
+  const dim3 grid(F * H, (S + 255) / 256);
+  const auto* qp = static_cast<const uint16_t*>(q);
+  const auto* sp = static_cast<const uint16_t*>(state);
+  const auto* gp = static_cast<const uint16_t*>(gate);
+  auto* op = static_cast<uint16_t*>(out);
+  if (d == 128) {
+    if (int rc = set_smem(readout_kernel<128>, smem)) return rc;
+    readout_kernel<128><<<grid, 256, smem, stream>>>(qp, q_sf, q_ss, q_sh, sp, gp, g_sf, g_ss, g_sh,
+                                                      norm_weight, eps, S, H, op);
+  } else {
+    if (int rc = set_smem(readout_kernel<64>, smem)) return rc;
+    readout_kernel<64><<<grid, 256, smem, stream>>>(qp, q_sf, q_ss, q_sh, sp, gp, g_sf, g_ss, g_sh,
+                                                     norm_weight, eps, S, H, op);
+  }
+  VDN_LAUNCH_CHECK("vda readout");
+  return VDN_OK;
+}
+
+}  // namespace vdn
+
+using namespace vdn;
+
+extern "C" {
+
+int vdn_delta_factors(const float* A, const float* B, const float* alpha, int64_t n, int d,
+                      float* T, float* J, cudaStream_t stream) {
+  return launch_factors(A, B, alpha, n, d, T, J, stream);
+}
+
+int vdn_vda_statistics(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, const void* v,
+                       int64_t v_sf, int64_t v_ss, int64_t v_sh, const void* beta, int64_t b_sf,
+                       int64_t b_ss, int64_t b_sh, int features_applied, int F, int S, int H,
+                       int d, float* A, float* B, cudaStream_t stream) {
+  return launch_stats(k, k_sf, k_ss, k_sh, v, v_sf, v_ss, v_sh, beta, b_sf, b_ss, b_sh,
+                      features_applied, F, S, H, d, A, B, stream);
+}
+
+int vdn_vda_scan(const float* T, const float* J, const float* seed, int F, int H, int d,
+                 float* prefix, float* suffix, cudaStream_t stream) {
+  return launch_scan(T, J, seed, F, H, d, prefix, suffix, stream);
+}
+
+int vdn_vda_gather(const float* prefix, const float* suffix, const float* alpha,
+                   const int32_t* bounds, const float* seed, int bridge, int F, int H, int d,
+                   void* out, int out_dtype, cudaStream_t stream) {
+  return launch_gather(prefix, suffix, alpha, bounds, seed, bridge, F, H, d, out, out_dtype, stream);
+}
+
+int vdn_vda_readout(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, const void* state,
+                    const void* gate, int64_t g_sf, int64_t g_ss, int64_t g_sh,
+                    const float* norm_weight, float eps, int F, int S, int H, int d, void* out,
+                    cudaStream_t stream) {
+  return launch_readout(q, q_sf, q_ss, q_sh, state, gate, g_sf, g_ss, g_sh, norm_weight, eps, F,
+                        S, H, d, out, stream);
+}
+
+size_t vdn_vda_workspace_size(int F, int S, int H, int d) {
+  (void)S;
+  const size_t plane = (size_t)F * H * d * d;
+  // A/T and B/J (fp32, factors overwrite statistics in place), prefix, suffix
+  // (fp32) and the gathered state (bf16), each region 256-byte aligned.
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  return 4 * up(plane * 4) + up(plane * 2);
+}
+
+int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss, int64_t qkv_sh,
+                    const void* beta, int64_t b_ss, int64_t b_sh, const void* gate, int64_t g_ss,
+                    int64_t g_sh, const float* alpha, const float* norm_weight, float eps,
+                    const int32_t* bounds, const float* seed, int bridge, int F, int S, int H,
+                    int d, void* out, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream) {
+  if (int rc = check_d(d)) return rc;
+  VDN_CHECK_ARG(F >= 1 && S >= 1 && H >= 1, "positive F, S, H required");
+  VDN_CHECK_ARG(q && k && v && beta && gate && alpha && norm_weight && out, "null pointer");
+  const size_t need = vdn_vda_workspace_size(F, S, H, d);
+  VDN_CHECK_ARG(workspace && workspace_bytes >= need, "workspace too small: need %zu bytes", need);
+  VDN_CHECK_ARG(aligned16(workspace), "workspace must be 16-byte aligned");
+  FrameBounds fb;
+  if (int rc = fill_bounds(bounds, F, &fb)) return rc;
+  const size_t plane = (size_t)F * H * d * d;
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  char* ws = static_cast<char*>(workspace);
+  float* A = reinterpret_cast<float*>(ws);
+  float* B = reinterpret_cast<float*>(ws + up(plane * 4));
+  float* prefix = reinterpret_cast<float*>(ws + 2 * up(plane * 4));
+  float* suffix = reinterpret_cast<float*>(ws + 3 * up(plane * 4));
+  void* state = ws + 4 * up(plane * 4);
+  const int64_t sf = (int64_t)S * qkv_ss;
+  if (int rc = launch_stats(k, sf, qkv_ss, qkv_sh, v, sf, qkv_ss, qkv_sh, beta, (int64_t)S * b_ss,
+                            b_ss, b_sh, 0, F, S, H, d, A, B, stream))
+    return rc;
+  if (int rc = launch_factors(A, B, alpha, (int64_t)F * H, d, A, B, stream)) return rc;
+  if (int rc = launch_scan(A, B, seed, F, H, d, prefix, suffix, stream)) return rc;
+  if (int rc = launch_gather(prefix, suffix, alpha, bounds, seed, bridge, F, H, d, state,
+                             VDN_DTYPE_BF16, stream))
+    return rc;
+  return launch_readout(q, sf, qkv_ss, qkv_sh, state, gate, (int64_t)S * g_ss, g_ss, g_sh,
+                        norm_weight, eps, F, S, H, d, out, stream);
+}
+
+}  // extern "C"
