@@ -100,11 +100,13 @@ int vdn_mxfp8_quantize_host(const void* x, int dtype, int64_t rows, int64_t k,
  *   y[:rows_out, :n] = bf16(dequant(xq, xs) @ dequant(wq, ws)^T) (+ bias[n] bf16)
  * xq [m_pad, k_pad] / wq [n_pad, k_pad] E4M3 codes, xs / ws swizzled E8M0
  * scales, m_pad, n_pad, k_pad multiples of 128.  y bf16 with row stride ldy.
+ * status: optional device int; set to VDN_ERR_TIMEOUT if a pipeline wait inside
+ * the kernel gave up (the kernel then returns without finishing the tile).
  * Replaces MXFP8Linear.forward_quantized, src/models/ops/mxfp8_linear.py:60-93
  * (F.scaled_mm BlockWise1x32 / SWIZZLE_32_4_4). */
 int vdn_mxfp8_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, const uint8_t* ws,
                    const void* bias, int64_t m_pad, int64_t n, int64_t n_pad, int64_t k_pad,
-                   int64_t rows_out, void* y, int64_t ldy, cudaStream_t stream);
+                   int64_t rows_out, void* y, int64_t ldy, int* status, cudaStream_t stream);
 
 /* -------------------------------------------------------------------- VDA */
 

@@ -1,0 +1,147 @@
+"""GPU: the tcgen05 block-scaled MXFP8 GEMM against the dequantised oracle.
+
+Mirrors the reference's GEMM oracle (tests/test_paper_stack_mxfp8_ops.py:160-220):
+y == bf16(dequant(x) @ dequant(w)^T) + bias within rtol .01 / atol .016, plus the
+BASELINE config-1 shapes (M = 32760; N in {15360, 5120, 13824}; K in {5120, 13824})
+checked on sampled rows.  Tests run smallest first.
+"""
+import numpy as np
+import pytest
+import torch
+from torch import nn
+
+from oracle import mxfp8 as omx
+
+pytestmark = pytest.mark.gpu
+
+
+def unswizzle_index(rows, k, device):
+    r = torch.arange(rows, device=device)[:, None]
+    c = torch.arange(k // 32, device=device)[None, :]
+    return ((r // 128) * (k // 128) + c // 4) * 512 + r % 32 * 16 + (r % 128 // 32) * 4 + c % 4
+
+
+def dequant(data, scale):
+    r, k = data.shape
+    natural = scale[unswizzle_index(r, k, data.device)]
+    return (data.view(torch.float8_e4m3fn).float().reshape(r, k // 32, 32)
+            * torch.exp2(natural.float() - 127)[..., None]).reshape(r, k)
+
+
+def oracle_gemm(xq, xs, wq, ws, rows, n, bias=None):
+    y = (dequant(xq, xs).double() @ dequant(wq, ws).double().T)[:rows, :n]
+    y = y.float().bfloat16()
+    return y if bias is None else y + bias.bfloat16()
+
+
+def quantised(m, k, device, seed, scale=1.0, outliers=False):
+    from vdn_b200.mxfp8_quant import quantize_activation
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(m, k, device=device, generator=g) * scale
+    if outliers:
+        idx = torch.randperm(k, device=device, generator=g)[:max(1, k // 100)]
+        x[:, idx] *= 50
+    return quantize_activation(x.bfloat16())
+
+
+def run(xq, xs, wq, ws, rows, n, bias=None):
+    from vdn_b200.mxfp8_linear import mxfp8_gemm, check_gemm_status
+    y = mxfp8_gemm(xq, xs, wq, ws, n, rows=rows, bias=bias)
+    torch.cuda.synchronize()
+    check_gemm_status(xq.device)
+    return y
+
+
+def test_single_tile(cuda):
+    xq, xs = quantised(128, 128, cuda, 1)
+    wq, ws = quantised(256, 128, cuda, 2)
+    y = run(xq, xs, wq, ws, 128, 256)
+    torch.testing.assert_close(y, oracle_gemm(xq, xs, wq, ws, 128, 256), rtol=.01, atol=.016)
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 512), (256, 384, 256), (384, 512, 1024),
+                                   (1024, 1024, 1024), (4096, 2048, 512), (640, 640, 13824 // 27)])
+def test_tiles_kblocks_and_persistence(cuda, m, n, k):
+    k = (k + 127) // 128 * 128
+    xq, xs = quantised(m, k, cuda, m + n)
+    wq, ws = quantised(n, k, cuda, k)
+    y = run(xq, xs, wq, ws, m, n)
+    torch.testing.assert_close(y, oracle_gemm(xq, xs, wq, ws, m, n), rtol=.01, atol=.016)
+
+
+def test_crop_bias_and_row_stride(cuda):
+    from vdn_b200.mxfp8_linear import mxfp8_gemm
+    xq, xs = quantised(300, 384, cuda, 5)
+    wq, ws = quantised(200, 384, cuda, 6)
+    bias = torch.randn(200, device=cuda).bfloat16()
+    out = torch.full((290, 256), 7.0, device=cuda, dtype=torch.bfloat16)
+    y = mxfp8_gemm(xq, xs, wq, ws, 200, rows=290, bias=bias, out=out[:, :200])
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y, oracle_gemm(xq, xs, wq, ws, 290, 200, bias), rtol=.01, atol=.016)
+    assert bool((out[:, 200:] == 7.0).all())
+
+
+@pytest.mark.parametrize("shape", [(0, 7, 3), (1, 1, 1), (17, 37, 31), (129, 133, 257), (128, 128, 256)])
+@torch.no_grad()
+def test_linear_shape_oracle(cuda, shape):
+    """Reference test_fused_quant_and_native_gemm_shape_oracle (strided rows, bias)."""
+    from vdn_b200.mxfp8_linear import MXFP8Linear
+    from vdn_b200.mxfp8_quant import quantize_activation, quantize_cpu
+    m, n, k = shape
+    torch.manual_seed(42)
+    base = torch.randn(m * 2, k, dtype=torch.bfloat16)
+    linear = nn.Linear(k, n, bias=True, dtype=torch.bfloat16).eval()
+    packed = MXFP8Linear(linear).to(cuda)
+    xg = base.to(cuda)[::2]
+    q, s = quantize_activation(xg)
+    cq, cs = quantize_cpu(base[::2])
+    assert torch.equal(q.cpu(), cq) and torch.equal(s.cpu(), cs)
+    y = packed(xg)
+    assert y.shape == (m, n) and y.dtype == torch.bfloat16 and bool(y.isfinite().all())
+    if m:
+        oracle = (dequant(q, s) @ dequant(packed.weight_data, packed.weight_scale).T)[:m, :n]
+        oracle = oracle.to(torch.bfloat16) + packed.bias
+        torch.testing.assert_close(y, oracle, rtol=.01, atol=.016)
+    assert torch.equal(packed.weight_data.cpu(), quantize_cpu(linear.weight)[0])
+
+
+@torch.no_grad()
+def test_reject_nonfinite_inputs_and_results(cuda):
+    from vdn_b200.mxfp8_linear import MXFP8Linear
+    p = MXFP8Linear(nn.Linear(32, 16, bias=False, dtype=torch.bfloat16)).to(cuda)
+    x = torch.ones(3, 32, dtype=torch.bfloat16, device=cuda)
+    x[0, 0] = float("nan")
+    with pytest.raises(ValueError, match="nonfinite MXFP8 activation"):
+        p(x)
+    x.fill_(1)
+    p.weight_data.fill_(127)   # E4M3 NaN: a corrupted compressed weight
+    with pytest.raises(ValueError, match="nonfinite MXFP8 result"):
+        p(x)
+
+
+@torch.no_grad()
+def test_project_qkv_fused_matches_separate(cuda):
+    from vdn_b200.mxfp8_linear import MXFP8Linear, project_qkv
+    torch.manual_seed(3)
+    projs = [MXFP8Linear(nn.Linear(256, 384, bias=True, dtype=torch.bfloat16), check_finite=False).to(cuda)
+             for _ in range(3)]
+    x = torch.randn(2, 129, 256, device=cuda, dtype=torch.bfloat16)
+    fused = project_qkv(projs, x)
+    for got, p in zip(fused, projs):
+        assert got.shape == (2, 129, 384)
+        assert torch.equal(got, p(x))
+
+
+@pytest.mark.parametrize("n,k", [(15360, 5120), (5120, 5120), (13824, 5120), (5120, 13824)])
+def test_config1_shapes_sampled_rows(cuda, n, k):
+    """BASELINE config 1 at full size: M = 32760 activation rows with 1% outlier
+    channels x50, weights N(0, 0.02); rows sampled across the M range."""
+    m = 32760
+    xq, xs = quantised(m, k, cuda, n + k, outliers=True)
+    wq, ws = quantised(n, k, cuda, 11, scale=0.02)
+    y = run(xq, xs, wq, ws, m, n)
+    assert y.shape == (m, n) and bool(torch.isfinite(y).all())
+    rows = torch.cat([torch.arange(0, 256), torch.arange(16000, 16128), torch.arange(m - 200, m)]).to(cuda)
+    xd = dequant(xq, xs)[rows]
+    want = (xd.double() @ dequant(wq, ws).double().T).float().bfloat16()
+    torch.testing.assert_close(y[rows], want, rtol=.01, atol=.016)

@@ -1,8 +1,341 @@
-// Block-scaled MXFP8 GEMM (tcgen05 kind::mxf8f6f4) -- entry point placeholder.
+// Block-scaled MXFP8 GEMM on sm_100a tensor cores (tcgen05 kind::mxf8f6f4,
+// one E8M0 scale per 32 K-elements):
+//     y[:rows_out, :n] = bf16( dequant(xq, xs) @ dequant(wq, ws)^T ) (+ bias)
+//
+// Persistent, warp-specialised CTA (192 threads, one per SM):
+//   warp 0     TMA producer: A tile 128x128 B and B tile 256x128 B (128B swizzle)
+//              plus the tile's scale atoms (512-byte bulk copies: the swizzled
+//              SWIZZLE_32_4_4 scale layout stores one 128-row x 128-K atom
+//              contiguously) into a 4-stage shared-memory ring
+//   warp 1     TMEM allocator and single-thread MMA issuer: per stage, three
+//              tcgen05.cp (scales -> TMEM) and four 128x256x32 block-scaled MMAs
+//              into a 128-lane x 256-column fp32 TMEM accumulator
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator (each warp its 32-lane
+//              quadrant), bf16 rounding, bias, cropped stores
+// Tiles are walked in groups of 16 M-tiles with N fastest so the live A and B
+// tiles of all CTAs stay in L2.  Every mbarrier wait is bounded (2 s); a
+// timeout aborts all roles, drains copies in flight, frees TMEM and reports
+// VDN_ERR_TIMEOUT through `status`.  No TMA multicast is used.
 #include "common.cuh"
+#include "sm100.cuh"
 
-extern "C" int vdn_mxfp8_gemm(const uint8_t*, const uint8_t*, const uint8_t*, const uint8_t*,
-                              const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*,
-                              int64_t, cudaStream_t) {
-  return vdn::set_error(VDN_ERR_RUNTIME, "vdn_mxfp8_gemm is not built yet");
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace vdn {
+namespace gemm {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 128;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;              // 16 KB
+constexpr int B_BYTES = BN * BK;              // 32 KB
+constexpr int SF_STAGE = 512 * 3;             // SFA atom + two SFB atoms
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_COL = 0;
+constexpr int SF_COL = 256;                   // 12 columns per stage: SFA 4, SFB 8
+constexpr int GROUP_M = 16;
+constexpr int THREADS = 192;
+constexpr size_t SMEM_BYTES =
+    1024 + STAGES * (A_BYTES + B_BYTES + SF_STAGE) + (2 * STAGES + 3) * 8 + 16;
+
+struct Params {
+  const uint8_t* xs;
+  const uint8_t* ws;
+  const uint16_t* bias;
+  uint16_t* y;
+  int64_t ldy;
+  int64_t rows_out;
+  int64_t n;
+  int m_tiles, n_tiles, k_blocks, n_groups;  // n_groups = n_pad / 128
+  int* status;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mb, int& nb) {
+  const int per_group = GROUP_M * n_tiles;
+  const int g = t / per_group;
+  const int first = g * GROUP_M;
+  const int gsize = min(GROUP_M, m_tiles - first);
+  const int local = t - g * per_group;
+  mb = first + local % gsize;
+  nb = local / gsize;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                      const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sSF = sB + STAGES * B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSF + STAGES * SF_STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* mma_done = acc_empty + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tmap_a);
+    prefetch_tensormap(&tmap_b);
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t pending = 0;            // stages with loads issued (bit mask)
+      uint32_t pending_phase = 0;      // the full-barrier parity those loads complete
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+        const bool has_b1 = 2 * nb + 1 < p.n_groups;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
+          const uint32_t bytes = A_BYTES + B_BYTES + (has_b1 ? 3 : 2) * 512;
+          mbar_arrive_expect_tx(&full[stage], bytes);
+          tma_load_2d(sA + stage * A_BYTES, &tmap_a, &full[stage], kb * BK, mb * BM);
+          tma_load_2d(sB + stage * B_BYTES, &tmap_b, &full[stage], kb * BK, nb * BN);
+          uint8_t* sf = sSF + stage * SF_STAGE;
+          bulk_load(sf, p.xs + ((int64_t)mb * p.k_blocks + kb) * 512, 512, &full[stage]);
+          bulk_load(sf + 512, p.ws + ((int64_t)(2 * nb) * p.k_blocks + kb) * 512, 512, &full[stage]);
+          if (has_b1)
+            bulk_load(sf + 1024, p.ws + ((int64_t)(2 * nb + 1) * p.k_blocks + kb) * 512, 512, &full[stage]);
+          pending |= 1u << stage;
+          pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Let every copy already issued land before the CTA can exit.
+        for (int s = 0; s < STAGES; ++s) {
+          if (!(pending >> s & 1)) continue;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&full[s], (pending_phase >> s) & 1) &&
+                 globaltimer() - t0 < kWaitLimitNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ----------------------------------------------------------------- MMA
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool issued = false;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        if (!mbar_wait(acc_empty, acc_phase ^ 1, abort_flag)) break;
+        tc_fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sf_a = tmem + SF_COL + stage * 12;
+          const uint32_t sf_b = sf_a + 4;
+          const uint32_t sf_smem = smem_u32(sSF + stage * SF_STAGE);
+          tmem_cp_32x128_x4(sf_a, desc_sf_atom(sf_smem));
+          tmem_cp_32x128_x4(sf_b, desc_sf_atom(sf_smem + 512));
+          tmem_cp_32x128_x4(sf_b + 4, desc_sf_atom(sf_smem + 1024));
+          const uint64_t adesc = desc_k_sw128(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bdesc = desc_k_sw128(smem_u32(sB + stage * B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            // +32 bytes along K inside the 128-byte swizzled row: +2 in start>>4.
+            mma_mxf8(tmem + ACC_COL, adesc + 2 * k, bdesc + 2 * k, idesc_mxf8(BM, BN, k),
+                     sf_a | ((uint32_t)k << 30), sf_b | ((uint32_t)k << 30), (kb | k) != 0);
+          }
+          issued = true;
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(acc_full);
+        acc_phase ^= 1;
+      }
+      if (*abort_flag && issued) {
+        // Wait for every MMA / copy issued so far before TMEM is freed.
+        tc_commit(mma_done);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(mma_done, 0) && globaltimer() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;                      // TMEM lane quadrant of this warp
+    const int row_in_tile = quad * 32 + lane;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, acc_phase, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)mb * BM + row_in_tile;
+      uint16_t* yrow = p.y + row * p.ldy;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(quad * 32) << 16) + ACC_COL + c * 32, r);
+        tmem_ld_wait();
+        const int64_t col0 = (int64_t)nb * BN + c * 32;
+        if (row >= p.rows_out || col0 >= p.n) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v[i] = round_bf16(__uint_as_float(r[i]));
+          if (p.bias) {
+            const int64_t col = col0 + i;
+            const float b = col < p.n ? bf16_bits_to_f32(p.bias[col]) : 0.f;
+            v[i] = round_bf16(v[i] + b);
+          }
+        }
+        if (col0 + 32 <= p.n && ((reinterpret_cast<uintptr_t>(yrow + col0) & 15) == 0)) {
+          uint4* dst = reinterpret_cast<uint4*>(yrow + col0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = pack8(v + 8 * i);
+        } else {
+          for (int i = 0; i < 32 && col0 + i < p.n; ++i) yrow[col0 + i] = f32_to_bf16_bits(v[i]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort_flag && p.status) atomicExch(p.status, VDN_ERR_TIMEOUT);
+}
+
+// -------------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+static int make_map(CUtensorMap* map, const void* base, int64_t k_pad, int64_t rows, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(VDN_ERR_RUNTIME, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)k_pad, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)k_pad};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VDN_ERR_RUNTIME, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return VDN_OK;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  bool smem_set = false;
+};
+
+static int device_info(DeviceInfo** out) {
+  static DeviceInfo info[64];
+  static std::mutex mu;
+  int dev = 0;
+  VDN_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(VDN_ERR_RUNTIME, "device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  DeviceInfo& d = info[dev];
+  if (!d.smem_set) {
+    VDN_CUDA_TRY(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    VDN_CUDA_TRY(cudaFuncSetAttribute(mxfp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)SMEM_BYTES));
+    d.smem_set = true;
+  }
+  *out = &d;
+  return VDN_OK;
+}
+
+}  // namespace gemm
+}  // namespace vdn
+
+using namespace vdn;
+
+extern "C" int vdn_mxfp8_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq,
+                              const uint8_t* ws, const void* bias, int64_t m_pad, int64_t n,
+                              int64_t n_pad, int64_t k_pad, int64_t rows_out, void* y, int64_t ldy,
+                              int* status, cudaStream_t stream) {
+  using namespace vdn::gemm;
+  VDN_CHECK_ARG(m_pad >= 0 && n > 0 && n_pad > 0 && k_pad > 0, "bad GEMM extents");
+  VDN_CHECK_ARG(m_pad % 128 == 0 && n_pad % 128 == 0 && k_pad % 128 == 0,
+                "m_pad, n_pad and k_pad must be multiples of 128");
+  VDN_CHECK_ARG(n <= n_pad && rows_out >= 0 && rows_out <= m_pad, "crop exceeds the padded extents");
+  VDN_CHECK_ARG(ldy >= n, "ldy must be at least n");
+  if (rows_out == 0 || m_pad == 0) return VDN_OK;
+  VDN_CHECK_ARG(xq && xs && wq && ws && y, "null pointer");
+  VDN_CHECK_ARG(aligned16(xq) && aligned16(xs) && aligned16(wq) && aligned16(ws),
+                "codes and scales must be 16-byte aligned");
+  VDN_CHECK_ARG(m_pad / 128 < (1 << 30) && n_pad / 128 < (1 << 30), "extents too large");
+  DeviceInfo* info = nullptr;
+  if (int rc = device_info(&info)) return rc;
+  CUtensorMap ma, mb;
+  if (int rc = make_map(&ma, xq, k_pad, m_pad, BM)) return rc;
+  if (int rc = make_map(&mb, wq, k_pad, n_pad, BN)) return rc;
+  Params p;
+  p.xs = xs;
+  p.ws = ws;
+  p.bias = static_cast<const uint16_t*>(bias);
+  p.y = static_cast<uint16_t*>(y);
+  p.ldy = ldy;
+  p.rows_out = rows_out;
+  p.n = n;
+  p.m_tiles = (int)(m_pad / BM);
+  p.n_tiles = (int)((n_pad + BN - 1) / BN);
+  p.k_blocks = (int)(k_pad / BK);
+  p.n_groups = (int)(n_pad / 128);
+  p.status = status;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < info->sms ? tiles : info->sms;
+  mxfp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  VDN_LAUNCH_CHECK("mxfp8 gemm");
+  return VDN_OK;
 }

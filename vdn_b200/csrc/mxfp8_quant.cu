@@ -342,14 +342,14 @@ int vdn_mxfp8_padded_shape(int64_t rows, int64_t k, int64_t* rows_padded, int64_
 static int launch_act_quantize(int act, const void* x, int64_t rows, int64_t k, int64_t row_stride,
                                uint8_t* q, uint8_t* s, int* nonfinite, cudaStream_t stream) {
   VDN_CHECK_ARG(rows >= 0 && k > 0, "rows must be nonnegative and K positive");
+  if (rows == 0) return VDN_OK;  // zero padded rows: nothing to write
   VDN_CHECK_ARG(q && s, "q and s must not be null");
-  VDN_CHECK_ARG(rows == 0 || x, "x must not be null");
+  VDN_CHECK_ARG(x, "x must not be null");
   const int64_t width = act == ACT_SWIGLU ? 2 * k : k;
   VDN_CHECK_ARG(rows <= 1 || row_stride >= width, "row_stride %lld shorter than the row width %lld",
                 (long long)row_stride, (long long)width);
   VDN_CHECK_ARG(aligned16(q) && aligned16(s), "q and s must be 16-byte aligned");
   const int64_t rp = (rows + 127) / 128 * 128, kp = (k + 127) / 128 * 128;
-  if (rp == 0) return VDN_OK;
   const bool vec = aligned16(x) && (row_stride % 8 == 0) && (act != ACT_SWIGLU || k % 8 == 0);
   const int64_t threads = rp * (kp / 32);
   const dim3 grid((unsigned)((threads + 255) / 256)), block(256);
@@ -386,12 +386,12 @@ int vdn_mxfp8_prenorm_quantize(const void* x, int64_t rows, int64_t k, int64_t x
                                const int64_t* indices, void* y, uint8_t* q, uint8_t* s,
                                uint8_t* finite, cudaStream_t stream) {
   VDN_CHECK_ARG(rows >= 0 && k > 0, "rows must be nonnegative and K positive");
+  if (rows == 0) return VDN_OK;
   VDN_CHECK_ARG(q && s && finite, "q, s and finite must not be null");
   VDN_CHECK_ARG(rows == 0 || (x && weight && scale && shift && indices), "inputs must not be null");
   VDN_CHECK_ARG(weight_dtype == VDN_DTYPE_F32 || weight_dtype == VDN_DTYPE_BF16,
                 "weight must be fp32 or bf16");
   const int64_t rp = (rows + 127) / 128 * 128, kp = (k + 127) / 128 * 128;
-  if (rp == 0) return VDN_OK;
   const uint16_t* xp = static_cast<const uint16_t*>(x);
   if (weight_dtype == VDN_DTYPE_F32) {
     prenorm_quantize_kernel<float><<<(unsigned)rp, 256, 0, stream>>>(

@@ -25,8 +25,9 @@ struct FrameBounds {
   int32_t hi[kMaxFrames];
 };
 
-// Features of one token row (d = 32 * PER lanes' worth): SiLU, optional L2 over
-// d (sum clamped at 1e-12), rounded to bf16 once (paper_sglang.py:211-250).
+// Features of one token row (d = 32 * PER lanes' worth) with the eager
+// reference's bf16 rounding points (features.py:47-60): x = bf16(silu(raw));
+// for q / k, norm = max(bf16(||x||), bf16(1e-6)) and x = bf16(x / norm).
 template <int PER>
 __device__ __forceinline__ void warp_features(const uint16_t* __restrict__ src, bool l2, float* out) {
   const int lane = threadIdx.x & 31;
@@ -35,18 +36,18 @@ __device__ __forceinline__ void warp_features(const uint16_t* __restrict__ src, 
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const float x = bf16_bits_to_f32(src[lane * PER + i]);
-    y[i] = silu_f(x);
+    y[i] = round_bf16(silu_f(x));
     ss += y[i] * y[i];
   }
   if (l2) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = 1.0f / sqrtf(fmaxf(ss, 1e-12f));
+    const float nrm = fmaxf(round_bf16(sqrtf(ss)), round_bf16(1e-6f));
 #pragma unroll
-    for (int i = 0; i < PER; ++i) y[i] *= inv;
+    for (int i = 0; i < PER; ++i) y[i] = round_bf16(__fdiv_rn(y[i], nrm));
   }
 #pragma unroll
-  for (int i = 0; i < PER; ++i) out[i] = round_bf16(y[i]);
+  for (int i = 0; i < PER; ++i) out[i] = y[i];
 }
 
 // ----------------------------------------------------------------- statistics
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(256) readout_kernel(
   }
   float w[PER];
 #pragma unroll
-  for (int i = 0; i < PER; ++i) w[i] = norm_w[lane * PER + i];
+  for (int i = 0; i < PER; ++i) w[i] = round_bf16(norm_w[lane * PER + i]);
   __syncthreads();
   float* myq = qs + warp * D * TOK;
   const int s_begin = blockIdx.y * 256;
@@ -406,13 +407,17 @@ __global__ void __launch_bounds__(256) readout_kernel(
 #pragma unroll
       for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       if (s >= s_end) continue;
-      const float inv = 1.0f / sqrtf(ss / (float)D + eps);
+      // Eager RMSNorm rounding points (ops/rms_norm.py:29-32): ms from the fp32
+      // norm squared, bf16 reciprocal, then bf16 after each multiply.
+      const float nrm = sqrtf(ss);
+      const float inv = round_bf16(__fdiv_rn(1.0f, sqrtf(nrm * nrm / (float)D + eps)));
       const uint16_t* gr = gate + (int64_t)f * g_sf + (int64_t)s * g_ss + (int64_t)h * g_sh;
       uint16_t* orow = out + ((int64_t)f * S + s) * ((int64_t)H * D) + (int64_t)h * D;
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
         const int c = lane * PER + i;
-        orow[c] = f32_to_bf16_bits(r[i] * inv * w[i] * bf16_bits_to_f32(gr[c]));
+        const float y = round_bf16(round_bf16(r[i] * inv) * w[i]);
+        orow[c] = f32_to_bf16_bits(y * bf16_bits_to_f32(gr[c]));
       }
     }
   }
