@@ -178,6 +178,24 @@ int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss,
                     int F, int S, int H, int d, void* out,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* vdn_vda_forward without a workspace argument, for callers that cannot give
+ * this library device memory or let it call cudaMalloc (a host engine that owns
+ * all device memory through its own pool, or a latency-critical loop that cannot
+ * take cudaMalloc's device synchronisation).  Same kernels and results as
+ * vdn_vda_forward; the scratch is a 64 MiB array built into the library, held
+ * by every GPU that loads it until the process exits.  Geometries needing more
+ * than 64 MiB (18 * F * H * d^2 bytes plus alignment) return VDN_ERR_VALUE.
+ * The first call on a device looks the array's address up (make it before any
+ * stream capture); all calls share the array, so calls that overlap on the GPU
+ * race.  It allocates nothing.  This entry point has no counterpart in the
+ * reference (ec-jt/vdn): its branch body always allocates through PyTorch. */
+int vdn_vda_forward_noalloc(const void* q, const void* k, const void* v, int64_t qkv_ss,
+                            int64_t qkv_sh, const void* beta, int64_t b_ss, int64_t b_sh,
+                            const void* gate, int64_t g_ss, int64_t g_sh,
+                            const float* alpha, const float* norm_weight, float eps,
+                            const int32_t* bounds, const float* seed, int bridge,
+                            int F, int S, int H, int d, void* out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

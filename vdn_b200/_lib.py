@@ -46,6 +46,8 @@ SIGNATURES = {
     "vdn_vda_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
     "vdn_vda_forward": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _f32,
                                _p, _p, _i32, _i32, _i32, _i32, _i32, _p, _p, _sz, _p]),
+    "vdn_vda_forward_noalloc": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _p,
+                                       _f32, _p, _p, _i32, _i32, _i32, _i32, _i32, _p, _p]),
 }
 
 _LOCK = threading.Lock()
