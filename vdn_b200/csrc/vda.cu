@@ -423,6 +423,19 @@ __global__ void __launch_bounds__(256) readout_kernel(
   }
 }
 
+// Tensor-core (tcgen05) paths for d = 128, defined in vda_tc.cu.
+bool tc_stats_supported(int d, const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, const void* v,
+                        int64_t v_sf, int64_t v_ss, int64_t v_sh);
+int launch_stats_tc(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sf,
+                    int64_t v_ss, int64_t v_sh, const void* beta, int64_t b_sf, int64_t b_ss,
+                    int64_t b_sh, int features_applied, int F, int S, int H, float* A, float* B,
+                    int* status, cudaStream_t stream);
+bool tc_readout_supported(int d, const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh,
+                          const void* state, const void* gate, int64_t g_ss, int64_t g_sh);
+int launch_readout_tc(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, const void* state,
+                      const void* gate, int64_t g_sf, int64_t g_ss, int64_t g_sh, const float* norm_w,
+                      float eps, int F, int S, int H, void* out, int* status, cudaStream_t stream);
+
 static int check_d(int d) {
   if (d != 64 && d != 128) return set_error(VDN_ERR_VALUE, "head_dim must be 64 or 128, got %d", d);
   return VDN_OK;
@@ -454,6 +467,9 @@ int launch_stats(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, const 
   if (int rc = check_d(d)) return rc;
   VDN_CHECK_ARG(F >= 1 && S >= 1 && H >= 1, "positive F, S, H required");
   VDN_CHECK_ARG(k && v && beta && A && B, "null pointer");
+  if (tc_stats_supported(d, k, k_sf, k_ss, k_sh, v, v_sf, v_ss, v_sh))
+    return launch_stats_tc(k, k_sf, k_ss, k_sh, v, v_sf, v_ss, v_sh, beta, b_sf, b_ss, b_sh,
+                           features_applied, F, S, H, A, B, nullptr, stream);
   const size_t smem = std::max<size_t>(3 * 32 * d, (size_t)d * d) * sizeof(float);
   const auto* kp = static_cast<const uint16_t*>(k);
   const auto* vp = static_cast<const uint16_t*>(v);
@@ -534,6 +550,9 @@ int launch_readout(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, cons
   if (int rc = check_d(d)) return rc;
   VDN_CHECK_ARG(F >= 1 && S >= 1 && H >= 1, "positive F, S, H required");
   VDN_CHECK_ARG(q && state && gate && norm_weight && out, "null pointer");
+  if (tc_readout_supported(d, q, q_sf, q_ss, q_sh, state, gate, g_ss, g_sh) && aligned16(out))
+    return launch_readout_tc(q, q_sf, q_ss, q_sh, state, gate, g_sf, g_ss, g_sh, norm_weight, eps, F, S,
+                             H, out, nullptr, stream);
   const size_t smem = ((size_t)d * d + 8 * d * 8) * sizeof(float);
   const dim3 grid(F * H, (S + 255) / 256);
   const auto* qp = static_cast<const uint16_t*>(q);
