@@ -13,11 +13,15 @@ reference algorithm restated in numpy) on a bounded sample of the same workload
 on the host cores.
 
 Workloads:
+  block (default)  BASELINE config 3: one hybrid DiT block (hidden 5120, 40 x 128
+        heads, GELU FFN 13824, MXFP8 projections, VDA + window softmax +-1 frame)
+        over 21 frames x 1560 tokens = 32760 tokens; metric = tokens/s of the
+        whole job.  N > 1: Ulysses sequence parallelism over NCCL (sequence
+        shards, all-to-all to heads around attention): strong scaling, the same
+        32760-token block split over N GPUs.
   vda   BASELINE config 2: the VDA branch, H=40, d=128, 21 frames x 1560 tokens,
         metric = algorithmic HBM GB/s (q, k, v, gate, beta, alpha in; out).
-        Multi-GPU: heads are independent, each rank runs its head shard (no
-        collective on the data path): weak scaling over 40/N heads... per rank
-        the full 40 heads (replica-free weak scaling: fixed work per GPU).
+        N > 1: independent replicas (heads are independent; no collective).
 """
 from __future__ import annotations
 
@@ -276,13 +280,139 @@ def cpu_baseline_vda(threads):
             "kind": "port", "sample": "oracle VDA body, 1 of 40 heads at 21x1560 tokens, time x40"}
 
 
+# ---------------------------------------------------------------------- block
+BLOCK_CFG = dict(F=21, S=1560, hidden=5120, heads=40, head_dim=128, ffn=13824)
+
+
+def bench_block(args, torch, dist, rank, world):
+    from vdn_b200.block import HybridBlock
+    from vdn_b200.ulysses import init_ulysses
+    from vdn_b200.mxfp8_quant import quantize_activation
+    F, S = BLOCK_CFG["F"], BLOCK_CFG["S"]
+    T = F * S
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    block = HybridBlock(seed=0, device=dev)
+    runtime = None
+    lo, hi = 0, T
+    if world > 1:
+        runtime = init_ulysses("nccl")
+        runtime.configure(T, BLOCK_CFG["heads"])
+        lo, hi = runtime.local_start, runtime.local_end
+    g = torch.Generator(device=dev).manual_seed(1234)
+    x_full = torch.randn(T, BLOCK_CFG["hidden"], device=dev, generator=g).bfloat16()
+    temb = torch.randn(BLOCK_CFG["hidden"], device=dev, generator=g)
+    x = x_full[lo:hi].contiguous()
+    del x_full
+    rows = hi - lo
+
+    def step():
+        return block(x, temb, F, S, runtime)
+
+    with ClockSampler(dev.index) as clk:
+        ms = time_steps(torch, step, args.steps, args.warmup, dist, stream)
+    per_step_ms = ms / args.steps
+    value = T / (per_step_ms * 1e-3)
+    flops = 2 * T * BLOCK_CFG["hidden"] * (3 * BLOCK_CFG["hidden"] + 2 * BLOCK_CFG["hidden"]
+                                           + 2 * BLOCK_CFG["ffn"])
+
+    # Dominant kernel: the FFN-up / QKV MXFP8 GEMMs; time the QKV launch on this rank's rows.
+    y1 = torch.randn(rows, BLOCK_CFG["hidden"], device=dev).bfloat16()
+    q1, s1 = quantize_activation(y1)
+    out = torch.empty(rows, 3 * BLOCK_CFG["hidden"], device=dev, dtype=torch.bfloat16)
+    kt = kernel_times(torch, [("mxfp8_gemm_qkv", lambda: block._gemm(q1, s1, block.qkv, rows, out,
+                                                                    bias=block.qkv.bias))], 10, stream)
+    gemm_flops = 2 * rows * 3 * BLOCK_CFG["hidden"] * BLOCK_CFG["hidden"]
+    achieved = gemm_flops / (kt["mxfp8_gemm_qkv"] * 1e-3) / 1e12
+    pk, src = peaks()
+    fp8_peak = 2 * pk["bf16_tflops"]
+    comp = {}
+    try:
+        x8 = y1.to(torch.float8_e4m3fn)
+        w8 = torch.randn(3 * BLOCK_CFG["hidden"], BLOCK_CFG["hidden"], device=dev).to(torch.float8_e4m3fn)
+        one = torch.ones((), device=dev)
+        ct = kernel_times(torch, [("cublas_fp8_per_tensor", lambda: torch._scaled_mm(
+            x8, w8.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16))], 10, stream)
+        comp["cublas_fp8_per_tensor_tflops"] = round(gemm_flops / (ct["cublas_fp8_per_tensor"] * 1e-3) / 1e12, 1)
+    except Exception as e:  # comparator only
+        comp["cublas_fp8_per_tensor_error"] = repr(e)[:120]
+
+    # End to end through the public API: pinned host rows in, block output back to the host.
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = block(x_dev, temb, F, S, runtime)
+        out_host.copy_(y, non_blocking=True)
+
+    e2e_steps = max(2, args.steps // 2)
+    e2e_ms = time_steps(torch, e2e_step, e2e_steps, 1, dist, stream) / e2e_steps
+    rec = {
+        "metric": "hybrid-block tokens/s (BASELINE config 3, 32760 tokens)",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_step_ms, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "mxfp8 GEMMs (fp32 accumulate), bf16 activations",
+        "data": "synthetic (seeded N(0,1) tokens and timestep embedding, random-init weights)",
+        "config": {"workload": "hybrid_block_config3", "frames": F, "tokens_per_frame": S,
+                   "hidden": BLOCK_CFG["hidden"], "heads": BLOCK_CFG["heads"],
+                   "head_dim": BLOCK_CFG["head_dim"], "ffn": BLOCK_CFG["ffn"], "window": "+-1 frame",
+                   "lora_rank": 32, "parallelism": f"ulysses sp{world}" if world > 1 else "single GPU",
+                   "l2": "per-step working set (activations > 1 GB) larger than L2",
+                   "gemm_tflops_per_step": round(flops / 1e12, 3)},
+        "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2},
+        "gpu_launches": block.launches_per_forward(world) * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (QKV, %d x 15360 x 5120)" % rows,
+                     "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / fp8_peak, 4), "traffic": None,
+                     "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']}): the FP8 rate",
+                     "algorithmic_flops_per_launch": gemm_flops},
+        "comparators": comp,
+        "kernels_ms": {k_: round(v_, 4) for k_, v_ in kt.items()},
+        "clocks": clk.summary(),
+    }
+    return rec
+
+
+def cpu_baseline_block(threads):
+    """Reference block composition (oracle/block.py) on the CPU for 3 of 21 frames."""
+    import torch
+    from oracle import block as oblock
+    from vdn_b200.block import BlockConfig
+    cfg = BlockConfig()
+    frames, tokens = 3, BLOCK_CFG["S"]
+    hd, ffn = cfg.hidden, cfg.ffn
+    g = torch.Generator().manual_seed(0)
+    w = dict(adaln_w=torch.randn(6 * hd, hd, generator=g) * 0.02, adaln_b=torch.zeros(6 * hd),
+             norm1=torch.ones(hd), norm2=torch.ones(hd),
+             qkv=torch.randn(3 * hd, hd, generator=g) * 0.02, qkv_b=torch.zeros(3 * hd),
+             o=torch.randn(hd, hd, generator=g) * 0.02, ol=torch.randn(hd, hd, generator=g) * 0.02,
+             o_b=torch.zeros(hd), up=torch.randn(ffn, hd, generator=g) * 0.02, up_b=torch.zeros(ffn),
+             down=torch.randn(hd, ffn, generator=g) * 0.02, down_b=torch.zeros(hd),
+             sg_w=torch.zeros(cfg.heads, hd), sg_b=torch.full((cfg.heads,), 4.595),
+             beta_w=torch.randn(cfg.heads, hd, generator=g) * 0.02,
+             og_down=torch.randn(cfg.head_dim, hd, generator=g) * 0.02,
+             og_up=torch.randn(hd, cfg.head_dim, generator=g) * 0.02, og_b=torch.zeros(hd))
+    x = torch.randn(frames * tokens, hd, generator=g).bfloat16()
+    temb = torch.randn(hd, generator=g)
+    alpha = lambda fm: torch.exp(-torch.nn.functional.softplus(torch.zeros(frames, cfg.heads, cfg.head_dim)))
+    t0 = time.perf_counter()
+    oblock.block_reference(x, temb, w, frames, tokens, cfg, alpha)
+    dt = time.perf_counter() - t0
+    return {"value": round(frames * tokens / dt, 2), "unit": "tokens/s", "cores": threads,
+            "kind": "port", "sample": "reference block composition (fp32 torch CPU + numpy oracle), "
+            "3 frames x 1560 tokens (per-token work is constant in the frame count)"}
+
+
 # ---------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="vda", choices=["vda"])
+    ap.add_argument("--workload", default="block", choices=["block", "vda"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -294,24 +424,29 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        import numpy as np  # noqa: F401
-        os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-        times = []
-        for _ in range(args.warmup):
-            cpu_baseline_vda(threads)
-        for _ in range(args.steps):
-            times.append(cpu_baseline_vda(threads)["value"])
-        value = sorted(times)[len(times) // 2]
-        base = cpu_baseline_vda(threads)
-        base["value"] = value
+        import torch
+        torch.set_num_threads(threads)
+        fn = cpu_baseline_block if args.workload == "block" else cpu_baseline_vda
+        steps, warmup = max(1, min(args.steps, 3)), 1
+        for _ in range(warmup):
+            fn(threads)
+        vals = sorted(fn(threads)["value"] for _ in range(steps))
+        base = fn(threads)
+        base["value"] = vals[len(vals) // 2]
+        if args.workload == "block":
+            meta = dict(metric="hybrid-block tokens/s (BASELINE config 3, 32760 tokens)",
+                        unit="tokens/s", scaling="strong",
+                        config={"workload": "hybrid_block_config3", **BLOCK_CFG})
+        else:
+            meta = dict(metric="VDA branch HBM GB/s (algorithmic bytes), BASELINE config 2",
+                        unit="GB/s", scaling="weak", config={"workload": "vda_config2", **VDA_CFG})
         print(json.dumps({
-            "impl": "reference", "metric": "VDA branch HBM GB/s (algorithmic bytes), BASELINE config 2",
-            "value": value, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp64/fp32 (numpy oracle)", "data": "synthetic",
-            "config": {"workload": "vda_config2", **VDA_CFG},
-            "cpu_baseline": base,
-            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+            "impl": "reference", "metric": meta["metric"], "value": base["value"], "unit": meta["unit"],
+            "n_gpus": args.gpus, "steps": steps, "warmup": warmup, "higher_is_better": True,
+            "scaling": meta["scaling"], "vs_baseline": None, "dtype": "fp32 (CPU reference port)",
+            "data": "synthetic", "config": meta["config"], "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": meta["unit"], "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}))
         return
 
     import torch
@@ -321,15 +456,20 @@ def main():
         from datetime import timedelta
         local = int(os.environ.get("LOCAL_RANK", "0"))
         torch.cuda.set_device(local)
-        dist_mod.init_process_group("nccl", timeout=timedelta(seconds=300),
+        dist_mod.init_process_group("nccl", timeout=timedelta(seconds=120),
                                     device_id=torch.device("cuda", local))
         dist = dist_mod
     else:
         torch.cuda.set_device(0)
-    rec = bench_vda(args, torch, dist, rank, world)
+    if args.workload == "block":
+        rec = bench_block(args, torch, dist, rank, world)
+    else:
+        rec = bench_vda(args, torch, dist, rank, world)
     if rank == 0:
         if not args.no_cpu_baseline:
-            rec["cpu_baseline"] = cpu_baseline_vda(threads)
+            torch.set_num_threads(threads)
+            rec["cpu_baseline"] = (cpu_baseline_block if args.workload == "block"
+                                   else cpu_baseline_vda)(threads)
         print(json.dumps(rec))
     if dist is not None:
         dist.barrier()

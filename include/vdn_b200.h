@@ -65,6 +65,15 @@ int vdn_mxfp8_padded_shape(int64_t rows, int64_t k, int64_t* rows_padded, int64_
 int vdn_mxfp8_quantize(const void* x, int64_t rows, int64_t k, int64_t row_stride,
                        uint8_t* q, uint8_t* s, int* nonfinite, cudaStream_t stream);
 
+/* vdn_mxfp8_quantize where logical column j of a row sits at element
+ * (j / group) * group_stride + j % group of that row: quantises one half of
+ * per-head interleaved [softmax | linear] rows (the Ulysses return buffer)
+ * without a copy.  group a multiple of 32.  Same codes as vdn_mxfp8_quantize
+ * on the gathered matrix. */
+int vdn_mxfp8_quantize_grouped(const void* x, int64_t rows, int64_t k, int64_t row_stride,
+                               int64_t group, int64_t group_stride, uint8_t* q, uint8_t* s,
+                               int* nonfinite, cudaStream_t stream);
+
 /* Fused activation producer: act(x) rounded to bf16, then quantised as above.
  * act = VDN_ACT_GELU_TANH / VDN_ACT_GELU_ERF read x [rows, k]; VDN_ACT_SWIGLU
  * reads x [rows, 2k] as (a | g) and produces a * silu(g).
@@ -107,6 +116,36 @@ int vdn_mxfp8_quantize_host(const void* x, int dtype, int64_t rows, int64_t k,
 int vdn_mxfp8_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, const uint8_t* ws,
                    const void* bias, int64_t m_pad, int64_t n, int64_t n_pad, int64_t k_pad,
                    int64_t rows_out, void* y, int64_t ldy, int* status, cudaStream_t stream);
+
+/* vdn_mxfp8_gemm over two K ranges with one accumulator, and an optional gated
+ * residual epilogue:
+ *   r = bf16(dequant(x1) dequant(w1)^T + dequant(x2) dequant(w2)^T) (+ bias)
+ *   y = resid != NULL ? bf16(resid + bf16(gate[col] * r)) : r
+ * (k_pad2 = 0 for a single range).  Covers the block's output projection
+ * to_out(softmax) + to_out_linear(VDA) as one GEMM over K = 2 x 5120, and the
+ * AdaLN gated residual adds, fused into the GEMM store.
+ * Replaces HybridAttention's to_out + to_out_linear add (src/models/hybrid_attention.py:217-254)
+ * and _post_ref (src/models/ops/fused_block.py:49-51) around MXFP8Linear. */
+int vdn_mxfp8_gemm_fused(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, const uint8_t* ws,
+                         int64_t k_pad, const uint8_t* xq2, const uint8_t* xs2, const uint8_t* wq2,
+                         const uint8_t* ws2, int64_t k_pad2, const void* bias, int64_t m_pad,
+                         int64_t n, int64_t n_pad, int64_t rows_out, void* y, int64_t ldy,
+                         const void* resid, int64_t ldr, const void* gate, int* status,
+                         cudaStream_t stream);
+
+/* Window-softmax combine: merges n_partials dense attentions of query frame f
+ * against key frame f + delta_j (outs[j] bf16 [rows_j, H*d] token-major, lses[j]
+ * fp32 [batches_j, H, S]; batch = f - batch0[j], valid for frame_lo[j] <= f <=
+ * frame_hi[j]) by their log-sum-exps, rounds to bf16, multiplies by the softmax
+ * gate (bf16, element (t, h) at t*g_ss + h*g_sh) and writes bf16 out (element
+ * (t, h, j) at t*out_ld + h*out_hs + j) and/or MXFP8 codes q [RP, H*d] and
+ * swizzled scales s.
+ * Replaces the window softmax combine and apply_softmax_gate of
+ * src/models/softmax_attention/decomposed.py and src/models/hybrid_attention.py:165-222. */
+int vdn_window_merge(int n_partials, const void* const* outs, const float* const* lses,
+                     const int* batch0, const int* frame_lo, const int* frame_hi, int F, int S,
+                     int H, int d, const void* gate, int64_t g_ss, int64_t g_sh, void* out_bf16,
+                     int64_t out_ld, int64_t out_hs, uint8_t* q, uint8_t* s, cudaStream_t stream);
 
 /* -------------------------------------------------------------------- VDA */
 

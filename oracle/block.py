@@ -1,0 +1,87 @@
+"""CPU fp32 reference of the hybrid DiT block. TEST INFRASTRUCTURE ONLY.
+
+Composition of the reference pieces (ec-jt/vdn), evaluated in fp32 on the CPU
+with the MXFP8 quantisation points of the B200 path reproduced bit-exactly by
+oracle.mxfp8 (so the GEMM inputs match) and the VDA branch by oracle.vda:
+
+  pre-norm + AdaLN ........ src/models/ops/fused_block.py:43-46 (_pre_ref)
+  MXFP8 linears ........... src/models/ops/mxfp8_linear.py:60-102 (dequantised GEMM)
+  window softmax .......... src/models/softmax_attention/window.py:56-111
+  softmax gate ............ src/models/attention_gates.py:13-55, hybrid_attention.py:217-222
+  linear branch ........... src/models/linear_attention/branch.py (oracle.vda)
+  output merge ............ src/models/hybrid_attention.py:250-255 (to_out + to_out_linear)
+  gated residual .......... src/models/ops/fused_block.py:49-51 (_post_ref)
+  GELU FFN ................ the BASELINE block's FFN (tanh GELU)
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import mxfp8 as omx
+from . import vda as ovda
+
+
+def _bf16(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.bfloat16).float()
+
+
+def _qdq(x: torch.Tensor) -> torch.Tensor:
+    """Activation through the MXFP8 quantiser and back (fp32 values of the codes)."""
+    q, s = omx.quantize(x.float().numpy())
+    return torch.from_numpy(omx.dequantize(q, s)[: x.shape[0], : x.shape[1]]).float()
+
+
+def _linear(x_dq, w_dq, bias):
+    y = _bf16(x_dq @ w_dq.T)
+    return y if bias is None else _bf16(y + bias.float())
+
+
+def prenorm(x, weight, scale, shift, eps):
+    x = x.float()
+    inv = torch.rsqrt(x.square().mean(-1, keepdim=True) + eps)
+    return _bf16((x * inv * weight.float()) * (1 + scale.float()) + shift.float())
+
+
+def window_attention(q, k, v, frames, tokens, radius, scale):
+    """Exact windowed softmax, one SDPA per query frame, fp32. q/k/v [T, H, d]."""
+    out = torch.empty_like(q)
+    for f in range(frames):
+        lo, hi = max(0, f - radius), min(frames - 1, f + radius)
+        qs = q[f * tokens:(f + 1) * tokens].permute(1, 0, 2)
+        ks = k[lo * tokens:(hi + 1) * tokens].permute(1, 0, 2)
+        vs = v[lo * tokens:(hi + 1) * tokens].permute(1, 0, 2)
+        out[f * tokens:(f + 1) * tokens] = F.scaled_dot_product_attention(
+            qs, ks, vs, scale=scale).permute(1, 0, 2)
+    return out
+
+
+def block_reference(x, temb, w, frames, tokens, cfg, alpha_fn):
+    """x [T, hidden] bf16 values; w: dict of dequantised fp32 weights / biases."""
+    hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+    T = frames * tokens
+    x = x.float()
+    ada = _bf16(F.silu(_bf16(temb.float())) @ w["adaln_w"].T + w["adaln_b"]).view(6, hd)
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = ada
+    y1 = prenorm(x, w["norm1"], scale_msa, shift_msa, cfg.eps)
+    qkv = _linear(_qdq(y1), w["qkv"], w["qkv_b"])
+    q, k, v = (qkv[:, i * hd:(i + 1) * hd].reshape(T, H, d) for i in range(3))
+    sgate = _bf16(torch.sigmoid(_bf16(y1 @ w["sg_w"].T + w["sg_b"])))
+    beta = _bf16(torch.sigmoid(_bf16(y1 @ w["beta_w"].T)))
+    lg = _bf16(torch.sigmoid(_bf16(_bf16(y1 @ w["og_down"].T) @ w["og_up"].T + w["og_b"])))
+    att = window_attention(q, k, v, frames, tokens, cfg.radius, d ** -0.5)
+    att = _bf16(_bf16(att) * sgate[..., None])
+    frame_mean = y1.view(frames, tokens, hd).mean(1)
+    alpha = alpha_fn(frame_mean).numpy()
+    lin = ovda.readout(q.numpy(), k.numpy(), v.numpy(), beta.numpy(), lg.view(T, H, d).numpy(),
+                       alpha, ovda.window_bounds(frames, cfg.radius), frames, tokens)
+    lin = torch.from_numpy(lin)
+    o = _bf16(_qdq(att.reshape(T, hd)) @ w["o"].T + _qdq(lin) @ w["ol"].T)
+    o = _bf16(o + w["o_b"].float())
+    x1 = _bf16(x + _bf16(gate_msa * o))
+    y2 = prenorm(x1, w["norm2"], scale_mlp, shift_mlp, cfg.eps)
+    up = _linear(_qdq(y2), w["up"], w["up_b"])
+    act = _bf16(F.gelu(up, approximate=cfg.gelu))
+    down = _linear(_qdq(act), w["down"], w["down_b"])
+    return _bf16(x1 + _bf16(gate_mlp * down))

@@ -1,0 +1,115 @@
+"""GPU: the hybrid DiT block against a CPU fp32 composition of the reference pieces.
+
+The reference composition (oracle/block.py) reproduces every MXFP8 quantisation
+point bit-exactly and evaluates the rest in fp32 (window softmax by one SDPA per
+frame, the VDA branch by the numpy oracle).  Tolerance on the block output:
+relative L2 < 1e-2 (bf16 rounding points and rare one-code MXFP8 flips they
+cause), and each sub-result is checked on its own first.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import block as oblock
+from oracle import mxfp8 as omx
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    a, b = a.double().cpu(), b.double().cpu()
+    return float((a - b).norm() / b.norm())
+
+
+def _deq(p):
+    w = omx.dequantize(p.q.cpu().numpy(), p.s.cpu().numpy())[: p.n, : p.k]
+    return torch.from_numpy(w).float()
+
+
+def _weights(block):
+    og = block.output_gate
+    return dict(
+        adaln_w=block.adaln.weight.float().cpu(), adaln_b=block.adaln.bias.float().cpu(),
+        norm1=block.norm1.cpu(), norm2=block.norm2.cpu(),
+        qkv=_deq(block.qkv), qkv_b=block.qkv.bias.float().cpu(),
+        o=_deq(block.o), ol=_deq(block.ol), o_b=block.o_bias.float().cpu(),
+        up=_deq(block.up), up_b=block.up.bias.float().cpu(),
+        down=_deq(block.down), down_b=block.down.bias.float().cpu(),
+        sg_w=block.softmax_gate.weight.float().cpu(), sg_b=block.softmax_gate.bias.float().cpu(),
+        beta_w=block.beta_proj.weight.float().cpu(),
+        og_down=og.down.weight.float().cpu(), og_up=og.up.weight.float().cpu(),
+        og_b=og.up.bias.float().cpu())
+
+
+def _small_block(cuda, seed=0):
+    from vdn_b200.block import BlockConfig, HybridBlock
+    cfg = BlockConfig(hidden=256, heads=2, head_dim=128, ffn=512, radius=1, lora_rank=8)
+    block = HybridBlock(cfg, seed=seed, device=cuda)
+    # Give the softmax gate live weights so the test exercises it.
+    torch.nn.init.normal_(block.softmax_gate.weight, std=0.05)
+    return cfg, block
+
+
+@pytest.mark.parametrize("frames,tokens", [(4, 64), (3, 100)])
+@torch.no_grad()
+def test_block_matches_reference_composition(cuda, frames, tokens):
+    cfg, block = _small_block(cuda)
+    g = torch.Generator().manual_seed(frames * 1000 + tokens)
+    T = frames * tokens
+    x = torch.randn(T, cfg.hidden, generator=g).bfloat16()
+    temb = torch.randn(cfg.hidden, generator=g)
+    out = block(x.to(cuda), temb.to(cuda), frames, tokens)
+    torch.cuda.synchronize()
+    assert out.shape == (T, cfg.hidden) and out.dtype == torch.bfloat16
+    assert bool(torch.isfinite(out).all())
+    ref = oblock.block_reference(x, temb, _weights(block), frames, tokens, cfg,
+                                 lambda fm: block.alpha(fm.to(cuda)).float().cpu())
+    err = _rel(out.float(), ref)
+    assert err < 1e-2, err
+
+
+@torch.no_grad()
+def test_window_softmax_matches_exact_window(cuda):
+    from vdn_b200.window import window_softmax
+    g = torch.Generator().manual_seed(5)
+    frames, tokens, H, d = 5, 48, 2, 128
+    T = frames * tokens
+    q, k, v = (torch.randn(T, H, d, generator=g).bfloat16() for _ in range(3))
+    gate = torch.rand(T, H, generator=g).bfloat16()
+    out = torch.zeros(T, H, d, dtype=torch.bfloat16, device=cuda)
+    codes = window_softmax(q.to(cuda), k.to(cuda), v.to(cuda), gate.to(cuda), frames, tokens, 1,
+                           out=out, quantize=True)
+    ref = oblock.window_attention(q.float(), k.float(), v.float(), frames, tokens, 1, d ** -0.5)
+    ref = (ref.bfloat16().float() * gate.float()[..., None])
+    assert _rel(out.float(), ref) < 5e-3
+    # The MXFP8 output is exactly the quantisation of the bf16 output.
+    rq, rs = omx.quantize(out.float().cpu().numpy().reshape(T, H * d))
+    assert np.array_equal(codes[0].cpu().numpy(), rq) and np.array_equal(codes[1].cpu().numpy(), rs)
+
+
+@torch.no_grad()
+def test_fused_gemm_dual_k_and_gated_residual(cuda):
+    from vdn_b200 import _lib
+    from vdn_b200.mxfp8_quant import quantize_activation
+    g = torch.Generator(device=cuda).manual_seed(9)
+    m, n, k1, k2 = 300, 384, 256, 512
+    x1 = torch.randn(m, k1, device=cuda, generator=g).bfloat16()
+    x2 = torch.randn(m, k2, device=cuda, generator=g).bfloat16()
+    w1 = (torch.randn(n, k1, device=cuda, generator=g) * 0.05).bfloat16()
+    w2 = (torch.randn(n, k2, device=cuda, generator=g) * 0.05).bfloat16()
+    (a1, s1), (a2, s2) = quantize_activation(x1), quantize_activation(x2)
+    (b1, t1), (b2, t2) = quantize_activation(w1), quantize_activation(w2)
+    bias = torch.randn(n, device=cuda, generator=g).bfloat16()
+    resid = torch.randn(m, n, device=cuda, generator=g).bfloat16()
+    gate = torch.rand(n, device=cuda, generator=g).bfloat16()
+    y = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
+    _lib.call("vdn_mxfp8_gemm_fused", _lib.ptr(a1), _lib.ptr(s1), _lib.ptr(b1), _lib.ptr(t1), k1,
+              _lib.ptr(a2), _lib.ptr(s2), _lib.ptr(b2), _lib.ptr(t2), k2, _lib.ptr(bias), a1.shape[0],
+              n, b1.shape[0], m, _lib.ptr(y), n, _lib.ptr(resid), n, _lib.ptr(gate), None,
+              _lib.stream_of(cuda))
+    torch.cuda.synchronize()
+    deq = lambda q, s: torch.from_numpy(omx.dequantize(q.cpu().numpy(), s.cpu().numpy()))
+    acc = deq(a1, s1)[:m, :k1] @ deq(b1, t1)[:n, :k1].T + deq(a2, s2)[:m, :k2] @ deq(b2, t2)[:n, :k2].T
+    r = (acc.float().bfloat16().float() + bias.float().cpu()).bfloat16().float()
+    want = (resid.float().cpu() + (gate.float().cpu() * r).bfloat16().float()).bfloat16()
+    torch.testing.assert_close(y.cpu(), want, rtol=.01, atol=.02)

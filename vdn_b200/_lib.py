@@ -36,6 +36,11 @@ SIGNATURES = {
     "vdn_finite_parts": (_i32, [_p, _i64, _i32, _i32, _p, _p]),
     "vdn_mxfp8_quantize_host": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _i32]),
     "vdn_mxfp8_gemm": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
+    "vdn_mxfp8_gemm_fused": (_i32, [_p, _p, _p, _p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64,
+                                    _i64, _p, _i64, _p, _i64, _p, _p, _p]),
+    "vdn_mxfp8_quantize_grouped": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "vdn_window_merge": (_i32, [_i32, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _p, _i64, _i64, _p,
+                                _i64, _i64, _p, _p, _p]),
     "vdn_delta_factors": (_i32, [_p, _p, _p, _i64, _i32, _p, _p, _p]),
     "vdn_vda_statistics": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                   _i32, _i32, _i32, _i32, _i32, _p, _p, _p]),

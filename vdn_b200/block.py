@@ -1,0 +1,222 @@
+"""One VDN-H3-style hybrid DiT block on the B200 kernels.
+
+    x -> RMSNorm * (1 + scale_msa) + shift_msa -> [bf16 y1, MXFP8]      prenorm producer
+      -> QKV (MXFP8 GEMM, N = 3 * hidden)
+      -> gates from y1: softmax gate [T,H], beta [T,H], linear gate [T,H*d] (bf16 linears)
+      -> frame mean of y1 -> alpha (FrameKDAAlpha)
+      -> [Ulysses: sequence -> heads all-to-all]
+      -> window softmax (+-radius frames) * softmax gate     cuDNN legs + vdn_window_merge
+      -> VDA linear branch                                    vdn_vda_forward
+      -> [Ulysses: heads -> sequence all-to-all]
+      -> x1 = x + gate_msa * (to_out(softmax) + to_out_linear(VDA))   one dual-K MXFP8 GEMM
+      -> RMSNorm * (1 + scale_mlp) + shift_mlp -> MXFP8 -> FFN up (MXFP8 GEMM)
+      -> GELU -> MXFP8 -> FFN down, x2 = x1 + gate_mlp * ffn          fused GEMM epilogue
+
+The pieces follow the reference: the pre-norm producer and gated residual of
+src/models/ops/fused_block.py:43-51 / mxfp8_kernels.py:86-139, the hybrid
+attention merge of src/models/hybrid_attention.py:178-255 (to_out + to_out_linear
+on the video rows), the standard Ulysses forward of
+src/inference/utils/ulysses.py:271-419 and the branch of
+src/models/linear_attention/branch.py.  The BASELINE block has no RoPE / QK-norm
+and no text rows; the FFN is GELU (tanh form) rather than H3's SwiGLU.  Weights
+are random (seeded), with a rank-32 LoRA merged into Q, K, V and O on the host
+before MXFP8 quantisation, as the reference merges before conversion.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import _lib
+from .linear_attention import FrameKDAAlpha, OutputGate, window_bounds
+from .mxfp8_kernels import launch_gelu_quantize, launch_prenorm_quantize
+from .mxfp8_quant import quantize_cpu, quantize_activation
+from .window import window_softmax
+
+__all__ = ["HybridBlock", "BlockConfig"]
+
+
+class BlockConfig:
+    def __init__(self, hidden=5120, heads=40, head_dim=128, ffn=13824, radius=1, lora_rank=32,
+                 eps=1e-6, gelu="tanh"):
+        self.hidden, self.heads, self.head_dim, self.ffn = hidden, heads, head_dim, ffn
+        self.radius, self.lora_rank, self.eps, self.gelu = radius, lora_rank, eps, gelu
+
+
+class _Packed:
+    """MXFP8 weight (codes, swizzled scales) + optional bf16 bias, resident on device."""
+
+    def __init__(self, w: torch.Tensor, bias: torch.Tensor | None, device):
+        self.n, self.k = w.shape
+        q, s = quantize_cpu(w.float())
+        self.q, self.s = q.to(device), s.to(device)
+        self.bias = None if bias is None else bias.to(torch.bfloat16).to(device)
+        self.n_pad, self.k_pad = q.shape
+
+
+class HybridBlock(nn.Module):
+    def __init__(self, cfg: BlockConfig | None = None, *, seed=0, device="cuda"):
+        super().__init__()
+        cfg = cfg or BlockConfig()
+        self.cfg = cfg
+        hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+        if H * d != hd:
+            raise ValueError("heads * head_dim must equal hidden")
+        g = torch.Generator().manual_seed(seed)
+        dev = torch.device(device)
+
+        def rnd(*shape, std=0.02):
+            return torch.randn(*shape, generator=g) * std
+
+        def lora(w):
+            r = cfg.lora_rank
+            a = torch.randn(r, w.shape[1], generator=g) * (1.0 / r) ** 0.5
+            b = torch.randn(w.shape[0], r, generator=g) * 0.02
+            return w + b @ a
+
+        wq, wk, wv = (lora(rnd(hd, hd)) for _ in range(3))
+        self.qkv = _Packed(torch.cat([wq, wk, wv]), rnd(3 * hd), dev)
+        self.o = _Packed(lora(rnd(hd, hd)), rnd(hd), dev)
+        self.ol = _Packed(rnd(hd, hd), rnd(hd), dev)
+        self.up = _Packed(rnd(cfg.ffn, hd), rnd(cfg.ffn), dev)
+        self.down = _Packed(rnd(hd, cfg.ffn), rnd(hd), dev)
+        self.o_bias = (self.o.bias.float() + self.ol.bias.float()).to(torch.bfloat16)
+        # bf16 small projections (the reference keeps these unquantised)
+        self.adaln = nn.Linear(hd, 6 * hd).to(dev, torch.bfloat16)
+        self.softmax_gate = nn.Linear(hd, H).to(dev, torch.bfloat16)
+        nn.init.zeros_(self.softmax_gate.weight)
+        nn.init.constant_(self.softmax_gate.bias, math.log(0.99 / 0.01))
+        self.beta_proj = nn.Linear(hd, H, bias=False).to(dev, torch.bfloat16)
+        self.output_gate = OutputGate(hd, H, d, bottleneck=d, init="random").to(dev, torch.bfloat16)
+        self.alpha = FrameKDAAlpha(hd, H, d).to(dev)
+        self.norm1 = torch.ones(hd, device=dev)
+        self.norm2 = torch.ones(hd, device=dev)
+        self.vda_norm = torch.ones(d, device=dev)
+        self.eval()
+        self._status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    # ---------------------------------------------------------------- helpers
+    def _gemm(self, a_q, a_s, w: _Packed, rows, out, *, second=None, bias=None, resid=None, gate=None):
+        m_pad = a_q.shape[0]
+        aq2 = as2 = wq2 = ws2 = None
+        k2 = 0
+        if second is not None:
+            (aq2, as2), w2 = second
+            wq2, ws2, k2 = w2.q, w2.s, w2.k_pad
+        _lib.call("vdn_mxfp8_gemm_fused", _lib.ptr(a_q), _lib.ptr(a_s), _lib.ptr(w.q), _lib.ptr(w.s),
+                  w.k_pad, _lib.ptr(aq2), _lib.ptr(as2), _lib.ptr(wq2), _lib.ptr(ws2), k2,
+                  _lib.ptr(bias), m_pad, w.n, w.n_pad, rows, _lib.ptr(out), out.stride(0),
+                  _lib.ptr(resid), resid.stride(0) if resid is not None else 0, _lib.ptr(gate),
+                  _lib.ptr(self._status), _lib.stream_of(out.device))
+        return out
+
+    def launches_per_forward(self, world_size=1):
+        """Kernels of this library launched per block forward (for bench accounting)."""
+        # prenorm, QKV GEMM, window merge, VDA (5), quantise VDA out, O GEMM, prenorm,
+        # FFN up, GELU quantise, FFN down; Ulysses adds two grouped quantisers
+        return 14 + (1 if world_size > 1 else 0)
+
+    # ---------------------------------------------------------------- forward
+    @torch.no_grad()
+    def forward(self, x, temb, frames, tokens, runtime=None):
+        """x: this rank's rows [T_local, hidden] bf16 (all T rows when runtime is None)."""
+        cfg = self.cfg
+        hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+        T = frames * tokens
+        rows = x.shape[0]
+        dev = x.device
+        ada = self.adaln(F.silu(temb.to(torch.bfloat16)).view(1, hd)).view(6, hd)
+        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = ada
+        idx = torch.zeros(rows, dtype=torch.int64, device=dev)
+        y1, q1, s1, _ = launch_prenorm_quantize(x, self.norm1, cfg.eps, scale_msa.view(1, hd),
+                                                shift_msa.view(1, hd), idx, write_bf16=True)
+        qkv = torch.empty(rows, 3 * hd, device=dev, dtype=torch.bfloat16)
+        self._gemm(q1, s1, self.qkv, rows, qkv, bias=self.qkv.bias)
+        sgate = torch.sigmoid(self.softmax_gate(y1))                      # [rows, H]
+        beta = torch.sigmoid(self.beta_proj(y1))                          # [rows, H]
+        lgate = self.output_gate(y1).reshape(rows, hd)                    # [rows, H*d]
+        if runtime is None:
+            frame_mean = y1.view(frames, tokens, hd).mean(1, dtype=torch.float32)
+            first, second = self._attention(qkv, sgate, beta, lgate, frame_mean, frames, tokens,
+                                            heads=slice(0, H))
+        else:
+            first, second = self._attention_ulysses(qkv, sgate, beta, lgate, y1, frames, tokens,
+                                                    runtime)
+        x1 = torch.empty_like(x)
+        self._gemm(first[0], first[1], self.o, rows, x1, second=(second, self.ol),
+                   bias=self.o_bias, resid=x, gate=gate_msa.contiguous())
+        _, q2, s2, _ = launch_prenorm_quantize(x1, self.norm2, cfg.eps, scale_mlp.view(1, hd),
+                                               shift_mlp.view(1, hd), idx, write_bf16=False)
+        up = torch.empty(rows, cfg.ffn, device=dev, dtype=torch.bfloat16)
+        self._gemm(q2, s2, self.up, rows, up, bias=self.up.bias)
+        q3, s3, _ = launch_gelu_quantize(up, approximate=cfg.gelu)
+        x2 = torch.empty_like(x)
+        self._gemm(q3, s3, self.down, rows, x2, bias=self.down.bias, resid=x1, gate=gate_mlp.contiguous())
+        return x2
+
+    def _attention(self, qkv, sgate, beta, lgate, frame_mean, frames, tokens, heads):
+        """Single-GPU attention: returns ((codes, scales) softmax, (codes, scales) VDA)."""
+        from .linear_attention import vda_forward
+        cfg = self.cfg
+        hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+        T = frames * tokens
+        q = qkv[:, :hd].view(T, H, d)
+        k = qkv[:, hd:2 * hd].view(T, H, d)
+        v = qkv[:, 2 * hd:].view(T, H, d)
+        att = window_softmax(q, k, v, sgate, frames, tokens, cfg.radius, quantize=True)
+        alpha = self.alpha(frame_mean, heads=heads)
+        bounds = window_bounds(frames, cfg.radius)
+        lin = vda_forward(q, k, v, beta, lgate.view(T, H, d), alpha, bounds, frames, tokens,
+                          self.vda_norm)
+        return att, quantize_activation(lin, check_finite=False)
+
+    def _attention_ulysses(self, qkv, sgate, beta, lgate, y1, frames, tokens, rt):
+        """Head-sharded attention between the two Ulysses exchanges."""
+        from .linear_attention import vda_forward
+        cfg = self.cfg
+        hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+        T = frames * tokens
+        rows = qkv.shape[0]
+        P = rt.world_size
+        hl = H // P
+        sums, work = rt.video_frame_mean_async(y1, frames, tokens)
+        # Pack per head: q | k | v | linear gate | softmax gate | beta | pad -> W = 4d + 8.
+        W = 4 * d + 8
+        pack = torch.empty(rows, H, W, device=qkv.device, dtype=torch.bfloat16)
+        pack[:, :, 0:3 * d] = qkv.view(rows, 3, H, d).permute(0, 2, 1, 3).reshape(rows, H, 3 * d)
+        pack[:, :, 3 * d:4 * d] = lgate.view(rows, H, d)
+        pack[:, :, 4 * d] = sgate
+        pack[:, :, 4 * d + 1] = beta
+        recv = rt.sequence_to_heads(pack)                                 # [T, H/P, W]
+        work.wait()
+        frame_mean = sums / tokens
+        first = rt.rank * hl
+        heads = slice(first, first + hl)
+        q, k, v = recv[:, :, 0:d], recv[:, :, d:2 * d], recv[:, :, 2 * d:3 * d]
+        ret = torch.empty(T, hl, 2 * d, device=qkv.device, dtype=torch.bfloat16)
+        window_softmax(q, k, v, recv[:, :, 4 * d], frames, tokens, cfg.radius, out=ret[:, :, :d])
+        alpha = self.alpha(frame_mean, heads=heads)
+        bounds = window_bounds(frames, cfg.radius)
+        lin = vda_forward(q, k, v, recv[:, :, 4 * d + 1], recv[:, :, 3 * d:4 * d], alpha, bounds,
+                          frames, tokens, self.vda_norm)
+        ret[:, :, d:] = lin.view(T, hl, d)
+        back = rt.heads_to_sequence(ret)                                  # [rows, H, 2d]
+        flat = back.view(rows, H * 2 * d)
+        att = self._quantize_grouped(flat, 0, rows)
+        lq = self._quantize_grouped(flat, d, rows)
+        return att, lq
+
+    def _quantize_grouped(self, flat, offset, rows):
+        cfg = self.cfg
+        hd, d = cfg.hidden, cfg.head_dim
+        rp = (rows + 127) // 128 * 128
+        q = torch.empty(rp, hd, dtype=torch.uint8, device=flat.device)
+        s = torch.empty(rp * hd // 32, dtype=torch.uint8, device=flat.device)
+        src = flat[:, offset:]
+        _lib.call("vdn_mxfp8_quantize_grouped", _lib.C.c_void_p(src.data_ptr()), rows, hd,
+                  flat.stride(0), d, 2 * d, _lib.ptr(q), _lib.ptr(s), None,
+                  _lib.stream_of(flat.device))
+        return q, s

@@ -43,13 +43,21 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
   return __uint_as_float(bits16 << 16);
 }
 
-// Round to nearest even, finite inputs (the hardware conversion).
+// fp32 -> bf16, round to nearest even (hardware conversion).
 __device__ __forceinline__ uint16_t f32_to_bf16_bits(float x) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
 __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// Two roundings in one conversion instruction.
+__device__ __forceinline__ void round_bf16_pair(float& a, float& b) {
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(b), "f"(a));
+  a = __uint_as_float(p << 16);
+  b = __uint_as_float(p & 0xFFFF0000u);
 }
 
 // Unpacks the 8 bf16 values of a 16-byte vector.
@@ -62,13 +70,26 @@ __device__ __forceinline__ void unpack8(const uint4& v, float* out) {
   }
 }
 
+// Rounds two floats to bf16 and packs them (lo in the low half), one instruction.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(hi), "f"(lo));
+  return p;
 }
 
 __device__ __forceinline__ uint4 pack8(const float* v) {
   return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
                     pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+}
+
+// Packs floats that already hold bf16 values (no rounding: a byte permute).
+__device__ __forceinline__ uint32_t pack_exact2(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+}
+
+__device__ __forceinline__ uint4 pack_exact8(const float* v) {
+  return make_uint4(pack_exact2(v[0], v[1]), pack_exact2(v[2], v[3]),
+                    pack_exact2(v[4], v[5]), pack_exact2(v[6], v[7]));
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }

@@ -44,12 +44,17 @@ constexpr size_t SMEM_BYTES =
 struct Params {
   const uint8_t* xs;
   const uint8_t* ws;
+  const uint8_t* xs2;        // second K range (k_blocks2 > 0): scales of A2 / B2
+  const uint8_t* ws2;
   const uint16_t* bias;
+  const uint16_t* resid;     // optional epilogue: y = resid + gate[col] * result
+  const uint16_t* gate;
+  int64_t ldr;
   uint16_t* y;
   int64_t ldy;
   int64_t rows_out;
   int64_t n;
-  int m_tiles, n_tiles, k_blocks, n_groups;  // n_groups = n_pad / 128
+  int m_tiles, n_tiles, k_blocks, k_blocks2, n_groups;  // n_groups = n_pad / 128
   int* status;
 };
 
@@ -65,7 +70,9 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 
 __global__ void __launch_bounds__(THREADS, 1)
     mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                      const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+                      const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_a2,
+                      const __grid_constant__ CUtensorMap tmap_b2, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -92,6 +99,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_barrier_init();
     prefetch_tensormap(&tmap_a);
     prefetch_tensormap(&tmap_b);
+    if (p.k_blocks2) {
+      prefetch_tensormap(&tmap_a2);
+      prefetch_tensormap(&tmap_b2);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
   tc_fence_before();
@@ -111,17 +122,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         int mb, nb;
         tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
         const bool has_b1 = 2 * nb + 1 < p.n_groups;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        const int kb_total = p.k_blocks + p.k_blocks2;
+        for (int kbt = 0; kbt < kb_total; ++kbt) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
+          // K blocks of the first operand pair, then of the second (K concatenation).
+          const bool second = kbt >= p.k_blocks;
+          const int kb = second ? kbt - p.k_blocks : kbt;
+          const int kbn = second ? p.k_blocks2 : p.k_blocks;
+          const CUtensorMap* ma = second ? &tmap_a2 : &tmap_a;
+          const CUtensorMap* mbm = second ? &tmap_b2 : &tmap_b;
+          const uint8_t* xs = second ? p.xs2 : p.xs;
+          const uint8_t* ws = second ? p.ws2 : p.ws;
           const uint32_t bytes = A_BYTES + B_BYTES + (has_b1 ? 3 : 2) * 512;
           mbar_arrive_expect_tx(&full[stage], bytes);
-          tma_load_2d(sA + stage * A_BYTES, &tmap_a, &full[stage], kb * BK, mb * BM);
-          tma_load_2d(sB + stage * B_BYTES, &tmap_b, &full[stage], kb * BK, nb * BN);
+          tma_load_2d(sA + stage * A_BYTES, ma, &full[stage], kb * BK, mb * BM);
+          tma_load_2d(sB + stage * B_BYTES, mbm, &full[stage], kb * BK, nb * BN);
           uint8_t* sf = sSF + stage * SF_STAGE;
-          bulk_load(sf, p.xs + ((int64_t)mb * p.k_blocks + kb) * 512, 512, &full[stage]);
-          bulk_load(sf + 512, p.ws + ((int64_t)(2 * nb) * p.k_blocks + kb) * 512, 512, &full[stage]);
+          bulk_load(sf, xs + ((int64_t)mb * kbn + kb) * 512, 512, &full[stage]);
+          bulk_load(sf + 512, ws + ((int64_t)(2 * nb) * kbn + kb) * 512, 512, &full[stage]);
           if (has_b1)
-            bulk_load(sf + 1024, p.ws + ((int64_t)(2 * nb + 1) * p.k_blocks + kb) * 512, 512, &full[stage]);
+            bulk_load(sf + 1024, ws + ((int64_t)(2 * nb + 1) * kbn + kb) * 512, 512, &full[stage]);
           pending |= 1u << stage;
           pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -151,7 +171,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(acc_empty, acc_phase ^ 1, abort_flag)) break;
         tc_fence_after();
         bool ok = true;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        const int kb_total = p.k_blocks + p.k_blocks2;
+        for (int kb = 0; kb < kb_total; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
             break;
@@ -214,10 +235,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           v[i] = round_bf16(__uint_as_float(r[i]));
+          const int64_t col = col0 + i;
           if (p.bias) {
-            const int64_t col = col0 + i;
             const float b = col < p.n ? bf16_bits_to_f32(p.bias[col]) : 0.f;
             v[i] = round_bf16(v[i] + b);
+          }
+          if (p.resid && col < p.n) {  // gated residual: resid + bf16(gate * y), bf16
+            const float g = bf16_bits_to_f32(p.gate[col]);
+            v[i] = bf16_bits_to_f32(p.resid[row * p.ldr + col]) + round_bf16(g * v[i]);
           }
         }
         if (col0 + 32 <= p.n && ((reinterpret_cast<uintptr_t>(yrow + col0) & 15) == 0)) {
@@ -300,30 +325,48 @@ static int device_info(DeviceInfo** out) {
 
 using namespace vdn;
 
-extern "C" int vdn_mxfp8_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq,
-                              const uint8_t* ws, const void* bias, int64_t m_pad, int64_t n,
-                              int64_t n_pad, int64_t k_pad, int64_t rows_out, void* y, int64_t ldy,
-                              int* status, cudaStream_t stream) {
+static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, const uint8_t* ws,
+                       int64_t k_pad, const uint8_t* xq2, const uint8_t* xs2, const uint8_t* wq2,
+                       const uint8_t* ws2, int64_t k_pad2, const void* bias, int64_t m_pad,
+                       int64_t n, int64_t n_pad, int64_t rows_out, void* y, int64_t ldy,
+                       const void* resid, int64_t ldr, const void* gate, int* status,
+                       cudaStream_t stream) {
   using namespace vdn::gemm;
-  VDN_CHECK_ARG(m_pad >= 0 && n > 0 && n_pad > 0 && k_pad > 0, "bad GEMM extents");
-  VDN_CHECK_ARG(m_pad % 128 == 0 && n_pad % 128 == 0 && k_pad % 128 == 0,
+  VDN_CHECK_ARG(m_pad >= 0 && n > 0 && n_pad > 0 && k_pad > 0 && k_pad2 >= 0, "bad GEMM extents");
+  VDN_CHECK_ARG(m_pad % 128 == 0 && n_pad % 128 == 0 && k_pad % 128 == 0 && k_pad2 % 128 == 0,
                 "m_pad, n_pad and k_pad must be multiples of 128");
   VDN_CHECK_ARG(n <= n_pad && rows_out >= 0 && rows_out <= m_pad, "crop exceeds the padded extents");
   VDN_CHECK_ARG(ldy >= n, "ldy must be at least n");
+  VDN_CHECK_ARG(!resid || (gate && ldr >= n), "a residual needs a gate vector and ldr >= n");
   if (rows_out == 0 || m_pad == 0) return VDN_OK;
   VDN_CHECK_ARG(xq && xs && wq && ws && y, "null pointer");
   VDN_CHECK_ARG(aligned16(xq) && aligned16(xs) && aligned16(wq) && aligned16(ws),
                 "codes and scales must be 16-byte aligned");
+  VDN_CHECK_ARG(k_pad2 == 0 || (xq2 && xs2 && wq2 && ws2 && aligned16(xq2) && aligned16(xs2) &&
+                                aligned16(wq2) && aligned16(ws2)),
+                "second operand pair must be non-null and 16-byte aligned");
   VDN_CHECK_ARG(m_pad / 128 < (1 << 30) && n_pad / 128 < (1 << 30), "extents too large");
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, ma2, mb2;
   if (int rc = make_map(&ma, xq, k_pad, m_pad, BM)) return rc;
   if (int rc = make_map(&mb, wq, k_pad, n_pad, BN)) return rc;
+  if (k_pad2) {
+    if (int rc = make_map(&ma2, xq2, k_pad2, m_pad, BM)) return rc;
+    if (int rc = make_map(&mb2, wq2, k_pad2, n_pad, BN)) return rc;
+  } else {
+    ma2 = ma;
+    mb2 = mb;
+  }
   Params p;
   p.xs = xs;
   p.ws = ws;
+  p.xs2 = xs2;
+  p.ws2 = ws2;
   p.bias = static_cast<const uint16_t*>(bias);
+  p.resid = static_cast<const uint16_t*>(resid);
+  p.gate = static_cast<const uint16_t*>(gate);
+  p.ldr = ldr;
   p.y = static_cast<uint16_t*>(y);
   p.ldy = ldy;
   p.rows_out = rows_out;
@@ -331,11 +374,31 @@ extern "C" int vdn_mxfp8_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_
   p.m_tiles = (int)(m_pad / BM);
   p.n_tiles = (int)((n_pad + BN - 1) / BN);
   p.k_blocks = (int)(k_pad / BK);
+  p.k_blocks2 = (int)(k_pad2 / BK);
   p.n_groups = (int)(n_pad / 128);
   p.status = status;
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < info->sms ? tiles : info->sms;
-  mxfp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  mxfp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, p);
   VDN_LAUNCH_CHECK("mxfp8 gemm");
   return VDN_OK;
+}
+
+extern "C" int vdn_mxfp8_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq,
+                              const uint8_t* ws, const void* bias, int64_t m_pad, int64_t n,
+                              int64_t n_pad, int64_t k_pad, int64_t rows_out, void* y, int64_t ldy,
+                              int* status, cudaStream_t stream) {
+  return launch_gemm(xq, xs, wq, ws, k_pad, nullptr, nullptr, nullptr, nullptr, 0, bias, m_pad, n,
+                     n_pad, rows_out, y, ldy, nullptr, 0, nullptr, status, stream);
+}
+
+extern "C" int vdn_mxfp8_gemm_fused(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq,
+                                    const uint8_t* ws, int64_t k_pad, const uint8_t* xq2,
+                                    const uint8_t* xs2, const uint8_t* wq2, const uint8_t* ws2,
+                                    int64_t k_pad2, const void* bias, int64_t m_pad, int64_t n,
+                                    int64_t n_pad, int64_t rows_out, void* y, int64_t ldy,
+                                    const void* resid, int64_t ldr, const void* gate, int* status,
+                                    cudaStream_t stream) {
+  return launch_gemm(xq, xs, wq, ws, k_pad, xq2, xs2, wq2, ws2, k_pad2, bias, m_pad, n, n_pad,
+                     rows_out, y, ldy, resid, ldr, gate, status, stream);
 }

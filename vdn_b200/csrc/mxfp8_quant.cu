@@ -67,21 +67,26 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
 }
 
+// Column grouping: logical column j of a row lives at (j / group) * group_stride
+// + j % group (group = k, group_stride = k for a plain row).  Used to quantise
+// one half of per-head interleaved [softmax | linear] rows without a copy.
 // Loads the 32 inputs of block (r, c) as fp32, zero outside [rows, k).
 template <bool VEC>
 __device__ __forceinline__ void load_block(const uint16_t* __restrict__ x, int64_t row_stride,
                                            int64_t r, int64_t c, int64_t rows, int64_t k,
-                                           float* v) {
+                                           float* v, int64_t group = 0, int64_t group_stride = 0) {
   const int64_t col0 = c * 32;
+  const int64_t phys0 = group ? (col0 / group) * group_stride + col0 % group : col0;
   if (r < rows && VEC && col0 + 32 <= k) {
-    const uint4* p = reinterpret_cast<const uint4*>(x + r * row_stride + col0);
+    const uint4* p = reinterpret_cast<const uint4*>(x + r * row_stride + phys0);
 #pragma unroll
     for (int i = 0; i < 4; ++i) unpack8(__ldg(p + i), v + 8 * i);
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int64_t col = col0 + i;
-      v[i] = (r < rows && col < k) ? bf16_bits_to_f32(x[r * row_stride + col]) : 0.0f;
+      const int64_t phys = group ? (col / group) * group_stride + col % group : col;
+      v[i] = (r < rows && col < k) ? bf16_bits_to_f32(x[r * row_stride + phys]) : 0.0f;
     }
   }
 }
@@ -91,7 +96,8 @@ __device__ __forceinline__ void load_block(const uint16_t* __restrict__ x, int64
 template <int ACT, bool VEC>
 __global__ void __launch_bounds__(256) act_quantize_kernel(
     const uint16_t* __restrict__ x, int64_t row_stride, int64_t rows, int64_t k, int64_t rp,
-    int64_t kp, uint8_t* __restrict__ q, uint8_t* __restrict__ s, int* __restrict__ nonfinite) {
+    int64_t kp, uint8_t* __restrict__ q, uint8_t* __restrict__ s, int* __restrict__ nonfinite,
+    int64_t group = 0, int64_t group_stride = 0) {
   const int64_t nblk = kp >> 5;
   const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool active = g < rp * nblk;
@@ -102,7 +108,7 @@ __global__ void __launch_bounds__(256) act_quantize_kernel(
   for (int i = 0; i < 32; ++i) v[i] = 0.0f;
   bool bad = false;
   if (active) {
-    load_block<VEC>(x, row_stride, r, c, rows, k, v);
+    load_block<VEC>(x, row_stride, r, c, rows, k, v, group, group_stride);
 #pragma unroll
     for (int i = 0; i < 32; ++i) bad |= !isfinite(v[i]);
     if (ACT == ACT_SWIGLU) {
@@ -372,6 +378,30 @@ static int launch_act_quantize(int act, const void* x, int64_t rows, int64_t k, 
 int vdn_mxfp8_quantize(const void* x, int64_t rows, int64_t k, int64_t row_stride, uint8_t* q,
                        uint8_t* s, int* nonfinite, cudaStream_t stream) {
   return launch_act_quantize(ACT_NONE, x, rows, k, row_stride, q, s, nonfinite, stream);
+}
+
+int vdn_mxfp8_quantize_grouped(const void* x, int64_t rows, int64_t k, int64_t row_stride,
+                               int64_t group, int64_t group_stride, uint8_t* q, uint8_t* s,
+                               int* nonfinite, cudaStream_t stream) {
+  VDN_CHECK_ARG(rows >= 0 && k > 0, "rows must be nonnegative and K positive");
+  VDN_CHECK_ARG(group > 0 && group % 32 == 0 && group_stride >= group,
+                "group must be a positive multiple of 32 and group_stride >= group");
+  if (rows == 0) return VDN_OK;
+  VDN_CHECK_ARG(x && q && s, "null pointer");
+  VDN_CHECK_ARG(aligned16(q) && aligned16(s), "q and s must be 16-byte aligned");
+  const int64_t rp = (rows + 127) / 128 * 128, kp = (k + 127) / 128 * 128;
+  const bool vec = aligned16(x) && row_stride % 8 == 0 && group_stride % 8 == 0;
+  const int64_t threads = rp * (kp / 32);
+  const dim3 grid((unsigned)((threads + 255) / 256)), block(256);
+  const uint16_t* xp = static_cast<const uint16_t*>(x);
+  if (vec)
+    act_quantize_kernel<ACT_NONE, true><<<grid, block, 0, stream>>>(xp, row_stride, rows, k, rp, kp, q, s,
+                                                                     nonfinite, group, group_stride);
+  else
+    act_quantize_kernel<ACT_NONE, false><<<grid, block, 0, stream>>>(xp, row_stride, rows, k, rp, kp, q, s,
+                                                                      nonfinite, group, group_stride);
+  VDN_LAUNCH_CHECK("mxfp8 quantize (grouped)");
+  return VDN_OK;
 }
 
 int vdn_mxfp8_act_quantize(int act, const void* x, int64_t rows, int64_t k, int64_t row_stride,

@@ -13,6 +13,7 @@
 // Reference: ec-jt/vdn src/models/linear_attention/{scan.py, delta_rule.py,
 // branch.py, paper_stack.py, paper_sglang.py}.
 #include "common.cuh"
+#include "sm100.cuh"
 
 #include <algorithm>
 
@@ -148,21 +149,24 @@ __global__ void __launch_bounds__(256) stats_kernel(
 // One CTA per matrix; thread (ty, tx) holds rows ty*T.., cols tx*T.. of the
 // working matrix in registers. T may alias A and J may alias B (each CTA reads
 // its whole matrix before the first store), so those pointers are not restrict.
-// Non-pivoting in-place Gauss-Jordan inversion of the SPD M = I + A: at pivot p the owners publish row p and column p through
-// double-buffered shared vectors, then every thread applies the rank-1 update.
+// Non-pivoting in-place Gauss-Jordan inversion of the SPD M = I + A: at pivot p
+// the owners publish row p and column p through double-buffered shared vectors,
+// every thread applies the rank-1 update with one FMA per element, and the
+// owners of row / column p then overwrite those entries.  J = B inv reads B
+// rows from global (L2) and inv from shared memory.
 template <int D>
-__global__ void __launch_bounds__(256) factor_kernel(const float* A, const float* B,
-                                                     const float* __restrict__ alpha,
-                                                     float* Tout, float* Jout) {
+__global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const float* B,
+                                                        const float* __restrict__ alpha,
+                                                        float* Tout, float* Jout) {
   constexpr int T = D / 16;
   extern __shared__ float smem[];
   float* rowbuf = smem;            // [2][D]
   float* colbuf = smem + 2 * D;    // [2][D]
-  float* inv_s = smem + 4 * D;     // [D][D] inverse, then reused
-  float* b_s = inv_s + D * D;      // [D][D] B
+  float* inv_s = smem + 4 * D;     // [D][D]
   const int64_t mat = blockIdx.x;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const float* a_in = A + mat * D * D;
+  const float* b_in = B + mat * D * D;
   float m[T][T];
 #pragma unroll
   for (int i = 0; i < T; ++i)
@@ -171,11 +175,6 @@ __global__ void __launch_bounds__(256) factor_kernel(const float* A, const float
       const int r = ty * T + i, c = tx * T + j;
       m[i][j] = a_in[r * D + c] + (r == c ? 1.0f : 0.0f);
     }
-  // Stage B while the inversion runs (read-only until the product).
-  const float* b_in = B + mat * D * D;
-  for (int e = threadIdx.x * 4; e < D * D; e += 256 * 4)
-    *reinterpret_cast<float4*>(b_s + e) = *reinterpret_cast<const float4*>(b_in + e);
-
   // Outer loop over pivot blocks, inner loop unrolled so the pivot's position
   // inside a thread's tile is a compile-time index (m stays in registers).
   for (int pb = 0; pb < D / T; ++pb) {
@@ -193,31 +192,30 @@ __global__ void __launch_bounds__(256) factor_kernel(const float* A, const float
         for (int i = 0; i < T; ++i) cb[ty * T + i] = m[i][pi];
       }
       __syncthreads();
-      const float piv = rb[p];
-      const float ip = __fdiv_rn(1.0f, piv);
+      const float ip = __fdiv_rn(1.0f, rb[p]);
       float prow[T], pcol[T];
 #pragma unroll
       for (int j = 0; j < T; ++j) prow[j] = rb[tx * T + j] * ip;
 #pragma unroll
       for (int i = 0; i < T; ++i) pcol[i] = cb[ty * T + i];
 #pragma unroll
-      for (int i = 0; i < T; ++i) {
-        const bool row_is_p = (ty == pb) && (i == pi);
+      for (int i = 0; i < T; ++i)
 #pragma unroll
-        for (int j = 0; j < T; ++j) {
-          const bool col_is_p = (tx == pb) && (j == pi);
-          float val;
-          if (row_is_p) val = col_is_p ? ip : prow[j];
-          else if (col_is_p) val = -pcol[i] * ip;
-          else val = fmaf(-pcol[i], prow[j], m[i][j]);
-          m[i][j] = val;
-        }
+        for (int j = 0; j < T; ++j) m[i][j] = fmaf(-pcol[i], prow[j], m[i][j]);
+      if (ty == pb) {
+#pragma unroll
+        for (int j = 0; j < T; ++j) m[pi][j] = prow[j];
+      }
+      if (tx == pb) {
+#pragma unroll
+        for (int i = 0; i < T; ++i) m[i][pi] = -pcol[i] * ip;
+        if (ty == pb) m[pi][pi] = ip;
       }
     }
   }
-  __syncthreads();
   const float* al = alpha ? alpha + mat * D : nullptr;
   float* t_out = Tout + mat * D * D;
+  __syncthreads();  // all reads of A are done before T (which may alias A) is stored
 #pragma unroll
   for (int i = 0; i < T; ++i)
 #pragma unroll
@@ -233,17 +231,24 @@ __global__ void __launch_bounds__(256) factor_kernel(const float* A, const float
   for (int i = 0; i < T; ++i)
 #pragma unroll
     for (int j = 0; j < T; ++j) acc[i][j] = 0.f;
-  for (int kk = 0; kk < D; ++kk) {
-    float bv[T], iv[T];
+  for (int k4 = 0; k4 < D; k4 += 4) {
+    float4 bv[T];
 #pragma unroll
-    for (int i = 0; i < T; ++i) bv[i] = b_s[(ty * T + i) * D + kk];
+    for (int i = 0; i < T; ++i) bv[i] = *reinterpret_cast<const float4*>(b_in + (ty * T + i) * D + k4);
 #pragma unroll
-    for (int j = 0; j < T; ++j) iv[j] = inv_s[kk * D + tx * T + j];
+    for (int kk = 0; kk < 4; ++kk) {
+      float iv[T];
 #pragma unroll
-    for (int i = 0; i < T; ++i)
+      for (int j = 0; j < T; ++j) iv[j] = inv_s[(k4 + kk) * D + tx * T + j];
 #pragma unroll
-      for (int j = 0; j < T; ++j) acc[i][j] = fmaf(bv[i], iv[j], acc[i][j]);
+      for (int i = 0; i < T; ++i) {
+        const float b = kk == 0 ? bv[i].x : kk == 1 ? bv[i].y : kk == 2 ? bv[i].z : bv[i].w;
+#pragma unroll
+        for (int j = 0; j < T; ++j) acc[i][j] = fmaf(b, iv[j], acc[i][j]);
+      }
+    }
   }
+  __syncthreads();  // all reads of B are done before J (which may alias B) is stored
   float* j_out = Jout + mat * D * D;
 #pragma unroll
   for (int i = 0; i < T; ++i)
@@ -252,46 +257,105 @@ __global__ void __launch_bounds__(256) factor_kernel(const float* A, const float
 }
 
 // ----------------------------------------------------------------------- scan
-// grid (H, 2, D/16); 256 threads; thread owns row t/16 of the CTA's 16 rows and
-// D/16 consecutive columns.
+// grid (H, 2 directions, D/64 row blocks); 256 threads in a 16 x 16 grid, each
+// owning 4 state rows x D/16 columns.  Rows of the state evolve independently,
+// so a CTA carries 64 rows through all F steps.  T_f arrives by a 64 KB bulk copy
+// issued as soon as every thread is done with the previous frame's T (two CTAs
+// share an SM, so one computes while the other waits), the 64-row state sits
+// transposed in shared memory
+// (k-major), and each thread accumulates its 4 x D/16 tile with packed fp32 FMAs
+// (fma.rn.f32x2) on top of J_f.  Waits are bounded (2 s).
 template <int D>
 __global__ void __launch_bounds__(256) scan_kernel(const float* __restrict__ Tm,
                                                    const float* __restrict__ Jm,
                                                    const float* __restrict__ seed, int F, int H,
                                                    float* __restrict__ prefix,
-                                                   float* __restrict__ suffix) {
-  constexpr int R = 16, C = D / 16;
-  __shared__ float st[R][D];
+                                                   float* __restrict__ suffix,
+                                                   int* __restrict__ status) {
+  constexpr int R = 64, TC = D / 16;
+  extern __shared__ __align__(128) float sm[];
+  float* t_s = sm;                 // [D][D]  T_f
+  float* st_s = sm + D * D;        // [D][R]  state, transposed (k-major)
+  __shared__ __align__(8) uint64_t bar[1];
+  __shared__ int abort_flag;
   const int h = blockIdx.x, dir = blockIdx.y, rb = blockIdx.z;
-  const int r = threadIdx.x / 16, c0 = (threadIdx.x % 16) * C;
-  const int row = rb * R + r;
-  float cur[C];
-#pragma unroll
-  for (int j = 0; j < C; ++j) cur[j] = seed ? seed[((int64_t)h * D + row) * D + c0 + j] : 0.f;
+  const int tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
+  const int r0 = rg * 4, c0 = cg * TC;
+  const int row0 = rb * R + r0;
+  auto frame = [&](int step) { return dir == 0 ? step : F - 1 - step; };
+  auto issue = [&](int step) {
+    const int64_t base = ((int64_t)frame(step) * H + h) * D * D;
+    sm100::mbar_arrive_expect_tx(&bar[0], D * D * 4);
+    sm100::bulk_load(t_s, Tm + base, D * D * 4, &bar[0]);
+  };
+  if (tid == 0) {
+    sm100::mbar_init(&bar[0], 1);
+    abort_flag = 0;
+    sm100::fence_barrier_init();
+  }
+  for (int e = tid; e < R * D; e += 256) {
+    const int rr = e / D, kk = e % D;
+    st_s[kk * R + rr] = seed ? seed[((int64_t)h * D + rb * R + rr) * D + kk] : 0.f;
+  }
+  __syncthreads();
+  if (tid == 0) issue(0);
   float* bank = dir == 0 ? prefix : suffix;
+  float2 jn[4][TC / 2];
+  {
+    const int64_t base = ((int64_t)frame(0) * H + h) * D * D;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < TC / 2; ++j)
+        jn[i][j] = *reinterpret_cast<const float2*>(Jm + base + (int64_t)(row0 + i) * D + c0 + 2 * j);
+  }
   for (int step = 0; step < F; ++step) {
-    const int f = dir == 0 ? step : F - 1 - step;
-    __syncthreads();
+    const int64_t base = ((int64_t)frame(step) * H + h) * D * D;
+    float2 acc[4][TC / 2];
 #pragma unroll
-    for (int j = 0; j < C; ++j) st[r][c0 + j] = cur[j];
-    __syncthreads();
-    const int64_t base = ((int64_t)f * H + h) * D * D;
-    const float* tm = Tm + base;
-    float acc[C];
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < C; ++j) acc[j] = Jm[base + (int64_t)row * D + c0 + j];
-#pragma unroll 4
+      for (int j = 0; j < TC / 2; ++j) acc[i][j] = jn[i][j];
+    if (step + 1 < F) {  // J of the next frame, in flight during this step
+      const int64_t nb = ((int64_t)frame(step + 1) * H + h) * D * D;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < TC / 2; ++j)
+          jn[i][j] = *reinterpret_cast<const float2*>(Jm + nb + (int64_t)(row0 + i) * D + c0 + 2 * j);
+    }
+    if (!__syncthreads_and(sm100::mbar_wait(&bar[0], step & 1, &abort_flag))) break;
+    const float* tb = t_s;
+#pragma unroll 2
     for (int kk = 0; kk < D; ++kk) {
-      const float sv = st[r][kk];
-      const float* trow = tm + (int64_t)kk * D + c0;
+      const float4 sv = *reinterpret_cast<const float4*>(st_s + kk * R + r0);
+      const float svv[4] = {sv.x, sv.y, sv.z, sv.w};
+      float2 tv[TC / 2];
 #pragma unroll
-      for (int j = 0; j < C; ++j) acc[j] = fmaf(sv, __ldg(trow + j), acc[j]);
-    }
+      for (int j = 0; j < TC / 2; ++j) tv[j] = *reinterpret_cast<const float2*>(tb + kk * D + c0 + 2 * j);
 #pragma unroll
-    for (int j = 0; j < C; ++j) {
-      cur[j] = acc[j];
-      bank[base + (int64_t)row * D + c0 + j] = acc[j];
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < TC / 2; ++j) acc[i][j] = __ffma2_rn(make_float2(svv[i], svv[i]), tv[j], acc[i][j]);
     }
+    __syncthreads();  // every thread is done with T and st_s
+    if (tid == 0 && step + 1 < F) issue(step + 1);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < TC / 2; ++j) {
+        st_s[(c0 + 2 * j) * R + r0 + i] = acc[i][j].x;
+        st_s[(c0 + 2 * j + 1) * R + r0 + i] = acc[i][j].y;
+        *reinterpret_cast<float2*>(bank + base + (int64_t)(row0 + i) * D + c0 + 2 * j) = acc[i][j];
+      }
+    __syncthreads();
+  }
+  if (abort_flag) {  // let an issued copy land before the CTA exits
+    const uint64_t t0 = sm100::globaltimer();
+    while (!sm100::mbar_try_wait(&bar[0], 0) && !sm100::mbar_try_wait(&bar[0], 1) &&
+           sm100::globaltimer() - t0 < sm100::kWaitLimitNs) {
+    }
+    if (tid == 0 && status) atomicExch(status, VDN_ERR_TIMEOUT);
   }
 }
 
@@ -443,8 +507,8 @@ static int check_d(int d) {
 
 template <typename K>
 static int set_smem(K kernel, size_t bytes) {
-  if (bytes > 48 * 1024)
-    VDN_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  // Always raise the limit: static shared memory counts against the 48 KB default.
+  VDN_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
   return VDN_OK;
 }
 
@@ -495,7 +559,7 @@ int launch_factors(const float* A, const float* B, const float* alpha, int64_t n
   VDN_CHECK_ARG(A && B && T && J, "null pointer");
   VDN_CHECK_ARG(aligned16(A) && aligned16(B), "A and B must be 16-byte aligned");
   VDN_CHECK_ARG(n < (1ll << 31), "too many matrices");
-  const size_t smem = (4 * d + 2 * d * d) * sizeof(float);
+  const size_t smem = (4 * d + d * d) * sizeof(float);
   if (d == 128) {
     if (int rc = set_smem(factor_kernel<128>, smem)) return rc;
     factor_kernel<128><<<(unsigned)n, 256, smem, stream>>>(A, B, alpha, T, J);
@@ -512,9 +576,17 @@ int launch_scan(const float* T, const float* J, const float* seed, int F, int H,
   if (int rc = check_d(d)) return rc;
   VDN_CHECK_ARG(F >= 1 && H >= 1, "positive F and H required");
   VDN_CHECK_ARG(T && J && prefix && suffix, "null pointer");
-  const dim3 grid(H, 2, d / 16);
-  if (d == 128) scan_kernel<128><<<grid, 256, 0, stream>>>(T, J, seed, F, H, prefix, suffix);
-  else scan_kernel<64><<<grid, 256, 0, stream>>>(T, J, seed, F, H, prefix, suffix);
+  VDN_CHECK_ARG(aligned16(T) && aligned16(J) && aligned16(prefix) && aligned16(suffix),
+                "scan banks must be 16-byte aligned");
+  const dim3 grid(H, 2, d / 64);
+  const size_t smem = ((size_t)d * d + (size_t)d * 64) * sizeof(float);
+  if (d == 128) {
+    if (int rc = set_smem(scan_kernel<128>, smem)) return rc;
+    scan_kernel<128><<<grid, 256, smem, stream>>>(T, J, seed, F, H, prefix, suffix, nullptr);
+  } else {
+    if (int rc = set_smem(scan_kernel<64>, smem)) return rc;
+    scan_kernel<64><<<grid, 256, smem, stream>>>(T, J, seed, F, H, prefix, suffix, nullptr);
+  }
   VDN_LAUNCH_CHECK("vda scan");
   return VDN_OK;
 }

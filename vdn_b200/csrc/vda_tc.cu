@@ -33,178 +33,292 @@ __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t c) {
   return row * 128u + ((c ^ (row & 7u)) << 4);
 }
 
-__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+// x * sigmoid(x).  VDN_SILU selects the formulation (timed variants):
+//   0: __expf + __fdividef (two MUFU ops)
+//   1: ex2.approx + rcp.approx (two MUFU ops, no range handling)
+//   2: ex2.approx + magic-constant reciprocal and Newton steps (one MUFU op)
+#ifndef VDN_SILU
+#define VDN_SILU 0
+#endif
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float silu_fast(float x) {
+#if VDN_SILU == 0
+  return __fdividef(x, 1.0f + __expf(-x));
+#elif VDN_SILU == 1
+  return x * rcp_approx(1.0f + ex2_approx(fminf(-x, 80.0f) * 1.4426950408889634f));
+#else
+  const float y = 1.0f + ex2_approx(fminf(-x, 80.0f) * 1.4426950408889634f);
+  float r = __int_as_float(0x7EF311C3 - __float_as_int(y));
+#pragma unroll
+  for (int it = 0; it < 3; ++it) r = fmaf(r, fmaf(-y, r, 1.0f), r);
+  return x * r;
+#endif
+}
 
 // ------------------------------------------------------------------ statistics
+// Persistent, warp-specialised: grid = min(F*H, SMs), one CTA per SM walking
+// (frame, head) items.  Warp 0 lane 0 streams 32-token raw k / v chunks by TMA
+// into a 4-stage ring; warps 2-9 (8 threads per token) apply features and beta
+// and write kf / vb in place plus the khi / klo split; warp 1 lane 0 issues
+// A += khi.kf^T + klo.kf^T and B += vb.kf^T into one of two TMEM accumulator
+// pairs (512 columns); warps 10-13 drain an item's A (symmetrised through
+// shared memory) and B (bf16-rounded) while the next item streams.
 constexpr int ST_CH = 32;                       // tokens per chunk
-constexpr int ST_RAW_STAGES = 3;
+constexpr int ST_STAGES = 4;
 constexpr int ST_REGION = ST_CH * 128;          // 4 KB: 32 rows x 128 B
-constexpr int ST_RAW_BYTES = 4 * ST_REGION;     // k r0, k r1, v r0, v r1
-constexpr int ST_OP_BYTES = 8 * ST_REGION;      // kf, khi, klo, vb (2 regions each)
-constexpr int ST_OPS = 2;
-constexpr size_t ST_SMEM = 1024 + ST_RAW_STAGES * ST_RAW_BYTES + ST_OPS * ST_OP_BYTES + 128;
+constexpr int ST_STAGE_BYTES = 8 * ST_REGION;   // k(kf), v(vb), khi, klo: 2 regions each
+constexpr int ST_RAW_BYTES = 4 * ST_REGION;     // what TMA writes per stage
+constexpr int ST_THREADS = 448;
+constexpr int ST_TRANS_BYTES = 128 * 129 * 4;
+constexpr int ST_NBAR = 3 * ST_STAGES + 2 * 2 + 1;
+constexpr size_t ST_SMEM = 1024 + ST_STAGES * ST_STAGE_BYTES + ST_TRANS_BYTES + ST_NBAR * 8 + 64;
 
 struct StatsParams {
   const uint16_t* beta;
   int64_t b_sf, b_ss, b_sh;
   float* A;
   float* B;
-  int S, H;
+  int S, H, items;
   int* status;
 };
 
 template <bool FEATURES>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(ST_THREADS, 1)
     stats_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const StatsParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* raw = smem;
-  uint8_t* ops = raw + ST_RAW_STAGES * ST_RAW_BYTES;
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(ops + ST_OPS * ST_OP_BYTES);
-  uint64_t* mma_done = raw_full + ST_RAW_STAGES;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + ST_OPS);
+  uint8_t* stages = smem;
+  float* trans = reinterpret_cast<float*>(smem + ST_STAGES * ST_STAGE_BYTES);   // [128][129]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST_STAGES * ST_STAGE_BYTES + ST_TRANS_BYTES);
+  uint64_t* full = bars;
+  uint64_t* ready = full + ST_STAGES;
+  uint64_t* empty = ready + ST_STAGES;
+  uint64_t* acc_full = empty + ST_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_drain = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int fh = blockIdx.x, f = fh / p.H, h = fh % p.H;
   const int nch = (p.S + ST_CH - 1) / ST_CH;
 
   if (tid == 0) {
-    for (int s = 0; s < ST_RAW_STAGES; ++s) mbar_init(&raw_full[s], 1);
-    for (int s = 0; s < ST_OPS; ++s) mbar_init(&mma_done[s], 1);
+    for (int s = 0; s < ST_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 256);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0) tmem_alloc(tmem_holder, 256);
+  if (warp == 1) tmem_alloc(tmem_holder, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  auto issue_chunk = [&](int c) {
-    uint8_t* st = raw + (c % ST_RAW_STAGES) * ST_RAW_BYTES;
-    uint64_t* bar = &raw_full[c % ST_RAW_STAGES];
-    mbar_arrive_expect_tx(bar, ST_RAW_BYTES);
-    tma_load_4d(st, &tk, bar, 0, c * ST_CH, h, f);
-    tma_load_4d(st + ST_REGION, &tk, bar, 64, c * ST_CH, h, f);
-    tma_load_4d(st + 2 * ST_REGION, &tv, bar, 0, c * ST_CH, h, f);
-    tma_load_4d(st + 3 * ST_REGION, &tv, bar, 64, c * ST_CH, h, f);
-  };
-  if (tid == 0)
-    for (int c = 0; c < ST_RAW_STAGES && c < nch; ++c) issue_chunk(c);
-
-  // Thread -> (token row in the chunk, 16 consecutive d): region r, chunks cc, cc+1.
-  const uint32_t row = tid >> 3, e = tid & 7, r = e >> 2, cc = (e & 3) * 2;
-  constexpr uint32_t kIdesc = idesc_bf16(128, 128, 1, 1);
-  bool ok = true;
-  for (int c = 0; c < nch; ++c) {
-    const int rs = c % ST_RAW_STAGES, ob = c % ST_OPS;
-    ok = __syncthreads_and(ok ? mbar_wait(&raw_full[rs], (c / ST_RAW_STAGES) & 1, abort_flag) : 0);
-    if (!ok) break;
-    if (c >= ST_OPS) {
-      ok = __syncthreads_and(mbar_wait(&mma_done[ob], ((c - ST_OPS) / ST_OPS) & 1, abort_flag));
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int g = 0;
+      uint32_t pend = 0, pend_phase = 0;
+      for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
+        const int f = item / p.H, h = item % p.H;
+        for (int c = 0; c < nch; ++c, ++g) {
+          const int s = g % ST_STAGES;
+          const uint32_t ph = (g / ST_STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
+          uint8_t* st = stages + s * ST_STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], ST_RAW_BYTES);
+          tma_load_4d(st, &tk, &full[s], 0, c * ST_CH, h, f);
+          tma_load_4d(st + ST_REGION, &tk, &full[s], 64, c * ST_CH, h, f);
+          tma_load_4d(st + 2 * ST_REGION, &tv, &full[s], 0, c * ST_CH, h, f);
+          tma_load_4d(st + 3 * ST_REGION, &tv, &full[s], 64, c * ST_CH, h, f);
+          pend |= 1u << s;
+          pend_phase = (pend_phase & ~(1u << s)) | (ph << s);
+        }
+      }
+      if (*abort_flag) {
+        for (int s = 0; s < ST_STAGES; ++s) {
+          if (!(pend >> s & 1)) continue;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&full[s], (pend_phase >> s) & 1) && globaltimer() - t0 < kWaitLimitNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ----------------------------------------------------------------- MMA
+      constexpr uint32_t kIdesc = idesc_bf16(128, 128, 1, 1);
+      int g = 0, k = 0;
+      bool issued = false;
+      for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x, ++k) {
+        const int b = k & 1;
+        if (!mbar_wait(&acc_empty[b], ((k >> 1) & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t acc_a = tmem + b * 256, acc_b = acc_a + 128;
+        bool ok = true;
+        for (int c = 0; c < nch; ++c, ++g) {
+          const int s = g % ST_STAGES;
+          if (!mbar_wait(&ready[s], (g / ST_STAGES) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_u32(stages + s * ST_STAGE_BYTES);
+#pragma unroll
+          for (int ks = 0; ks < ST_CH / 16; ++ks) {
+            const uint32_t koff = ks * 16 * 128;  // 16 token rows
+            const uint64_t dkf = desc_mn_sw128(base + koff, ST_REGION);
+            const uint64_t dvb = desc_mn_sw128(base + 2 * ST_REGION + koff, ST_REGION);
+            const uint64_t dhi = desc_mn_sw128(base + 4 * ST_REGION + koff, ST_REGION);
+            const uint64_t dlo = desc_mn_sw128(base + 6 * ST_REGION + koff, ST_REGION);
+            const uint32_t acc = (c | ks) != 0;
+            mma_bf16(acc_a, dhi, dkf, kIdesc, acc);
+            mma_bf16(acc_a, dlo, dkf, kIdesc, 1);
+            mma_bf16(acc_b, dvb, dkf, kIdesc, acc);
+          }
+          issued = true;
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[b]);
+      }
+      if (*abort_flag && issued) {
+        tc_commit(mma_drain);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(mma_drain, 0) && globaltimer() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp < 10) {
+    // ----------------------------------------------------------- transform
+    const uint32_t t = tid - 64;                 // 0..255
+    const uint32_t row = t >> 3, e = t & 7, r = e >> 2, cc = (e & 3) * 2;
+    int g = 0;
+    for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
+      const int f = item / p.H, h = item % p.H;
+      auto load_beta = [&](int c) -> float {
+        const int s = c * ST_CH + (int)row;
+        return s < p.S ? bf16_bits_to_f32(p.beta[(int64_t)f * p.b_sf + (int64_t)s * p.b_ss + (int64_t)h * p.b_sh])
+                       : 0.f;
+      };
+      float bt_next = load_beta(0);
+      bool ok = true;
+      for (int c = 0; c < nch; ++c, ++g) {
+        const int s = g % ST_STAGES;
+        const float bt = bt_next;
+        if (c + 1 < nch) bt_next = load_beta(c + 1);
+        if (!mbar_wait(&full[s], (g / ST_STAGES) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = stages + s * ST_STAGE_BYTES;
+        float kv[16], vv[16];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const uint32_t off = r * ST_REGION + swz(row, cc + j);
+          unpack8(*reinterpret_cast<const uint4*>(st + off), kv + 8 * j);
+          unpack8(*reinterpret_cast<const uint4*>(st + 2 * ST_REGION + off), vv + 8 * j);
+        }
+        if (FEATURES) {
+          float ss = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            kv[i] = silu_fast(kv[i]);
+            kv[i + 1] = silu_fast(kv[i + 1]);
+            round_bf16_pair(kv[i], kv[i + 1]);
+            ss = fmaf(kv[i], kv[i], ss);
+            ss = fmaf(kv[i + 1], kv[i + 1], ss);
+            vv[i] = silu_fast(vv[i]);
+            vv[i + 1] = silu_fast(vv[i + 1]);
+            round_bf16_pair(vv[i], vv[i + 1]);
+          }
+          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+          ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+          const float nrm = fmaxf(round_bf16(sqrtf(ss)), round_bf16(1e-6f));
+          const float inv = __fdiv_rn(1.0f, nrm);
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            kv[i] *= inv;
+            kv[i + 1] *= inv;
+            round_bf16_pair(kv[i], kv[i + 1]);
+          }
+        }
+        // kf * beta is exact in fp32 (two bf16 factors, 16 significant bits); its
+        // bf16 rounding hi leaves a residual that is itself exactly a bf16 value.
+        uint32_t hi2[8], lo2[8], vb2[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float p0 = kv[i] * bt, p1 = kv[i + 1] * bt;
+          float h0 = p0, h1 = p1;
+          round_bf16_pair(h0, h1);
+          hi2[i / 2] = pack_exact2(h0, h1);
+          lo2[i / 2] = pack_exact2(p0 - h0, p1 - h1);
+          vb2[i / 2] = pack_bf16x2(vv[i] * bt, vv[i + 1] * bt);
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const uint32_t off = r * ST_REGION + swz(row, cc + j);
+          *reinterpret_cast<uint4*>(st + off) = pack_exact8(kv + 8 * j);
+          *reinterpret_cast<uint4*>(st + 2 * ST_REGION + off) =
+              make_uint4(vb2[4 * j], vb2[4 * j + 1], vb2[4 * j + 2], vb2[4 * j + 3]);
+          *reinterpret_cast<uint4*>(st + 4 * ST_REGION + off) =
+              make_uint4(hi2[4 * j], hi2[4 * j + 1], hi2[4 * j + 2], hi2[4 * j + 3]);
+          *reinterpret_cast<uint4*>(st + 6 * ST_REGION + off) =
+              make_uint4(lo2[4 * j], lo2[4 * j + 1], lo2[4 * j + 2], lo2[4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&ready[s]);
+      }
       if (!ok) break;
     }
-    const uint8_t* st = raw + rs * ST_RAW_BYTES;
-    uint8_t* op = ops + ob * ST_OP_BYTES;
-    const int s = c * ST_CH + (int)row;
-    float bt = 0.f;
-    if (s < p.S) bt = bf16_bits_to_f32(p.beta[(int64_t)f * p.b_sf + (int64_t)s * p.b_ss + (int64_t)h * p.b_sh]);
-    float kv[16], vv[16];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t off = r * ST_REGION + swz(row, cc + j);
-      unpack8(*reinterpret_cast<const uint4*>(st + off), kv + 8 * j);
-      unpack8(*reinterpret_cast<const uint4*>(st + 2 * ST_REGION + off), vv + 8 * j);
-    }
-    if (FEATURES) {
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        kv[i] = round_bf16(silu_fast(kv[i]));
-        ss = fmaf(kv[i], kv[i], ss);
-        vv[i] = round_bf16(silu_fast(vv[i]));
-      }
-      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-      ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-      const float nrm = fmaxf(round_bf16(sqrtf(ss)), round_bf16(1e-6f));
-      const float inv = __fdiv_rn(1.0f, nrm);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) kv[i] = round_bf16(kv[i] * inv);
-    }
-    float hi[16], lo[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float prod = kv[i] * bt;  // exact: two bf16 factors
-      hi[i] = round_bf16(prod);
-      lo[i] = round_bf16(prod - hi[i]);
-      vv[i] = round_bf16(vv[i] * bt);
-    }
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t off = r * ST_REGION + swz(row, cc + j);
-      *reinterpret_cast<uint4*>(op + off) = pack8(kv + 8 * j);
-      *reinterpret_cast<uint4*>(op + 2 * ST_REGION + off) = pack8(hi + 8 * j);
-      *reinterpret_cast<uint4*>(op + 4 * ST_REGION + off) = pack8(lo + 8 * j);
-      *reinterpret_cast<uint4*>(op + 6 * ST_REGION + off) = pack8(vv + 8 * j);
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0) {
-      if (c + ST_RAW_STAGES < nch) issue_chunk(c + ST_RAW_STAGES);  // raw stage rs is consumed
-      const uint32_t base = smem_u32(op);
-#pragma unroll
-      for (int ks = 0; ks < ST_CH / 16; ++ks) {
-        const uint32_t koff = ks * 16 * 128;  // 16 token rows
-        const uint64_t dkf = desc_mn_sw128(base + koff, ST_REGION);
-        const uint64_t dhi = desc_mn_sw128(base + 2 * ST_REGION + koff, ST_REGION);
-        const uint64_t dlo = desc_mn_sw128(base + 4 * ST_REGION + koff, ST_REGION);
-        const uint64_t dvb = desc_mn_sw128(base + 6 * ST_REGION + koff, ST_REGION);
-        const uint32_t acc = (c | ks) != 0;
-        mma_bf16(tmem, dhi, dkf, kIdesc, acc);
-        mma_bf16(tmem, dlo, dkf, kIdesc, 1);
-        mma_bf16(tmem + 128, dvb, dkf, kIdesc, acc);
-      }
-      tc_commit(&mma_done[ob]);
-    }
-  }
-  // Wait for the last chunk's MMAs (they cover every earlier one).
-  if (ok && nch > 0) {
-    const int last = nch - 1;
-    ok = __syncthreads_and(mbar_wait(&mma_done[last % ST_OPS], (last / ST_OPS) & 1, abort_flag));
-  }
-  tc_fence_after();
-  if (ok) {
-    // Epilogue: warps 0-3 hold A rows (lane quadrant = warp), warps 4-7 B rows.
-    float* trans = reinterpret_cast<float*>(smem);  // [128][129], reuses the rings
-    const int quad = warp & 3;
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;                   // warps 10..13 -> quadrants 2,3,0,1
     const int mrow = quad * 32 + lane;
-    const bool is_a = warp < 4;
-    const uint32_t col0 = is_a ? 0 : 128;
-    float* b_out = p.B + ((int64_t)fh * 128 + mrow) * 128;
+    int k = 0;
+    for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x, ++k) {
+      const int b = k & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (k >> 1) & 1, abort_flag))) break;
+      tc_fence_after();
+      const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + b * 256;
+      float* b_out = p.B + ((int64_t)item * 128 + mrow) * 128;
 #pragma unroll 1
-    for (int cb = 0; cb < 4; ++cb) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(tmem + ((uint32_t)(quad * 32) << 16) + col0 + cb * 32, v);
-      tmem_ld_wait();
-      if (is_a) {
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t va[32], vb[32];
+        tmem_ld_32x32b_x32(lane_base + cb * 32, va);
+        tmem_ld_32x32b_x32(lane_base + 128 + cb * 32, vb);
+        tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) trans[mrow * 129 + cb * 32 + i] = __uint_as_float(v[i]);
-      } else {
+        for (int i = 0; i < 32; ++i) trans[mrow * 129 + cb * 32 + i] = __uint_as_float(va[i]);
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
           *reinterpret_cast<float4*>(b_out + cb * 32 + i) =
-              make_float4(round_bf16(__uint_as_float(v[i])), round_bf16(__uint_as_float(v[i + 1])),
-                          round_bf16(__uint_as_float(v[i + 2])), round_bf16(__uint_as_float(v[i + 3])));
+              make_float4(round_bf16(__uint_as_float(vb[i])), round_bf16(__uint_as_float(vb[i + 1])),
+                          round_bf16(__uint_as_float(vb[i + 2])), round_bf16(__uint_as_float(vb[i + 3])));
       }
-    }
-    __syncthreads();
-    if (is_a) {
-      float* a_out = p.A + ((int64_t)fh * 128 + mrow) * 128;
+      tc_fence_before();
+      mbar_arrive(&acc_empty[b]);                 // TMEM pair b may be refilled
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      float* a_out = p.A + ((int64_t)item * 128 + mrow) * 128;
 #pragma unroll 4
       for (int cidx = 0; cidx < 128; cidx += 4) {
         float4 o;
@@ -214,25 +328,33 @@ __global__ void __launch_bounds__(256, 2)
         o.w = 0.5f * (trans[mrow * 129 + cidx + 3] + trans[(cidx + 3) * 129 + mrow]);
         *reinterpret_cast<float4*>(a_out + cidx) = o;
       }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // trans is free for the next item
     }
-  } else {
-    __syncthreads();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) {
+  if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
   if (tid == 0 && *abort_flag && p.status) atomicExch(p.status, VDN_ERR_TIMEOUT);
 }
 
 // --------------------------------------------------------------------- readout
+// Persistent, warp-specialised: grid = min(F*H, SMs), one CTA per SM walking
+// (frame, head) items.  Warp 0 lane 0 streams the item's bf16 state (double
+// buffered) and its 128-token q tiles (4-stage ring) by TMA; warps 2-5 turn
+// their tile row into features in place; warp 1 lane 0 issues q.state^T into
+// one of two TMEM accumulators; warps 6-9 drain them (thread = TMEM lane =
+// token): bf16 readout, RMSNorm over the row, * w, * gate, token-major store.
+// Hand-offs are mbarriers; every wait is bounded.
 constexpr int RO_TOK = 128;
-constexpr int RO_STAGES = 2;
+constexpr int RO_STAGES = 4;
+constexpr int RO_THREADS = 320;
 constexpr int RO_TILE = 2 * RO_TOK * 128;       // 2 regions x 128 rows x 128 B = 32 KB
-constexpr size_t RO_SMEM = 1024 + RO_TILE + RO_STAGES * RO_TILE + 128 * 4 + 128;
+constexpr int RO_NBAR = 3 * RO_STAGES + 2 * 2 + 2 * 2 + 1;
+constexpr size_t RO_SMEM = 1024 + 2 * RO_TILE + RO_STAGES * RO_TILE + 128 * 4 + RO_NBAR * 8 + 64;
 
 struct ReadoutParams {
   const uint16_t* gate;
@@ -240,170 +362,256 @@ struct ReadoutParams {
   const float* norm_w;
   float eps;
   uint16_t* out;
-  int S, H;
+  int S, H, items;
   int* status;
 };
 
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(RO_THREADS, 1)
     readout_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tstate,
                       const ReadoutParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* st_s = smem;
-  uint8_t* q_s = smem + RO_TILE;
+  uint8_t* st_s = smem;                           // 2 state buffers
+  uint8_t* q_s = smem + 2 * RO_TILE;              // RO_STAGES q tiles
   float* w_s = reinterpret_cast<float*>(q_s + RO_STAGES * RO_TILE);
-  uint64_t* state_full = reinterpret_cast<uint64_t*>(w_s + 128);
-  uint64_t* q_full = state_full + 1;
-  uint64_t* mma_done = q_full + RO_STAGES;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 2);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(w_s + 128);
+  uint64_t* q_full = bars;
+  uint64_t* q_ready = q_full + RO_STAGES;
+  uint64_t* q_empty = q_ready + RO_STAGES;
+  uint64_t* acc_full = q_empty + RO_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* st_full = acc_empty + 2;
+  uint64_t* st_empty = st_full + 2;
+  uint64_t* mma_drain = st_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int fh = blockIdx.x, f = fh / p.H, h = fh % p.H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nt = (p.S + RO_TOK - 1) / RO_TOK;
 
   if (tid == 0) {
-    mbar_init(state_full, 1);
-    for (int s = 0; s < RO_STAGES; ++s) mbar_init(&q_full[s], 1);
-    mbar_init(&mma_done[0], 1);
-    mbar_init(&mma_done[1], 1);
+    for (int s = 0; s < RO_STAGES; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_ready[s], 128);
+      mbar_init(&q_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+      mbar_init(&st_full[b], 1);
+      mbar_init(&st_empty[b], 1);
+    }
+    mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  w_s[tid] = round_bf16(p.norm_w[tid]);
-  if (warp == 0) tmem_alloc(tmem_holder, 256);
+  if (tid < 128) w_s[tid] = round_bf16(p.norm_w[tid]);
+  if (warp == 1) tmem_alloc(tmem_holder, 256);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  auto issue_tile = [&](int i) {
-    uint8_t* dst = q_s + (i % RO_STAGES) * RO_TILE;
-    uint64_t* bar = &q_full[i % RO_STAGES];
-    mbar_arrive_expect_tx(bar, RO_TILE);
-    tma_load_4d(dst, &tq, bar, 0, i * RO_TOK, h, f);
-    tma_load_4d(dst + RO_TILE / 2, &tq, bar, 64, i * RO_TOK, h, f);
-  };
-  if (tid == 0) {
-    mbar_arrive_expect_tx(state_full, RO_TILE);
-    tma_load_2d(st_s, &tstate, state_full, 0, fh * 128);
-    tma_load_2d(st_s + RO_TILE / 2, &tstate, state_full, 64, fh * 128);
-    for (int i = 0; i < RO_STAGES && i < nt; ++i) issue_tile(i);
-  }
-  constexpr uint32_t kIdesc = idesc_bf16(128, 128, 0, 0);
-  const uint32_t t = tid;
-  bool ok = true;
-
-  auto epilogue = [&](int j) -> bool {
-    const int b = j & 1;
-    if (!__syncthreads_and(mbar_wait(&mma_done[b], (j >> 1) & 1, abort_flag))) return false;
-    tc_fence_after();
-    if (tid == 0 && j + RO_STAGES < nt) issue_tile(j + RO_STAGES);  // its q stage is free now
-    const int s = j * RO_TOK + (int)t;
-    const bool valid = s < p.S;
-    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + b * 128;
-    float ss = 0.f;
-#pragma unroll 1
-    for (int cb = 0; cb < 4; ++cb) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(taddr + cb * 32, v);
-      tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float x = round_bf16(__uint_as_float(v[i]));
-        ss = fmaf(x, x, ss);
-      }
-    }
-    const float nrm = sqrtf(ss);
-    const float inv = round_bf16(__fdiv_rn(1.0f, sqrtf(nrm * nrm / 128.0f + p.eps)));
-    const uint16_t* grow = p.gate + (int64_t)f * p.g_sf + (int64_t)s * p.g_ss + (int64_t)h * p.g_sh;
-    uint16_t* orow = p.out + ((int64_t)f * p.S + s) * ((int64_t)p.H * 128) + (int64_t)h * 128;
-#pragma unroll 1
-    for (int cb = 0; cb < 4; ++cb) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(taddr + cb * 32, v);
-      tmem_ld_wait();
-      if (!valid) continue;
-      float g[32], y[32];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) unpack8(*reinterpret_cast<const uint4*>(grow + cb * 32 + 8 * i), g + 8 * i);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float rr = round_bf16(__uint_as_float(v[i]));
-        const float yy = round_bf16(round_bf16(rr * inv) * w_s[cb * 32 + i]);
-        y[i] = yy * g[i];
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(orow + cb * 32 + 8 * i) = pack8(y + 8 * i);
-    }
-    tc_fence_before();
-    return true;
-  };
-
-  for (int i = 0; i < nt && ok; ++i) {
-    const int qs = i % RO_STAGES;
-    ok = __syncthreads_and(mbar_wait(&q_full[qs], (i / RO_STAGES) & 1, abort_flag));
-    if (!ok) break;
-    // Row t of the tile -> features in place (SiLU, L2 over d, eager rounding).
-    uint8_t* tile = q_s + qs * RO_TILE;
-    uint32_t packed[64];
-    float ssum = 0.f;
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const uint32_t off = (c >> 3) * (RO_TILE / 2) + swz(t, c & 7);
-      float x[8];
-      unpack8(*reinterpret_cast<const uint4*>(tile + off), x);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        x[k] = round_bf16(silu_fast(x[k]));
-        ssum = fmaf(x[k], x[k], ssum);
-      }
-      const uint4 pk = pack8(x);
-      packed[4 * c] = pk.x;
-      packed[4 * c + 1] = pk.y;
-      packed[4 * c + 2] = pk.z;
-      packed[4 * c + 3] = pk.w;
-    }
-    const float nrm = fmaxf(round_bf16(sqrtf(ssum)), round_bf16(1e-6f));
-    const float inv = __fdiv_rn(1.0f, nrm);
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      float x[8];
-      unpack8(make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]), x);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = round_bf16(x[k] * inv);
-      const uint32_t off = (c >> 3) * (RO_TILE / 2) + swz(t, c & 7);
-      *reinterpret_cast<uint4*>(tile + off) = pack8(x);
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0) {
-      if (i == 0 && !mbar_wait(state_full, 0, abort_flag)) {
-        ok = false;
-      } else {
-        const uint32_t qa = smem_u32(tile), sb = smem_u32(st_s);
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t off = (ks >> 2) * (RO_TILE / 2) + (ks & 3) * 32;
-          mma_bf16(tmem + (i & 1) * 128, desc_k_sw128(qa + off), desc_k_sw128(sb + off), kIdesc, ks > 0);
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int g = 0, k = 0;
+      uint32_t pend = 0, pend_phase = 0;
+      for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x, ++k) {
+        const int f = item / p.H, h = item % p.H, sb = k & 1;
+        if (!mbar_wait(&st_empty[sb], ((k >> 1) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&st_full[sb], RO_TILE);
+        tma_load_2d(st_s + sb * RO_TILE, &tstate, &st_full[sb], 0, item * 128);
+        tma_load_2d(st_s + sb * RO_TILE + RO_TILE / 2, &tstate, &st_full[sb], 64, item * 128);
+        for (int i = 0; i < nt; ++i, ++g) {
+          const int s = g % RO_STAGES;
+          const uint32_t ph = (g / RO_STAGES) & 1;
+          if (!mbar_wait(&q_empty[s], ph ^ 1, abort_flag)) break;
+          uint8_t* dst = q_s + s * RO_TILE;
+          mbar_arrive_expect_tx(&q_full[s], RO_TILE);
+          tma_load_4d(dst, &tq, &q_full[s], 0, i * RO_TOK, h, f);
+          tma_load_4d(dst + RO_TILE / 2, &tq, &q_full[s], 64, i * RO_TOK, h, f);
+          pend |= 1u << s;
+          pend_phase = (pend_phase & ~(1u << s)) | (ph << s);
         }
-        tc_commit(&mma_done[i & 1]);
+      }
+      if (*abort_flag) {  // let every issued copy land before the CTA may exit
+        for (int s = 0; s < RO_STAGES; ++s) {
+          if (!(pend >> s & 1)) continue;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&q_full[s], (pend_phase >> s) & 1) && globaltimer() - t0 < kWaitLimitNs) {
+          }
+        }
+        for (int b = 0; b < 2 && k > b; ++b) {
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&st_full[(k - 1 - b) & 1], (((k - 1 - b) >> 1) & 1)) &&
+                 globaltimer() - t0 < kWaitLimitNs) {
+          }
+        }
       }
     }
-    ok = __syncthreads_and(ok && !*abort_flag);
-    if (!ok) break;
-    if (i >= 1 && !epilogue(i - 1)) {
-      ok = false;
-      break;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ----------------------------------------------------------------- MMA
+      constexpr uint32_t kIdesc = idesc_bf16(128, 128, 0, 0);
+      int g = 0, k = 0;
+      bool issued = false;
+      for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x, ++k) {
+        const int sb = k & 1;
+        if (!mbar_wait(&st_full[sb], (k >> 1) & 1, abort_flag)) break;
+        const uint32_t sbase = smem_u32(st_s + sb * RO_TILE);
+        bool ok = true;
+        for (int i = 0; i < nt; ++i, ++g) {
+          const int s = g % RO_STAGES, b = g & 1;
+          if (!mbar_wait(&q_ready[s], (g / RO_STAGES) & 1, abort_flag) ||
+              !mbar_wait(&acc_empty[b], ((g >> 1) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t qa = smem_u32(q_s + s * RO_TILE);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t off = (ks >> 2) * (RO_TILE / 2) + (ks & 3) * 32;
+            mma_bf16(tmem + b * 128, desc_k_sw128(qa + off), desc_k_sw128(sbase + off), kIdesc, ks > 0);
+          }
+          issued = true;
+          tc_commit(&q_empty[s]);
+          tc_commit(&acc_full[b]);
+        }
+        if (!ok) break;
+        tc_commit(&st_empty[sb]);
+      }
+      if (*abort_flag && issued) {
+        // The MMAs already issued must finish before TMEM is freed.
+        tc_commit(mma_drain);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(mma_drain, 0) && globaltimer() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp < 6) {
+    // ----------------------------------------------------------- transform
+    const uint32_t row = tid - 64;               // 0..127
+    int g = 0;
+    for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
+      bool ok = true;
+      for (int i = 0; i < nt; ++i, ++g) {
+        const int s = g % RO_STAGES;
+        if (!mbar_wait(&q_full[s], (g / RO_STAGES) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t* tile = q_s + s * RO_TILE;
+        // Pass 1: bf16(silu) written back in place, sum of squares; pass 2: / norm.
+        float ssum = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < 16; ++c) {
+          uint4* ptr = reinterpret_cast<uint4*>(tile + (c >> 3) * (RO_TILE / 2) + swz(row, c & 7));
+          float x[8];
+          unpack8(*ptr, x);
+#pragma unroll
+          for (int kk = 0; kk < 8; kk += 2) {
+            x[kk] = silu_fast(x[kk]);
+            x[kk + 1] = silu_fast(x[kk + 1]);
+            round_bf16_pair(x[kk], x[kk + 1]);
+            ssum = fmaf(x[kk], x[kk], ssum);
+            ssum = fmaf(x[kk + 1], x[kk + 1], ssum);
+          }
+          *ptr = pack_exact8(x);
+        }
+        const float nrm = fmaxf(round_bf16(sqrtf(ssum)), round_bf16(1e-6f));
+        const float inv = __fdiv_rn(1.0f, nrm);
+#pragma unroll 4
+        for (int c = 0; c < 16; ++c) {
+          uint4* ptr = reinterpret_cast<uint4*>(tile + (c >> 3) * (RO_TILE / 2) + swz(row, c & 7));
+          float x[8];
+          unpack8(*ptr, x);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) x[kk] *= inv;
+          *ptr = pack8(x);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&q_ready[s]);
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;                   // warps 6,7,8,9 -> lane quadrants 2,3,0,1
+    const uint32_t erow = quad * 32 + lane;
+    int g = 0;
+    for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
+      const int f = item / p.H, h = item % p.H;
+      bool ok = true;
+      for (int i = 0; i < nt; ++i, ++g) {
+        const int b = g & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (g >> 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int s = i * RO_TOK + (int)erow;
+        const bool valid = s < p.S;
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + b * 128;
+        float ss = 0.f;
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + cb * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
+            round_bf16_pair(x0, x1);
+            ss = fmaf(x0, x0, ss);
+            ss = fmaf(x1, x1, ss);
+          }
+        }
+        const float nrm = sqrtf(ss);
+        const float inv = round_bf16(__fdiv_rn(1.0f, sqrtf(nrm * nrm / 128.0f + p.eps)));
+        const uint16_t* grow = p.gate + (int64_t)f * p.g_sf + (int64_t)s * p.g_ss + (int64_t)h * p.g_sh;
+        uint16_t* orow = p.out + ((int64_t)f * p.S + s) * ((int64_t)p.H * 128) + (int64_t)h * 128;
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + cb * 32, v);
+          uint4 gv[4];
+          if (valid) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) gv[e] = *reinterpret_cast<const uint4*>(grow + cb * 32 + 8 * e);
+          }
+          tmem_ld_wait();
+          if (!valid) continue;
+          float gf[32], y[32];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) unpack8(gv[e], gf + 8 * e);
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float r0 = __uint_as_float(v[e]), r1 = __uint_as_float(v[e + 1]);
+            round_bf16_pair(r0, r1);
+            r0 *= inv;
+            r1 *= inv;
+            round_bf16_pair(r0, r1);
+            r0 *= w_s[cb * 32 + e];
+            r1 *= w_s[cb * 32 + e + 1];
+            round_bf16_pair(r0, r1);
+            y[e] = r0 * gf[e];
+            y[e + 1] = r1 * gf[e + 1];
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) *reinterpret_cast<uint4*>(orow + cb * 32 + 8 * e) = pack8(y + 8 * e);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[b]);
+      }
+      if (!ok) break;
     }
   }
-  if (ok && nt > 0) epilogue(nt - 1);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) {
+  if (warp == 1) {
     __syncwarp();
     tmem_dealloc(tmem, 256);
   }
@@ -441,20 +649,24 @@ int launch_stats_tc(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, con
   CUtensorMap mk, mv;
   if (int rc = map_tokens(&mk, k, k_sf, k_ss, k_sh, F, S, H, ST_CH)) return rc;
   if (int rc = map_tokens(&mv, v, v_sf, v_ss, v_sh, F, S, H, ST_CH)) return rc;
-  StatsParams p{static_cast<const uint16_t*>(beta), b_sf, b_ss, b_sh, A, B, S, H, status};
+  StatsParams p{static_cast<const uint16_t*>(beta), b_sf, b_ss, b_sh, A, B, S, H, F * H, status};
+  int dev = 0, sms = 148;
+  VDN_CUDA_TRY(cudaGetDevice(&dev));
+  VDN_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int grid = F * H < sms ? F * H : sms;
   static bool attr_set[2] = {false, false};
   if (features_applied) {
     if (!attr_set[0]) {
       VDN_CUDA_TRY(cudaFuncSetAttribute(stats_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ST_SMEM));
       attr_set[0] = true;
     }
-    stats_tc_kernel<false><<<F * H, 256, ST_SMEM, stream>>>(mk, mv, p);
+    stats_tc_kernel<false><<<grid, ST_THREADS, ST_SMEM, stream>>>(mk, mv, p);
   } else {
     if (!attr_set[1]) {
       VDN_CUDA_TRY(cudaFuncSetAttribute(stats_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ST_SMEM));
       attr_set[1] = true;
     }
-    stats_tc_kernel<true><<<F * H, 256, ST_SMEM, stream>>>(mk, mv, p);
+    stats_tc_kernel<true><<<grid, ST_THREADS, ST_SMEM, stream>>>(mk, mv, p);
   }
   VDN_LAUNCH_CHECK("vda statistics (tcgen05)");
   return VDN_OK;
@@ -477,13 +689,17 @@ int launch_readout_tc(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, c
   cuuint32_t box[2] = {64, 128};
   if (int rc = encode_map(&ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, state, dims, strides, box)) return rc;
   ReadoutParams p{static_cast<const uint16_t*>(gate), g_sf, g_ss, g_sh, norm_w, eps,
-                  static_cast<uint16_t*>(out), S, H, status};
+                  static_cast<uint16_t*>(out), S, H, F * H, status};
   static bool attr_set = false;
   if (!attr_set) {
     VDN_CUDA_TRY(cudaFuncSetAttribute(readout_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RO_SMEM));
     attr_set = true;
   }
-  readout_tc_kernel<<<F * H, 128, RO_SMEM, stream>>>(mq, ms, p);
+  int dev = 0, sms = 148;
+  VDN_CUDA_TRY(cudaGetDevice(&dev));
+  VDN_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int grid = F * H < sms ? F * H : sms;
+  readout_tc_kernel<<<grid, RO_THREADS, RO_SMEM, stream>>>(mq, ms, p);
   VDN_LAUNCH_CHECK("vda readout (tcgen05)");
   return VDN_OK;
 }

@@ -1,0 +1,200 @@
+"""Ulysses sequence parallelism: sequence <-> head all-to-all over NCCL.
+
+Mirrors ec-jt/vdn src/inference/utils/ulysses_runtime.py (sequence_splits,
+balanced_splits, UlyssesRuntime.configure / sequence_to_heads /
+heads_to_sequence / gather_sequence / video_frame_mean_async, init_ulysses)
+for the standard (head-sharded) exchange.  One process per GPU; the exchange is
+one torch.distributed all_to_all_single per direction on the NCCL process
+group (NVLink / NVSwitch inside a node).  Exact routing: every row / head
+arrives where the reference sends it.  Timeouts are short by default so that a
+rank that never joins ends the others' next collective with an error.
+"""
+from __future__ import annotations
+
+import math
+import os
+from dataclasses import dataclass, field
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+__all__ = ["sequence_splits", "balanced_splits", "UlyssesRuntime", "init_ulysses"]
+
+
+def sequence_splits(sequence_length: int, world_size: int) -> tuple[int, ...]:
+    """Contiguous shards: ceil(S/P) rows on ranks 0..P-2, the remainder last (ulysses_runtime.py:26-46)."""
+    if sequence_length <= 0 or world_size <= 0:
+        raise ValueError("sequence_length and world_size must be positive")
+    if world_size == 1:
+        return (sequence_length,)
+    chunk = math.ceil(sequence_length / world_size)
+    last = sequence_length - chunk * (world_size - 1)
+    if last <= 0:
+        base, extra = divmod(sequence_length, world_size)
+        return tuple(base + (rank < extra) for rank in range(world_size))
+    return (chunk,) * (world_size - 1) + (last,)
+
+
+def balanced_splits(total: int, parts: int) -> tuple[int, ...]:
+    """Contiguous split with imbalance at most one (ulysses_runtime.py:49-59)."""
+    if total <= 0 or parts <= 0 or parts > total:
+        raise ValueError(f"need 0 < parts <= total; got total={total}, parts={parts}")
+    base, extra = divmod(total, parts)
+    return tuple(base + (rank < extra) for rank in range(parts))
+
+
+@dataclass
+class UlyssesRuntime:
+    rank: int
+    world_size: int
+    local_rank: int
+    device: torch.device
+    backend: str
+    group: object | None = None
+    sequence_length: int = 0
+    splits: tuple[int, ...] = ()
+    local_start: int = 0
+    local_end: int = 0
+    heads_per_rank: int = 0
+    num_heads: int = 0
+    profile_enabled: bool = False
+    profile_events: dict = field(default_factory=dict)
+
+    @property
+    def is_main(self) -> bool:
+        return self.rank == 0
+
+    def barrier(self) -> None:
+        dist.barrier(group=self.group)
+
+    def configure(self, sequence_length: int, num_heads: int) -> None:
+        if num_heads % self.world_size:
+            raise ValueError(f"Ulysses needs num_heads divisible by world_size; got "
+                             f"{num_heads} heads on {self.world_size} ranks")
+        splits = sequence_splits(sequence_length, self.world_size)
+        if any(size <= 0 for size in splits):
+            raise ValueError(f"Ulysses requires at least one row per rank; S={sequence_length}, "
+                             f"P={self.world_size}")
+        if self.sequence_length and self.sequence_length != sequence_length:
+            raise RuntimeError("one Ulysses process supports one packed sequence geometry; "
+                               f"already configured for {self.sequence_length}, got {sequence_length}")
+        self.sequence_length = sequence_length
+        self.splits = splits
+        self.local_start = sum(splits[: self.rank])
+        self.local_end = self.local_start + splits[self.rank]
+        self.num_heads = num_heads
+        self.heads_per_rank = num_heads // self.world_size
+
+    def profile_start(self):
+        if not self.profile_enabled:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def profile_end(self, name, start):
+        if start is None:
+            return
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.profile_events.setdefault(name, []).append((start, e))
+
+    def profile_milliseconds(self):
+        torch.cuda.synchronize(self.device)
+        return {k: sum(a.elapsed_time(b) for a, b in v) for k, v in self.profile_events.items()}
+
+    def sequence_to_heads(self, tensor: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """[S_rank, H, W] -> [S, H/P, W] (ulysses_runtime.py:451-519)."""
+        local_rows, heads, width = tensor.shape
+        if local_rows != self.splits[self.rank]:
+            raise ValueError(f"local rows {local_rows} != configured {self.splits[self.rank]}")
+        if heads != self.heads_per_rank * self.world_size:
+            raise ValueError(f"heads {heads} != {self.heads_per_rank * self.world_size}")
+        send = (tensor.view(local_rows, self.world_size, self.heads_per_rank, width)
+                .permute(1, 0, 2, 3).contiguous().view(-1))
+        unit = self.heads_per_rank * width
+        recv = out if out is not None else tensor.new_empty(self.sequence_length * unit)
+        dist.all_to_all_single(recv.view(-1), send,
+                               output_split_sizes=[rows * unit for rows in self.splits],
+                               input_split_sizes=[local_rows * unit] * self.world_size,
+                               group=self.group)
+        return recv.view(self.sequence_length, self.heads_per_rank, width)
+
+    def heads_to_sequence(self, tensor: torch.Tensor) -> torch.Tensor:
+        """[S, H/P, W] -> [S_rank, H, W] (ulysses_runtime.py:522-582)."""
+        sequence_length, local_heads, width = tensor.shape
+        if sequence_length != self.sequence_length or local_heads != self.heads_per_rank:
+            raise ValueError(f"head shard has {tuple(tensor.shape[:2])}, expected "
+                             f"({self.sequence_length}, {self.heads_per_rank})")
+        unit = self.heads_per_rank * width
+        local_rows = self.splits[self.rank]
+        recv = tensor.new_empty(local_rows * unit * self.world_size)
+        dist.all_to_all_single(recv, tensor.contiguous().view(-1),
+                               output_split_sizes=[local_rows * unit] * self.world_size,
+                               input_split_sizes=[rows * unit for rows in self.splits],
+                               group=self.group)
+        return (recv.view(self.world_size, local_rows, self.heads_per_rank, width)
+                .permute(1, 0, 2, 3).contiguous()
+                .view(local_rows, self.heads_per_rank * self.world_size, width))
+
+    def gather_sequence(self, tensor: torch.Tensor) -> torch.Tensor:
+        """All-gather a sequence shard, padding confined to the last rank (ulysses_runtime.py:585-603)."""
+        local_rows = tensor.shape[0]
+        max_rows = max(self.splits)
+        padded = tensor
+        if local_rows < max_rows:
+            padded = tensor.new_zeros((max_rows, *tensor.shape[1:]))
+            padded[:local_rows].copy_(tensor)
+        gathered = tensor.new_empty((self.world_size * max_rows, *tensor.shape[1:]))
+        dist.all_gather_into_tensor(gathered, padded.contiguous(), group=self.group)
+        if self.splits[:-1] == (max_rows,) * (self.world_size - 1):
+            return gathered[: self.sequence_length]
+        chunks = gathered.view(self.world_size, max_rows, *tensor.shape[1:])
+        return torch.cat([chunks[r, :n] for r, n in enumerate(self.splits)], dim=0)
+
+    def local_frame_sums(self, local_x: torch.Tensor, num_frames: int, tokens_per_frame: int,
+                         video_start: int = 0) -> torch.Tensor:
+        """Per-frame fp32 sums of this rank's rows, one contiguous slice per frame
+        (deterministic; ulysses_runtime.py:606-635)."""
+        sums = torch.zeros(num_frames, local_x.shape[-1], device=local_x.device, dtype=torch.float32)
+        v0, v1 = video_start, video_start + num_frames * tokens_per_frame
+        lo, hi = max(self.local_start, v0), min(self.local_end, v1)
+        if hi <= lo:
+            return sums
+        first = (lo - v0) // tokens_per_frame
+        last = (hi - 1 - v0) // tokens_per_frame
+        for frame in range(first, last + 1):
+            a = max(lo, v0 + frame * tokens_per_frame)
+            b = min(hi, v0 + (frame + 1) * tokens_per_frame)
+            sums[frame] = local_x[a - self.local_start:b - self.local_start].sum(0, dtype=torch.float32)
+        return sums
+
+    def video_frame_mean_async(self, local_x, num_frames, tokens_per_frame, video_start=0):
+        """Launch the frame-sum all-reduce; returns (sums, work) (ulysses_runtime.py:638-643)."""
+        sums = self.local_frame_sums(local_x, num_frames, tokens_per_frame, video_start)
+        work = dist.all_reduce(sums, async_op=True, group=self.group)
+        return sums, work
+
+
+def init_ulysses(backend: str = "nccl", *, profile_enabled: bool = False,
+                 timeout_seconds: int = 120) -> UlyssesRuntime:
+    """Initialise the process group from torchrun's environment and bind LOCAL_RANK."""
+    world_size = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if backend == "nccl":
+        torch.cuda.set_device(local_rank)
+        device = torch.device("cuda", local_rank)
+    else:
+        device = torch.device("cpu")
+    if not dist.is_initialized():
+        kwargs = dict(backend=backend, timeout=timedelta(seconds=timeout_seconds))
+        if backend == "nccl":
+            kwargs["device_id"] = device
+        dist.init_process_group(**kwargs)
+    rank = dist.get_rank()
+    actual = dist.get_world_size()
+    if actual != world_size and "WORLD_SIZE" in os.environ:
+        raise RuntimeError(f"WORLD_SIZE={world_size}, process group has {actual}")
+    return UlyssesRuntime(rank=rank, world_size=actual, local_rank=local_rank, device=device,
+                          backend=backend, profile_enabled=profile_enabled)
