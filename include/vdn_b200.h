@@ -121,7 +121,7 @@ int vdn_mxfp8_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, cons
  * residual epilogue:
  *   r = bf16(dequant(x1) dequant(w1)^T + dequant(x2) dequant(w2)^T) (+ bias)
  *   y = resid != NULL ? bf16(resid + bf16(gate[col] * r)) : r
- * (k_pad2 = 0 for a single range).  Covers the block's output projection
+ * (k_pad2 = 0 for a single range).  y must not overlap resid (VDN_ERR_ARG).  Covers the block's output projection
  * to_out(softmax) + to_out_linear(VDA) as one GEMM over K = 2 x 5120, and the
  * AdaLN gated residual adds, fused into the GEMM store.
  * Replaces HybridAttention's to_out + to_out_linear add (src/models/hybrid_attention.py:217-254)

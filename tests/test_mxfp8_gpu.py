@@ -61,7 +61,7 @@ def test_reject_nonfinite_activation(cuda, value):
     quantize_activation(x, check_finite=False)   # caller-owned guard: no raise
 
 
-@pytest.mark.parametrize("rows,k", [(1, 128), (129, 256), (131, 1792), (129, 5120)])
+@pytest.mark.parametrize("rows,k", [(1, 128), (129, 256), (131, 1792), (129, 5120), (3, 200), (5, 12800)])
 def test_producers_layout_rounding_and_finite(cuda, rows, k):
     from vdn_b200.mxfp8_kernels import (launch_gelu_quantize, launch_prenorm_quantize,
                                         launch_swiglu_quantize)

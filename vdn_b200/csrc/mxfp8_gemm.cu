@@ -2,7 +2,7 @@
 // one E8M0 scale per 32 K-elements):
 //     y[:rows_out, :n] = bf16( dequant(xq, xs) @ dequant(wq, ws)^T ) (+ bias)
 //
-// Persistent, warp-specialised CTA (192 threads, one per SM):
+// Persistent, warp-specialised CTA (320 threads, one per SM):
 //   warp 0     TMA producer: A tile 128x128 B and B tile 256x128 B (128B swizzle)
 //              plus the tile's scale atoms (512-byte bulk copies: the swizzled
 //              SWIZZLE_32_4_4 scale layout stores one 128-row x 128-K atom
@@ -10,8 +10,10 @@
 //   warp 1     TMEM allocator and single-thread MMA issuer: per stage, three
 //              tcgen05.cp (scales -> TMEM) and four 128x256x32 block-scaled MMAs
 //              into a 128-lane x 256-column fp32 TMEM accumulator
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator (each warp its 32-lane
-//              quadrant), bf16 rounding, bias, cropped stores
+//   warps 2-9  epilogue: tcgen05.ld of the accumulator (each warp a 32-lane
+//              quadrant x 128 columns) into registers, immediate release of
+//              the accumulator, then bf16 rounding, bias, gated residual and
+//              16-byte stores overlapped with the next tile's MMAs
 // Tiles are walked in groups of 16 M-tiles with N fastest so the live A and B
 // tiles of all CTAs stay in L2.  Every mbarrier wait is bounded (2 s); a
 // timeout aborts all roles, drains copies in flight, frees TMEM and reports
@@ -37,7 +39,7 @@ constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;
 constexpr int SF_COL = 256;                   // 12 columns per stage: SFA 4, SFB 8
 constexpr int GROUP_M = 16;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
 constexpr size_t SMEM_BYTES =
     1024 + STAGES * (A_BYTES + B_BYTES + SF_STAGE) + (2 * STAGES + 3) * 8 + 16;
 
@@ -55,6 +57,7 @@ struct Params {
   int64_t rows_out;
   int64_t n;
   int m_tiles, n_tiles, k_blocks, k_blocks2, n_groups;  // n_groups = n_pad / 128
+  int vec_ok;                // 16-byte vector epilogue allowed (alignment of y / bias / resid / gate)
   int* status;
 };
 
@@ -66,6 +69,72 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   const int local = t - g * per_group;
   mb = first + local % gsize;
   nb = local / gsize;
+}
+
+__device__ __forceinline__ void prefetch_l2_row(const uint16_t* ptr, int64_t cols) {
+  const char* c = reinterpret_cast<const char*>(ptr);
+  for (int64_t off = 0; off < cols * 2; off += 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(c + off));
+}
+
+// One thread's row segment of the epilogue: y = bf16(acc) (+ bias, rounded to
+// bf16) and, with a residual, y = resid + bf16(gate * y), rounded to bf16.
+// Bias, gate and residual are read through the read-only path: y must not
+// overlap them.
+__device__ __forceinline__ void store_row(const Params& p, const uint32_t (&r)[128], int64_t row,
+                                          int64_t col0) {
+  uint16_t* yrow = p.y + row * p.ldy;
+  if (p.vec_ok && col0 + 128 <= p.n) {
+    const uint4* rrow = p.resid ? reinterpret_cast<const uint4*>(p.resid + row * p.ldr + col0) : nullptr;
+    const uint4* bias = p.bias ? reinterpret_cast<const uint4*>(p.bias + col0) : nullptr;
+    const uint4* gate = p.resid ? reinterpret_cast<const uint4*>(p.gate + col0) : nullptr;
+    uint4* dst = reinterpret_cast<uint4*>(yrow + col0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        v[i] = __uint_as_float(r[8 * j + i]);
+        v[i + 1] = __uint_as_float(r[8 * j + i + 1]);
+        round_bf16_pair(v[i], v[i + 1]);
+      }
+      if (bias) {
+        float b[8];
+        unpack8(__ldg(bias + j), b);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          v[i] += b[i];
+          v[i + 1] += b[i + 1];
+          round_bf16_pair(v[i], v[i + 1]);
+        }
+      }
+      if (rrow) {
+        float g[8], x[8];
+        unpack8(__ldg(gate + j), g);
+        unpack8(__ldg(rrow + j), x);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          float a = g[i] * v[i], b = g[i + 1] * v[i + 1];
+          round_bf16_pair(a, b);
+          v[i] = x[i] + a;
+          v[i + 1] = x[i + 1] + b;
+        }
+      }
+      dst[j] = pack8(v);
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 128; ++i) {
+    const int64_t col = col0 + i;
+    if (col < p.n) {
+      float v = round_bf16(__uint_as_float(r[i]));
+      if (p.bias) v = round_bf16(v + bf16_bits_to_f32(p.bias[col]));
+      if (p.resid)
+        v = bf16_bits_to_f32(p.resid[row * p.ldr + col]) + round_bf16(bf16_bits_to_f32(p.gate[col]) * v);
+      yrow[col] = f32_to_bf16_bits(v);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -93,7 +162,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    mbar_init(acc_empty, 256);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -213,49 +282,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;                      // TMEM lane quadrant of this warp
+    // Warps 2-9: TMEM lane quadrant warp % 4 (the only lanes a warp may read),
+    // column half (warp - 2) / 4.  Each thread owns one output row x 128 columns:
+    // it moves them into registers, hands the accumulator back to the MMA warp
+    // at once, and finishes bias / residual / stores while the next tile's
+    // MMAs run.
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quad * 32 + lane;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int mb, nb;
       tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+      const int64_t row = (int64_t)mb * BM + row_in_tile;
+      const int64_t col0 = (int64_t)nb * BN + half * 128;
+      const bool live = row < p.rows_out && col0 < p.n;
+      if (live && p.resid) prefetch_l2_row(p.resid + row * p.ldr + col0, p.n - col0 < 128 ? p.n - col0 : 128);
       const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, acc_phase, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      const int64_t row = (int64_t)mb * BM + row_in_tile;
-      uint16_t* yrow = p.y + row * p.ldy;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(quad * 32) << 16) + ACC_COL + c * 32, r);
-        tmem_ld_wait();
-        const int64_t col0 = (int64_t)nb * BN + c * 32;
-        if (row >= p.rows_out || col0 >= p.n) continue;
-        float v[32];
+      uint32_t r[128];
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + ACC_COL + half * 128;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          v[i] = round_bf16(__uint_as_float(r[i]));
-          const int64_t col = col0 + i;
-          if (p.bias) {
-            const float b = col < p.n ? bf16_bits_to_f32(p.bias[col]) : 0.f;
-            v[i] = round_bf16(v[i] + b);
-          }
-          if (p.resid && col < p.n) {  // gated residual: resid + bf16(gate * y), bf16
-            const float g = bf16_bits_to_f32(p.gate[col]);
-            v[i] = bf16_bits_to_f32(p.resid[row * p.ldr + col]) + round_bf16(g * v[i]);
-          }
-        }
-        if (col0 + 32 <= p.n && ((reinterpret_cast<uintptr_t>(yrow + col0) & 15) == 0)) {
-          uint4* dst = reinterpret_cast<uint4*>(yrow + col0);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = pack8(v + 8 * i);
-        } else {
-          for (int i = 0; i < 32 && col0 + i < p.n; ++i) yrow[col0 + i] = f32_to_bf16_bits(v[i]);
-        }
-      }
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(taddr + c * 32, r + 32 * c);
+      tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(acc_empty);
       acc_phase ^= 1;
+      if (live) store_row(p, r, row, col0);
     }
   }
 
@@ -346,6 +400,12 @@ static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, 
                                 aligned16(wq2) && aligned16(ws2)),
                 "second operand pair must be non-null and 16-byte aligned");
   VDN_CHECK_ARG(m_pad / 128 < (1 << 30) && n_pad / 128 < (1 << 30), "extents too large");
+  if (resid) {
+    // The epilogue reads the residual through the read-only cache path.
+    const uintptr_t y0 = reinterpret_cast<uintptr_t>(y), y1 = y0 + 2 * ((rows_out - 1) * ldy + n);
+    const uintptr_t r0 = reinterpret_cast<uintptr_t>(resid), r1 = r0 + 2 * ((rows_out - 1) * ldr + n);
+    VDN_CHECK_ARG(y1 <= r0 || r1 <= y0, "y must not overlap the residual");
+  }
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
   CUtensorMap ma, mb, ma2, mb2;
@@ -377,6 +437,8 @@ static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, 
   p.k_blocks2 = (int)(k_pad2 / BK);
   p.n_groups = (int)(n_pad / 128);
   p.status = status;
+  p.vec_ok = aligned16(y) && ldy % 8 == 0 && (!bias || aligned16(bias)) &&
+             (!resid || (aligned16(resid) && ldr % 8 == 0 && aligned16(gate)));
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < info->sms ? tiles : info->sms;
   mxfp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, p);

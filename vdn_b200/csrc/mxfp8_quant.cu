@@ -19,6 +19,7 @@
 #include <string.h>
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -157,84 +158,237 @@ __global__ void __launch_bounds__(256) act_quantize_kernel(
 }
 
 // RMSNorm * w, AdaLN affine (1 + scale[idx]) and shift[idx], bf16 rounding, then
-// MXFP8 of that bf16 value. One CTA per padded row; rows past `rows` quantise
+// MXFP8 of that bf16 value. Rows past `rows` quantise
 // exact zeros (reference src/models/ops/mxfp8_kernels.py:86-139).
 template <typename WT>
+__device__ __forceinline__ void load_weight8(const WT* w, float* out);
+template <>
+__device__ __forceinline__ void load_weight8<float>(const float* w, float* out) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(w));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(w) + 1);
+  out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load_weight8<__nv_bfloat16>(const __nv_bfloat16* w, float* out) {
+  unpack8(__ldg(reinterpret_cast<const uint4*>(w)), out);
+}
+
+// One warp per (padded) row, eight rows per CTA.  Pass 1 reduces the row's sum
+// of squares; pass 2 re-reads the row (L1/L2 resident) one 32-element block per
+// lane, applies RMSNorm * w * (1 + scale[idx]) + shift[idx] with the eager bf16
+// rounding point, and writes the optional bf16 copy, the E4M3 codes and the
+// block's E8M0 byte.  VEC: K % 32 == 0 and every operand 16-byte aligned, so a
+// block is four 16-byte loads per operand; otherwise element-wise loads.
+template <typename WT, bool VEC>
 __global__ void __launch_bounds__(256) prenorm_quantize_kernel(
     const uint16_t* __restrict__ x, int64_t xs, const WT* __restrict__ w,
     const uint16_t* __restrict__ scale, int64_t ss, const uint16_t* __restrict__ shift,
-    int64_t ts, const int64_t* __restrict__ idx, int64_t rows, int64_t k, int64_t kp, float eps,
-    uint16_t* __restrict__ y, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
+    int64_t ts, const int64_t* __restrict__ idx, int64_t rows, int64_t rp, int64_t k, int64_t kp,
+    float eps, uint16_t* __restrict__ y, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
     uint8_t* __restrict__ finite) {
-  const int64_t r = blockIdx.x;
-  const bool valid_row = r < rows;
-  __shared__ float red[8];
-  __shared__ int bad_any;
-  if (threadIdx.x == 0) bad_any = 0;
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rp) return;
+  const bool valid = r < rows;
+  const uint16_t* xr = x + r * xs;
   float sq = 0.f;
   bool bad = false;
-  if (valid_row) {
-    for (int64_t col = threadIdx.x; col < k; col += blockDim.x) {
-      const float xv = bf16_bits_to_f32(x[r * xs + col]);
-      sq += xv * xv;
-      bad |= !isfinite(xv);
+  if (valid) {
+    if (VEC) {
+      for (int64_t c = lane; c * 32 < k; c += 32) {
+        const uint4* src = reinterpret_cast<const uint4*>(xr + c * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float v[8];
+          unpack8(__ldg(src + j), v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            sq = fmaf(v[i], v[i], sq);
+            bad |= !isfinite(v[i]);
+          }
+        }
+      }
+    } else {
+      for (int64_t col = lane; col < k; col += 32) {
+        const float v = bf16_bits_to_f32(xr[col]);
+        sq = fmaf(v, v, sq);
+        bad |= !isfinite(v);
+      }
     }
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tot += red[i];
-  const float inv_rms = rsqrtf(tot / (float)k + eps);
-  const int64_t t = valid_row ? idx[r] : 0;
+  const float inv_rms = rsqrtf(sq / (float)k + eps);
+  const int64_t t = valid ? idx[r] : 0;
+  const uint16_t* scr = scale + t * ss;
+  const uint16_t* shr = shift + t * ts;
   const int64_t nblk = kp >> 5;
-  for (int64_t c0 = 0; c0 < nblk; c0 += blockDim.x) {
-    const int64_t c = c0 + threadIdx.x;
-    const bool active = c < nblk;
+  for (int64_t c = lane; c < nblk; c += 32) {
     float v[32];
+    const int64_t col0 = c * 32;
+    if (VEC && valid && col0 < k) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int64_t col = c * 32 + i;
-      float val = 0.f;
-      if (active && valid_row && col < k) {
-        const float xv = bf16_bits_to_f32(x[r * xs + col]);
-        const float wv = (float)w[col];
-        const float sc = bf16_bits_to_f32(scale[t * ss + col]);
-        const float sh = bf16_bits_to_f32(shift[t * ts + col]);
-        val = round_bf16(__fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(xv, inv_rms), wv),
-                                             __fadd_rn(1.0f, sc)), sh));
-        bad |= !isfinite(val);
-        if (y) y[r * k + col] = f32_to_bf16_bits(val);
+      for (int j = 0; j < 4; ++j) {
+        float xv[8], wv[8], sc[8], sh[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(xr + col0) + j), xv);
+        load_weight8<WT>(w + col0 + 8 * j, wv);
+        unpack8(__ldg(reinterpret_cast<const uint4*>(scr + col0) + j), sc);
+        unpack8(__ldg(reinterpret_cast<const uint4*>(shr + col0) + j), sh);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          v[8 * j + i] = __fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(xv[i], inv_rms), wv[i]),
+                                             __fadd_rn(1.0f, sc[i])), sh[i]);
       }
-      v[i] = val;
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) round_bf16_pair(v[i], v[i + 1]);
+      if (y) {
+        uint4* dst = reinterpret_cast<uint4*>(y + r * k + col0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dst[j] = pack_exact8(v + 8 * j);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int64_t col = col0 + i;
+        float val = 0.f;
+        if (!VEC && valid && col < k) {
+          const float xv = bf16_bits_to_f32(xr[col]);
+          const float wv = (float)w[col];
+          const float sc = bf16_bits_to_f32(scr[col]);
+          const float sh = bf16_bits_to_f32(shr[col]);
+          val = round_bf16(__fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(xv, inv_rms), wv),
+                                               __fadd_rn(1.0f, sc)), sh));
+          if (y) y[r * k + col] = f32_to_bf16_bits(val);
+        }
+        v[i] = val;
+      }
     }
     uint32_t amax_bits = 0;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
+      bad |= !isfinite(v[i]);
       const uint32_t b = __float_as_uint(v[i]) & 0x7FFFFFFFu;
       amax_bits = b > amax_bits ? b : amax_bits;
     }
     float inv;
     const uint32_t sbyte = e8m0_from_amax_bits(amax_bits, &inv);
-    if (active) {
-      uint32_t packed[8];
+    uint32_t packed[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        packed[i] = e4m3x4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv, v[4 * i + 3] * inv);
-      uint4* qp = reinterpret_cast<uint4*>(q + r * kp + c * 32);
-      qp[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      qp[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-      s[scale_offset(r, c, kp)] = (uint8_t)sbyte;
-    }
+    for (int i = 0; i < 8; ++i)
+      packed[i] = e4m3x4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv, v[4 * i + 3] * inv);
+    uint4* qp = reinterpret_cast<uint4*>(q + r * kp + col0);
+    qp[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    qp[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    s[scale_offset(r, c, kp)] = (uint8_t)sbyte;
   }
-  if (bad) bad_any = 1;
-  __syncthreads();
-  if (threadIdx.x == 0) finite[r] = bad_any ? 0 : 1;
+  bad = __any_sync(0xffffffffu, bad);
+  if (lane == 0) finite[r] = bad ? 0 : 1;
 }
 
 // Per-4096-element finite predicate (reference src/models/ops/mxfp8_kernels.py:142-162).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem)
+               : "memory");
+}
+
+// The staged form for K % 32 == 0, aligned operands and K <= kStagedMaxK: four
+// rows per CTA, each warp copies its whole row into shared memory with cp.async
+// (every byte of the row in flight at once), reduces it, then quantises it with
+// four lanes per 32-element block so every global access is a coalesced 16- or
+// 8-byte vector and the four E8M0 bytes of blocks c..c+3 leave as one word.
+constexpr int64_t kStagedMaxK = 12288;
+
+template <typename WT>
+__global__ void __launch_bounds__(128) prenorm_quantize_staged_kernel(
+    const uint16_t* __restrict__ x, int64_t xs, const WT* __restrict__ w,
+    const uint16_t* __restrict__ scale, int64_t ss, const uint16_t* __restrict__ shift,
+    int64_t ts, const int64_t* __restrict__ idx, int64_t rows, int64_t rp, int64_t k, int64_t kp,
+    float eps, uint16_t* __restrict__ y, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
+    uint8_t* __restrict__ finite) {
+  extern __shared__ uint4 staged_rows[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 4 + warp;
+  if (r >= rp) return;  // warp-uniform; the kernel has no CTA-wide barrier
+  const bool valid = r < rows;
+  const int64_t kv = k >> 3;
+  uint4* buf = staged_rows + warp * kv;
+  if (valid) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + r * xs);
+    for (int64_t i = lane; i < kv; i += 32) cp_async16(buf + i, src + i);
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+  }
+  __syncwarp();
+  float sq = 0.f;
+  bool bad = false;
+  if (valid) {
+    for (int64_t i = lane; i < kv; i += 32) {
+      float v[8];
+      unpack8(buf[i], v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sq = fmaf(v[j], v[j], sq);
+        bad |= !isfinite(v[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float inv_rms = rsqrtf(sq / (float)k + eps);
+  const int64_t t = valid ? idx[r] : 0;
+  const uint16_t* scr = scale + t * ss;
+  const uint16_t* shr = shift + t * ts;
+  const int64_t nblk = kp >> 5;
+  const int sub = lane & 3;
+  for (int64_t c0 = 0; c0 < nblk; c0 += 8) {
+    const int64_t c = c0 + (lane >> 2);
+    const int64_t col = c * 32 + sub * 8;
+    float v[8];
+    if (valid && col < k) {
+      float xv[8], wv[8], sc[8], sh[8];
+      unpack8(buf[col >> 3], xv);
+      load_weight8<WT>(w + col, wv);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(scr + col)), sc);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(shr + col)), sh);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(xv[i], inv_rms), wv[i]), __fadd_rn(1.0f, sc[i])),
+                         sh[i]);
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) round_bf16_pair(v[i], v[i + 1]);
+      if (y) *reinterpret_cast<uint4*>(y + r * k + col) = pack_exact8(v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    uint32_t amax_bits = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      bad |= !isfinite(v[i]);
+      const uint32_t b = __float_as_uint(v[i]) & 0x7FFFFFFFu;
+      amax_bits = b > amax_bits ? b : amax_bits;
+    }
+    amax_bits = max(amax_bits, __shfl_xor_sync(0xffffffffu, amax_bits, 1));
+    amax_bits = max(amax_bits, __shfl_xor_sync(0xffffffffu, amax_bits, 2));
+    float inv;
+    const uint32_t sbyte = e8m0_from_amax_bits(amax_bits, &inv);
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, sbyte, 4);
+    const uint32_t b2 = __shfl_down_sync(0xffffffffu, sbyte, 8);
+    const uint32_t b3 = __shfl_down_sync(0xffffffffu, sbyte, 12);
+    if (c < nblk) {
+      *reinterpret_cast<uint2*>(q + r * kp + col) =
+          make_uint2(e4m3x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv),
+                     e4m3x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv));
+      // Lanes 0 and 16 hold blocks c = c0 and c0 + 4 (c % 4 == 0; nblk % 4 == 0).
+      if ((lane & 15) == 0)
+        *reinterpret_cast<uint32_t*>(s + scale_offset(r, c, kp)) = sbyte | b1 << 8 | b2 << 16 | b3 << 24;
+    }
+  }
+  bad = __any_sync(0xffffffffu, bad);
+  if (lane == 0) finite[r] = bad ? 0 : 1;
+}
+
 template <typename T, int MODE>
 __global__ void finite_parts_kernel(const T* __restrict__ x, int64_t n, uint8_t* __restrict__ parts) {
   const int64_t base = (int64_t)blockIdx.x * 4096;
@@ -423,17 +577,48 @@ int vdn_mxfp8_prenorm_quantize(const void* x, int64_t rows, int64_t k, int64_t x
                 "weight must be fp32 or bf16");
   const int64_t rp = (rows + 127) / 128 * 128, kp = (k + 127) / 128 * 128;
   const uint16_t* xp = static_cast<const uint16_t*>(x);
-  if (weight_dtype == VDN_DTYPE_F32) {
-    prenorm_quantize_kernel<float><<<(unsigned)rp, 256, 0, stream>>>(
-        xp, x_stride, static_cast<const float*>(weight), static_cast<const uint16_t*>(scale),
-        scale_stride, static_cast<const uint16_t*>(shift), shift_stride, indices, rows, k, kp, eps,
-        static_cast<uint16_t*>(y), q, s, finite);
-  } else {
-    prenorm_quantize_kernel<__nv_bfloat16><<<(unsigned)rp, 256, 0, stream>>>(
-        xp, x_stride, static_cast<const __nv_bfloat16*>(weight), static_cast<const uint16_t*>(scale),
-        scale_stride, static_cast<const uint16_t*>(shift), shift_stride, indices, rows, k, kp, eps,
-        static_cast<uint16_t*>(y), q, s, finite);
+  const bool vec = k % 32 == 0 && aligned16(x) && x_stride % 8 == 0 && aligned16(weight) &&
+                   aligned16(scale) && scale_stride % 8 == 0 && aligned16(shift) &&
+                   shift_stride % 8 == 0 && (!y || aligned16(y));
+  if (vec && k <= kStagedMaxK) {
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+      const int bytes = (int)(4 * kStagedMaxK * 2);
+      attr = cudaFuncSetAttribute(prenorm_quantize_staged_kernel<float>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (attr == cudaSuccess)
+        attr = cudaFuncSetAttribute(prenorm_quantize_staged_kernel<__nv_bfloat16>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    });
+    VDN_CUDA_TRY(attr);
+    const unsigned sgrid = (unsigned)((rp + 3) / 4);
+    const size_t smem = (size_t)4 * k * 2;
+#define VDN_PRENORM_STAGED(WT)                                                                 \
+  prenorm_quantize_staged_kernel<WT><<<sgrid, 128, smem, stream>>>(                            \
+      xp, x_stride, static_cast<const WT*>(weight), static_cast<const uint16_t*>(scale),         \
+      scale_stride, static_cast<const uint16_t*>(shift), shift_stride, indices, rows, rp, k, kp, \
+      eps, static_cast<uint16_t*>(y), q, s, finite)
+    if (weight_dtype == VDN_DTYPE_F32) VDN_PRENORM_STAGED(float);
+    else VDN_PRENORM_STAGED(__nv_bfloat16);
+#undef VDN_PRENORM_STAGED
+    VDN_LAUNCH_CHECK("mxfp8 prenorm quantize");
+    return VDN_OK;
   }
+  const unsigned grid = (unsigned)((rp + 7) / 8);
+#define VDN_PRENORM(WT, V)                                                                     \
+  prenorm_quantize_kernel<WT, V><<<grid, 256, 0, stream>>>(                                    \
+      xp, x_stride, static_cast<const WT*>(weight), static_cast<const uint16_t*>(scale),         \
+      scale_stride, static_cast<const uint16_t*>(shift), shift_stride, indices, rows, rp, k, kp, \
+      eps, static_cast<uint16_t*>(y), q, s, finite)
+  if (weight_dtype == VDN_DTYPE_F32) {
+    if (vec) VDN_PRENORM(float, true);
+    else VDN_PRENORM(float, false);
+  } else {
+    if (vec) VDN_PRENORM(__nv_bfloat16, true);
+    else VDN_PRENORM(__nv_bfloat16, false);
+  }
+#undef VDN_PRENORM
   VDN_LAUNCH_CHECK("mxfp8 prenorm quantize");
   return VDN_OK;
 }
