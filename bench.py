@@ -22,6 +22,11 @@ Workloads:
   vda   BASELINE config 2: the VDA branch, H=40, d=128, 21 frames x 1560 tokens,
         metric = algorithmic HBM GB/s (q, k, v, gate, beta, alpha in; out).
         N > 1: independent replicas (heads are independent; no collective).
+        --frames F shrinks the clip (small profiling case).
+  gemm  BASELINE config 1: the MXFP8 GEMM sweep, M = 32760, (N, K) in
+        (15360, 5120), (5120, 5120), (13824, 5120), (5120, 13824); each step
+        quantises the bf16 activation and runs the four GEMMs; metric = TFLOP/s.
+        --rows M shrinks M (small profiling case).  N > 1: replicas.
 """
 from __future__ import annotations
 
@@ -167,6 +172,7 @@ def bench_vda(args, torch, dist, rank, world):
     from vdn_b200 import _lib
     from vdn_b200.linear_attention import vda_forward, window_bounds
     F, S, H, d = (VDA_CFG[k] for k in ("F", "S", "H", "d"))
+    F = args.frames or F
     dev = torch.device("cuda", torch.cuda.current_device())
     stream = torch.cuda.current_stream(dev)
     q, k, v, beta, gate, alpha = vda_inputs(torch, dev, F, S, H, d, seed=rank)
@@ -278,6 +284,129 @@ def cpu_baseline_vda(threads):
     dt = (time.perf_counter() - t0) * H
     return {"value": round(vda_bytes(F, S, H, d) / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
             "kind": "port", "sample": "oracle VDA body, 1 of 40 heads at 21x1560 tokens, time x40"}
+
+
+# ---------------------------------------------------------------------- gemm
+GEMM_SHAPES = (("qkv", 15360, 5120), ("o", 5120, 5120), ("ffn_up", 13824, 5120), ("ffn_down", 5120, 13824))
+GEMM_ROWS = 32760
+
+
+def gemm_activation(torch, device, rows, k, seed):
+    """bf16 N(0,1) with 1% of the K channels (a fixed seeded set) scaled x50."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(rows, k, device=device, generator=g)
+    cols = torch.randperm(k, generator=torch.Generator().manual_seed(seed))[: max(1, k // 100)]
+    x[:, cols.to(device)] *= 50.0
+    return x.bfloat16()
+
+
+def bench_gemm(args, torch, dist, rank, world):
+    """MXFP8 GEMM sweep, activation quantised on the fly each step."""
+    from vdn_b200.mxfp8_quant import quantize_activation
+    from vdn_b200.mxfp8_linear import mxfp8_gemm, check_gemm_status
+    M = args.rows or GEMM_ROWS
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    cases = []
+    for i, (name, n, k) in enumerate(GEMM_SHAPES):
+        x = gemm_activation(torch, dev, M, k, seed=10 + i)
+        g = torch.Generator(device=dev).manual_seed(20 + i)
+        w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+        wq, ws = quantize_activation(w)
+        del w
+        y = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
+        cases.append(dict(name=name, n=n, k=k, x=x, wq=wq, ws=ws, y=y, flops=2 * M * n * k))
+
+    def run(c, xq=None, xs=None):
+        if xq is None:
+            xq, xs = quantize_activation(c["x"], check_finite=False)
+        mxfp8_gemm(xq, xs, c["wq"], c["ws"], c["n"], rows=M, out=c["y"])
+
+    def step():
+        for c in cases:
+            run(c)
+
+    with ClockSampler(dev.index) as clk:
+        ms = time_steps(torch, step, args.steps, args.warmup, dist, stream)
+    check_gemm_status(dev)
+    per_step_ms = ms / args.steps
+    total_flops = sum(c["flops"] for c in cases)
+    value = world * total_flops / (per_step_ms * 1e-3) / 1e12
+
+    # Kernel-only times: each GEMM on pre-quantised operands, and each quantiser pass.
+    launches = []
+    for c in cases:
+        c["xq"], c["xs"] = quantize_activation(c["x"], check_finite=False)
+        launches.append((c["name"], (lambda c=c: run(c, c["xq"], c["xs"]))))
+        launches.append((c["name"] + "_quantize", (lambda c=c: quantize_activation(c["x"], check_finite=False))))
+    kt = kernel_times(torch, launches, 10, stream)
+    pk, src = peaks()
+    fp8_peak = 2 * pk["bf16_tflops"]
+    per_shape = {}
+    for c in cases:
+        tf = c["flops"] / (kt[c["name"]] * 1e-3) / 1e12
+        qbytes = M * c["k"] * 2 + (M + 127) // 128 * 128 * c["k"] * 33 // 32
+        per_shape[c["name"]] = {"m": M, "n": c["n"], "k": c["k"], "gemm_ms": round(kt[c["name"]], 4),
+                                "tflops": round(tf, 1), "frac_fp8_peak": round(tf / fp8_peak, 4),
+                                "quantize_ms": round(kt[c["name"] + "_quantize"], 4),
+                                "quantize_gbs": round(qbytes / (kt[c["name"] + "_quantize"] * 1e-3) / 1e9, 1)}
+    top = cases[0]
+    achieved = top["flops"] / (kt[top["name"]] * 1e-3) / 1e12
+
+    # End to end through the public API: host activations in, bf16 results out.
+    xh = [c["x"].cpu().pin_memory() for c in cases]
+    yh = [torch.empty(M, c["n"], dtype=torch.bfloat16).pin_memory() for c in cases]
+    xd = [torch.empty_like(c["x"]) for c in cases]
+
+    def e2e_step():
+        for c, h, d_, o in zip(cases, xh, xd, yh):
+            d_.copy_(h, non_blocking=True)
+            xq, xs = quantize_activation(d_, check_finite=False)
+            mxfp8_gemm(xq, xs, c["wq"], c["ws"], c["n"], rows=M, out=c["y"])
+            o.copy_(c["y"], non_blocking=True)
+
+    e2e_steps = max(2, args.steps // 2)
+    e2e_ms = time_steps(torch, e2e_step, e2e_steps, 1, dist, stream) / e2e_steps
+    return {
+        "metric": "MXFP8 GEMM TFLOP/s, BASELINE config 1 sweep (activation quantised each step)",
+        "value": round(value, 1), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_step_ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 e4m3 x e4m3, e8m0 per 32, fp32 accumulate",
+        "data": "synthetic (bf16 N(0,1) activations, 1% of channels x50; N(0,0.02) weights)",
+        "config": {"workload": "gemm_config1", "m": M, "shapes": [[n, k] for _, n, k in GEMM_SHAPES],
+                   "parallelism": f"replicated x{world}" if world > 1 else "single GPU",
+                   "l2": "operands and outputs of every GEMM larger than L2"},
+        "e2e": {"value": round(world * total_flops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": sum(h.numel() * 2 for h in xh),
+                "d2h_bytes_per_step": sum(o.numel() * 2 for o in yh)},
+        "gpu_launches": 2 * len(cases) * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (qkv, %d x 15360 x 5120)" % M,
+                     "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / fp8_peak, 4), "traffic": None,
+                     "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']}): the FP8 rate",
+                     "algorithmic_flops_per_launch": top["flops"]},
+        "shapes": per_shape,
+        "clocks": clk.summary(),
+    }
+
+
+def cpu_baseline_gemm(threads):
+    """Dequantised fp32 matmul oracle on a 256-row slice of the QKV shape, scaled to the sweep."""
+    import torch
+    from oracle import mxfp8 as omx
+    rows = 256
+    total = 0.0
+    for i, (name, n, k) in enumerate(GEMM_SHAPES[:1]):
+        x = gemm_activation(torch, torch.device("cpu"), rows, k, seed=10 + i)
+        w = (torch.randn(n, k, generator=torch.Generator().manual_seed(20 + i)) * 0.02).bfloat16()
+        xq, xs = omx.quantize(x.float().numpy())
+        wq, wsc = omx.quantize(w.float().numpy())
+        t0 = time.perf_counter()
+        omx.mxfp8_gemm(xq, xs, wq, wsc, rows, n)
+        total += time.perf_counter() - t0
+        flops = 2 * rows * n * k
+    return {"value": round(flops / total / 1e12, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": "oracle dequantise + fp32 matmul, 256 rows of the QKV shape (15360 x 5120)"}
 
 
 # ---------------------------------------------------------------------- block
@@ -406,13 +535,18 @@ def cpu_baseline_block(threads):
             "3 frames x 1560 tokens (per-token work is constant in the frame count)"}
 
 
+CPU_BASELINES = {"block": cpu_baseline_block, "vda": cpu_baseline_vda, "gemm": cpu_baseline_gemm}
+
+
 # ---------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="block", choices=["block", "vda"])
+    ap.add_argument("--workload", default="block", choices=["block", "vda", "gemm"])
+    ap.add_argument("--rows", type=int, default=0, help="gemm: M override (small profiling case)")
+    ap.add_argument("--frames", type=int, default=0, help="vda: frame-count override (small case)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -426,7 +560,7 @@ def main():
             return
         import torch
         torch.set_num_threads(threads)
-        fn = cpu_baseline_block if args.workload == "block" else cpu_baseline_vda
+        fn = CPU_BASELINES[args.workload]
         steps, warmup = max(1, min(args.steps, 3)), 1
         for _ in range(warmup):
             fn(threads)
@@ -437,6 +571,11 @@ def main():
             meta = dict(metric="hybrid-block tokens/s (BASELINE config 3, 32760 tokens)",
                         unit="tokens/s", scaling="strong",
                         config={"workload": "hybrid_block_config3", **BLOCK_CFG})
+        elif args.workload == "gemm":
+            meta = dict(metric="MXFP8 GEMM TFLOP/s, BASELINE config 1 sweep (activation quantised each step)",
+                        unit="TFLOP/s", scaling="weak",
+                        config={"workload": "gemm_config1", "m": GEMM_ROWS,
+                                "shapes": [[n, k] for _, n, k in GEMM_SHAPES]})
         else:
             meta = dict(metric="VDA branch HBM GB/s (algorithmic bytes), BASELINE config 2",
                         unit="GB/s", scaling="weak", config={"workload": "vda_config2", **VDA_CFG})
@@ -463,13 +602,14 @@ def main():
         torch.cuda.set_device(0)
     if args.workload == "block":
         rec = bench_block(args, torch, dist, rank, world)
+    elif args.workload == "gemm":
+        rec = bench_gemm(args, torch, dist, rank, world)
     else:
         rec = bench_vda(args, torch, dist, rank, world)
     if rank == 0:
         if not args.no_cpu_baseline:
             torch.set_num_threads(threads)
-            rec["cpu_baseline"] = (cpu_baseline_block if args.workload == "block"
-                                   else cpu_baseline_vda)(threads)
+            rec["cpu_baseline"] = CPU_BASELINES[args.workload](threads)
         print(json.dumps(rec))
     if dist is not None:
         dist.barrier()

@@ -1,0 +1,58 @@
+"""Multi-GPU check run under torchrun by tests/test_ulysses_gpu.py (one process per GPU).
+
+Every rank runs the hybrid block twice on identical seeded inputs: once on all
+rows on its own GPU (no exchange), once sequence-sharded through the Ulysses
+runtime (NCCL all-to-all around head-sharded attention, frame-sum all-reduce).
+The rank's shard of the two outputs must agree: the GEMMs and producers are
+row-independent and attention is head-independent, so the only difference is
+the summation order of the frame mean that feeds alpha.
+"""
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from vdn_b200.block import BlockConfig, HybridBlock  # noqa: E402
+from vdn_b200.ulysses import init_ulysses  # noqa: E402
+
+
+def main():
+    rt = init_ulysses("nccl", timeout_seconds=60)
+    dev = rt.device
+    failures = []
+    for frames, tokens in ((4, 64), (3, 100)):
+        cfg = BlockConfig(hidden=512, heads=4, head_dim=128, ffn=1024, radius=1, lora_rank=8)
+        block = HybridBlock(cfg, seed=3, device=dev)
+        with torch.random.fork_rng(devices=[]):
+            torch.manual_seed(11)
+            torch.nn.init.normal_(block.softmax_gate.weight, std=0.05)
+        g = torch.Generator().manual_seed(frames * 1000 + tokens)
+        T = frames * tokens
+        x = torch.randn(T, cfg.hidden, generator=g).bfloat16().to(dev)
+        temb = torch.randn(cfg.hidden, generator=g).to(dev)
+        full = block(x, temb, frames, tokens)
+        rt.sequence_length = 0
+        rt.configure(T, cfg.heads)
+        shard = block(x[rt.local_start:rt.local_end].contiguous(), temb, frames, tokens, rt)
+        torch.cuda.synchronize()
+        want = full[rt.local_start:rt.local_end].double()
+        err = float((shard.double() - want).norm() / want.norm())
+        ok = bool(torch.isfinite(shard).all()) and err < 2e-3
+        print(f"rank {rt.rank} frames={frames} tokens={tokens} rows={shard.shape[0]} rel_l2={err:.3e}",
+              flush=True)
+        if not ok:
+            failures.append((frames, tokens, err))
+        gathered = rt.gather_sequence(shard)
+        if gathered.shape != full.shape:
+            failures.append(("gather shape", tuple(gathered.shape)))
+    flag = torch.tensor([len(failures)], device=dev)
+    dist.all_reduce(flag)
+    dist.destroy_process_group()
+    sys.exit(1 if int(flag.item()) else 0)
+
+
+if __name__ == "__main__":
+    main()

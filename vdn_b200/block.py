@@ -84,14 +84,18 @@ class HybridBlock(nn.Module):
         self.up = _Packed(rnd(cfg.ffn, hd), rnd(cfg.ffn), dev)
         self.down = _Packed(rnd(hd, cfg.ffn), rnd(hd), dev)
         self.o_bias = (self.o.bias.float() + self.ol.bias.float()).to(torch.bfloat16)
-        # bf16 small projections (the reference keeps these unquantised)
-        self.adaln = nn.Linear(hd, 6 * hd).to(dev, torch.bfloat16)
-        self.softmax_gate = nn.Linear(hd, H).to(dev, torch.bfloat16)
-        nn.init.zeros_(self.softmax_gate.weight)
-        nn.init.constant_(self.softmax_gate.bias, math.log(0.99 / 0.01))
-        self.beta_proj = nn.Linear(hd, H, bias=False).to(dev, torch.bfloat16)
-        self.output_gate = OutputGate(hd, H, d, bottleneck=d, init="random").to(dev, torch.bfloat16)
-        self.alpha = FrameKDAAlpha(hd, H, d).to(dev)
+        # bf16 small projections (the reference keeps these unquantised).  Their
+        # default initialisers draw from the global generator: seed it here so
+        # that every Ulysses rank builds the same weights.
+        with torch.random.fork_rng(devices=[]):
+            torch.manual_seed(seed + 0x5EED)
+            self.adaln = nn.Linear(hd, 6 * hd).to(dev, torch.bfloat16)
+            self.softmax_gate = nn.Linear(hd, H).to(dev, torch.bfloat16)
+            nn.init.zeros_(self.softmax_gate.weight)
+            nn.init.constant_(self.softmax_gate.bias, math.log(0.99 / 0.01))
+            self.beta_proj = nn.Linear(hd, H, bias=False).to(dev, torch.bfloat16)
+            self.output_gate = OutputGate(hd, H, d, bottleneck=d, init="random").to(dev, torch.bfloat16)
+            self.alpha = FrameKDAAlpha(hd, H, d).to(dev)
         self.norm1 = torch.ones(hd, device=dev)
         self.norm2 = torch.ones(hd, device=dev)
         self.vda_norm = torch.ones(d, device=dev)
