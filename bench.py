@@ -502,6 +502,9 @@ def bench_block(args, torch, dist, rank, world):
         "kernels_ms": {k_: round(v_, 4) for k_, v_ in kt.items()},
         "clocks": clk.summary(),
     }
+    if runtime is not None:
+        rec["config"]["exchange"] = runtime.exchange_mode
+        runtime.close()
     return rec
 
 

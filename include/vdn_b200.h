@@ -121,7 +121,7 @@ int vdn_mxfp8_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, cons
  * residual epilogue:
  *   r = bf16(dequant(x1) dequant(w1)^T + dequant(x2) dequant(w2)^T) (+ bias)
  *   y = resid != NULL ? bf16(resid + bf16(gate[col] * r)) : r
- * (k_pad2 = 0 for a single range).  y must not overlap resid (VDN_ERR_ARG).  Covers the block's output projection
+ * (k_pad2 = 0 for a single range).  y must not overlap resid (VDN_ERR_VALUE).  Covers the block's output projection
  * to_out(softmax) + to_out_linear(VDA) as one GEMM over K = 2 x 5120, and the
  * AdaLN gated residual adds, fused into the GEMM store.
  * Replaces HybridAttention's to_out + to_out_linear add (src/models/hybrid_attention.py:217-254)
@@ -132,6 +132,19 @@ int vdn_mxfp8_gemm_fused(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq
                          int64_t n, int64_t n_pad, int64_t rows_out, void* y, int64_t ldy,
                          const void* resid, int64_t ldr, const void* gate, int* status,
                          cudaStream_t stream);
+
+/* vdn_mxfp8_gemm with a scatter epilogue: the 128 output columns of chunk c
+ * (bf16, bias added) go to chunk_dst[c] + (dst_row0 + row) * dst_ld elements,
+ * where chunk_dst is a DEVICE array of n / 128 bf16 pointers (local or peer
+ * memory).  n % 128 == 0, dst_ld % 8 == 0, every pointer 16-byte aligned.  The
+ * QKV projection uses it to store each head's q / k / v slice straight into
+ * the receive buffer of the Ulysses rank that owns the head.
+ * Replaces MXFP8Linear (src/models/ops/mxfp8_linear.py:60-102) followed by the
+ * sequence -> heads all-to-all (src/inference/utils/ulysses_runtime.py:451-519). */
+int vdn_mxfp8_gemm_scatter(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, const uint8_t* ws,
+                           int64_t k_pad, const void* bias, int64_t m_pad, int64_t n, int64_t n_pad,
+                           int64_t rows_out, const uint64_t* chunk_dst, int64_t dst_ld,
+                           int64_t dst_row0, int* status, cudaStream_t stream);
 
 /* Window-softmax combine: merges n_partials dense attentions of query frame f
  * against key frame f + delta_j (outs[j] bf16 [rows_j, H*d] token-major, lses[j]
@@ -146,6 +159,36 @@ int vdn_window_merge(int n_partials, const void* const* outs, const float* const
                      const int* batch0, const int* frame_lo, const int* frame_hi, int F, int S,
                      int H, int d, const void* gate, int64_t g_ss, int64_t g_sh, void* out_bf16,
                      int64_t out_ld, int64_t out_hs, uint8_t* q, uint8_t* s, cudaStream_t stream);
+
+/* ---------------------------------------------------------- peer memory */
+
+#define VDN_IPC_HANDLE_BYTES 64
+
+/* Zero-filled device buffer for exchange through CUDA IPC (cudaMalloc'd, so it
+ * is the base of its allocation), and its release. */
+int vdn_peer_alloc(size_t bytes, void** ptr);
+int vdn_peer_free(void* ptr);
+
+/* CUDA IPC: export a vdn_peer_alloc buffer as VDN_IPC_HANDLE_BYTES bytes, map a
+ * peer's exported buffer into this process (peer access enabled), unmap it. */
+int vdn_ipc_handle(const void* ptr, void* handle);
+int vdn_ipc_open(const void* handle, void** ptr);
+int vdn_ipc_close(void* ptr);
+
+/* Heads -> sequence return of a head-sharded bf16 output as MXFP8: element
+ * (t, j, e) of src (t < rows, j < heads_local, e < d) sits at t*row_stride +
+ * j*head_stride + e.  Each 32-element block is quantised with the MXFP8 rule
+ * and stored, with its E8M0 byte, into the operand of the rank that owns token
+ * t (row_starts[p] <= t < row_starts[p + 1], host array of nranks + 1): codes
+ * [rp_p, kp] at dst_codes[p], swizzled scales at dst_scales[p] (host arrays of
+ * device pointers, local or peer), column (head0 + j) * d + e.  nranks <= 8.
+ * Replaces the heads -> sequence all-to-all (src/inference/utils/ulysses_runtime.py:522-582)
+ * and the MXFP8 quantisation of to_out / to_out_linear inputs
+ * (src/models/ops/mxfp8_quant.py:77-90). */
+int vdn_mxfp8_quantize_scatter(const void* src, int64_t rows, int heads_local, int d,
+                               int64_t row_stride, int64_t head_stride, int head0, int64_t kp,
+                               int nranks, const int64_t* row_starts, void* const* dst_codes,
+                               void* const* dst_scales, int* nonfinite, cudaStream_t stream);
 
 /* -------------------------------------------------------------------- VDA */
 

@@ -34,20 +34,30 @@ def main():
         x = torch.randn(T, cfg.hidden, generator=g).bfloat16().to(dev)
         temb = torch.randn(cfg.hidden, generator=g).to(dev)
         full = block(x, temb, frames, tokens)
+        rt.close()
         rt.sequence_length = 0
         rt.configure(T, cfg.heads)
-        shard = block(x[rt.local_start:rt.local_end].contiguous(), temb, frames, tokens, rt)
-        torch.cuda.synchronize()
-        want = full[rt.local_start:rt.local_end].double()
-        err = float((shard.double() - want).norm() / want.norm())
-        ok = bool(torch.isfinite(shard).all()) and err < 2e-3
-        print(f"rank {rt.rank} frames={frames} tokens={tokens} rows={shard.shape[0]} rel_l2={err:.3e}",
-              flush=True)
-        if not ok:
-            failures.append((frames, tokens, err))
-        gathered = rt.gather_sequence(shard)
-        if gathered.shape != full.shape:
-            failures.append(("gather shape", tuple(gathered.shape)))
+        shards = {}
+        for mode in ("alltoall", "peer", "peer"):     # the peer path twice: buffer reuse
+            rt.exchange_mode = mode
+            shard = block(x[rt.local_start:rt.local_end].contiguous(), temb, frames, tokens, rt)
+            torch.cuda.synchronize()
+            want = full[rt.local_start:rt.local_end].double()
+            err = float((shard.double() - want).norm() / want.norm())
+            ok = bool(torch.isfinite(shard).all()) and err < 2e-3
+            print(f"rank {rt.rank} {mode} frames={frames} tokens={tokens} rows={shard.shape[0]} "
+                  f"rel_l2={err:.3e}", flush=True)
+            if not ok:
+                failures.append((mode, frames, tokens, err))
+            shards.setdefault(mode, shard)
+            gathered = rt.gather_sequence(shard)
+            if gathered.shape != full.shape:
+                failures.append(("gather shape", tuple(gathered.shape)))
+        # The two exchanges move the same bytes: identical block outputs.
+        if not torch.equal(shards["alltoall"], shards["peer"]):
+            d = (shards["alltoall"].float() - shards["peer"].float()).abs().max().item()
+            print(f"rank {rt.rank} alltoall vs peer max abs diff {d:.3e}", flush=True)
+    rt.close()
     flag = torch.tensor([len(failures)], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()

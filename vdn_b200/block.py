@@ -120,7 +120,8 @@ class HybridBlock(nn.Module):
     def launches_per_forward(self, world_size=1):
         """Kernels of this library launched per block forward (for bench accounting)."""
         # prenorm, QKV GEMM, window merge, VDA (5), quantise VDA out, O GEMM, prenorm,
-        # FFN up, GELU quantise, FFN down; Ulysses adds two grouped quantisers
+        # FFN up, GELU quantise, FFN down; the peer exchange quantises both
+        # outputs with two scatter launches instead of one local quantiser
         return 14 + (1 if world_size > 1 else 0)
 
     # ---------------------------------------------------------------- forward
@@ -137,18 +138,21 @@ class HybridBlock(nn.Module):
         idx = torch.zeros(rows, dtype=torch.int64, device=dev)
         y1, q1, s1, _ = launch_prenorm_quantize(x, self.norm1, cfg.eps, scale_msa.view(1, hd),
                                                 shift_msa.view(1, hd), idx, write_bf16=True)
-        qkv = torch.empty(rows, 3 * hd, device=dev, dtype=torch.bfloat16)
-        self._gemm(q1, s1, self.qkv, rows, qkv, bias=self.qkv.bias)
-        sgate = torch.sigmoid(self.softmax_gate(y1))                      # [rows, H]
-        beta = torch.sigmoid(self.beta_proj(y1))                          # [rows, H]
-        lgate = self.output_gate(y1).reshape(rows, hd)                    # [rows, H*d]
-        if runtime is None:
-            frame_mean = y1.view(frames, tokens, hd).mean(1, dtype=torch.float32)
-            first, second = self._attention(qkv, sgate, beta, lgate, frame_mean, frames, tokens,
-                                            heads=slice(0, H))
+        if runtime is not None and runtime.world_size > 1 and runtime.exchange_mode == "peer":
+            first, second = self._attention_peer(y1, q1, s1, frames, tokens, runtime)
         else:
-            first, second = self._attention_ulysses(qkv, sgate, beta, lgate, y1, frames, tokens,
-                                                    runtime)
+            qkv = torch.empty(rows, 3 * hd, device=dev, dtype=torch.bfloat16)
+            self._gemm(q1, s1, self.qkv, rows, qkv, bias=self.qkv.bias)
+            sgate = torch.sigmoid(self.softmax_gate(y1))                  # [rows, H]
+            beta = torch.sigmoid(self.beta_proj(y1))                      # [rows, H]
+            lgate = self.output_gate(y1).reshape(rows, hd)                # [rows, H*d]
+            if runtime is None:
+                frame_mean = y1.view(frames, tokens, hd).mean(1, dtype=torch.float32)
+                first, second = self._attention(qkv, sgate, beta, lgate, frame_mean, frames, tokens,
+                                                heads=slice(0, H))
+            else:
+                first, second = self._attention_ulysses(qkv, sgate, beta, lgate, y1, frames, tokens,
+                                                        runtime)
         x1 = torch.empty_like(x)
         self._gemm(first[0], first[1], self.o, rows, x1, second=(second, self.ol),
                    bias=self.o_bias, resid=x, gate=gate_msa.contiguous())
@@ -212,6 +216,50 @@ class HybridBlock(nn.Module):
         att = self._quantize_grouped(flat, 0, rows)
         lq = self._quantize_grouped(flat, d, rows)
         return att, lq
+
+    def _attention_peer(self, y1, q1, s1, frames, tokens, rt):
+        """Head-sharded attention with the exchange done by the producers (peer memory).
+
+        The QKV GEMM stores every head's slice into its owner's receive buffer;
+        the softmax / VDA outputs return as MXFP8 through the scatter quantiser.
+        The small per-token gate inputs (softmax gate, beta, the output gate's
+        low-rank hidden) travel by one all-gather, and the frame sums for alpha
+        by one all-reduce, both overlapping the QKV GEMM.
+        """
+        from .linear_attention import vda_forward
+        cfg = self.cfg
+        hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+        T = frames * tokens
+        ex = rt.exchange(H, d)
+        hl, h0 = ex.hl, ex.head0
+        og = self.output_gate
+        sums, work = rt.video_frame_mean_async(y1, frames, tokens)
+        small = torch.cat([torch.sigmoid(self.softmax_gate(y1)), torch.sigmoid(self.beta_proj(y1)),
+                           og.down(y1)], dim=1)                           # [rows, 2H + r]
+        gathered, gwork = ex.gather_rows_async(small)
+        w = self.qkv
+        _lib.call("vdn_mxfp8_gemm_scatter", _lib.ptr(q1), _lib.ptr(s1), _lib.ptr(w.q), _lib.ptr(w.s),
+                  w.k_pad, _lib.ptr(w.bias), q1.shape[0], w.n, w.n_pad, y1.shape[0],
+                  _lib.ptr(ex.chunk_dst), ex.dst_ld, rt.local_start, _lib.ptr(self._status),
+                  _lib.stream_of(y1.device))
+        ex.fence()
+        work.wait()
+        gwork.wait()
+        gathered = ex.finish_rows(gathered)                               # [T, 2H + r]
+        frame_mean = sums / tokens
+        recv = ex.qkv()                                                   # [T, hl, 3d]
+        q, k, v = recv[:, :, 0:d], recv[:, :, d:2 * d], recv[:, :, 2 * d:3 * d]
+        cols = slice(h0 * d, (h0 + hl) * d)
+        lgate = torch.sigmoid(F.linear(gathered[:, 2 * H:], og.up.weight[cols], og.up.bias[cols]))
+        att = torch.empty(T, hl, d, device=y1.device, dtype=torch.bfloat16)
+        window_softmax(q, k, v, gathered[:, h0:h0 + hl], frames, tokens, cfg.radius, out=att)
+        alpha = self.alpha(frame_mean, heads=slice(h0, h0 + hl))
+        lin = vda_forward(q, k, v, gathered[:, H + h0:H + h0 + hl], lgate.view(T, hl, d), alpha,
+                          window_bounds(frames, cfg.radius), frames, tokens, self.vda_norm)
+        ex.scatter_quantize(att, ex.att_dst)
+        ex.scatter_quantize(lin.view(T, hl, d), ex.lin_dst)
+        ex.fence()
+        return ex.operands()
 
     def _quantize_grouped(self, flat, offset, rows):
         cfg = self.cfg

@@ -58,6 +58,12 @@ struct Params {
   int64_t n;
   int m_tiles, n_tiles, k_blocks, k_blocks2, n_groups;  // n_groups = n_pad / 128
   int vec_ok;                // 16-byte vector epilogue allowed (alignment of y / bias / resid / gate)
+  // Scatter epilogue (chunk_dst != null): the 128 output columns of chunk c go to
+  // chunk_dst[c] + (dst_row0 + row) * dst_ld, e.g. each head's q / k / v slice
+  // straight into the receive buffer of the rank that owns the head.
+  const uint64_t* chunk_dst;
+  int64_t dst_ld;
+  int64_t dst_row0;
   int* status;
 };
 
@@ -83,12 +89,13 @@ __device__ __forceinline__ void prefetch_l2_row(const uint16_t* ptr, int64_t col
 // overlap them.
 __device__ __forceinline__ void store_row(const Params& p, const uint32_t (&r)[128], int64_t row,
                                           int64_t col0) {
-  uint16_t* yrow = p.y + row * p.ldy;
+  uint16_t* dst = p.chunk_dst ? reinterpret_cast<uint16_t*>(p.chunk_dst[col0 >> 7]) + (p.dst_row0 + row) * p.dst_ld
+                             : p.y + row * p.ldy + col0;
   if (p.vec_ok && col0 + 128 <= p.n) {
     const uint4* rrow = p.resid ? reinterpret_cast<const uint4*>(p.resid + row * p.ldr + col0) : nullptr;
     const uint4* bias = p.bias ? reinterpret_cast<const uint4*>(p.bias + col0) : nullptr;
     const uint4* gate = p.resid ? reinterpret_cast<const uint4*>(p.gate + col0) : nullptr;
-    uint4* dst = reinterpret_cast<uint4*>(yrow + col0);
+    uint4* dst4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       float v[8];
@@ -120,7 +127,7 @@ __device__ __forceinline__ void store_row(const Params& p, const uint32_t (&r)[1
           v[i + 1] = x[i + 1] + b;
         }
       }
-      dst[j] = pack8(v);
+      dst4[j] = pack8(v);
     }
     return;
   }
@@ -132,7 +139,7 @@ __device__ __forceinline__ void store_row(const Params& p, const uint32_t (&r)[1
       if (p.bias) v = round_bf16(v + bf16_bits_to_f32(p.bias[col]));
       if (p.resid)
         v = bf16_bits_to_f32(p.resid[row * p.ldr + col]) + round_bf16(bf16_bits_to_f32(p.gate[col]) * v);
-      yrow[col] = f32_to_bf16_bits(v);
+      dst[i] = f32_to_bf16_bits(v);
     }
   }
 }
@@ -384,16 +391,19 @@ static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, 
                        const uint8_t* ws2, int64_t k_pad2, const void* bias, int64_t m_pad,
                        int64_t n, int64_t n_pad, int64_t rows_out, void* y, int64_t ldy,
                        const void* resid, int64_t ldr, const void* gate, int* status,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const uint64_t* chunk_dst = nullptr,
+                       int64_t dst_ld = 0, int64_t dst_row0 = 0) {
   using namespace vdn::gemm;
   VDN_CHECK_ARG(m_pad >= 0 && n > 0 && n_pad > 0 && k_pad > 0 && k_pad2 >= 0, "bad GEMM extents");
   VDN_CHECK_ARG(m_pad % 128 == 0 && n_pad % 128 == 0 && k_pad % 128 == 0 && k_pad2 % 128 == 0,
                 "m_pad, n_pad and k_pad must be multiples of 128");
   VDN_CHECK_ARG(n <= n_pad && rows_out >= 0 && rows_out <= m_pad, "crop exceeds the padded extents");
-  VDN_CHECK_ARG(ldy >= n, "ldy must be at least n");
+  VDN_CHECK_ARG(chunk_dst || ldy >= n, "ldy must be at least n");
+  VDN_CHECK_ARG(!chunk_dst || (n % 128 == 0 && dst_ld % 8 == 0 && dst_ld >= 128 && dst_row0 >= 0 && !resid),
+                "scatter epilogue needs n % 128 == 0, dst_ld % 8 == 0 and no residual");
   VDN_CHECK_ARG(!resid || (gate && ldr >= n), "a residual needs a gate vector and ldr >= n");
   if (rows_out == 0 || m_pad == 0) return VDN_OK;
-  VDN_CHECK_ARG(xq && xs && wq && ws && y, "null pointer");
+  VDN_CHECK_ARG(xq && xs && wq && ws && (y || chunk_dst), "null pointer");
   VDN_CHECK_ARG(aligned16(xq) && aligned16(xs) && aligned16(wq) && aligned16(ws),
                 "codes and scales must be 16-byte aligned");
   VDN_CHECK_ARG(k_pad2 == 0 || (xq2 && xs2 && wq2 && ws2 && aligned16(xq2) && aligned16(xs2) &&
@@ -437,8 +447,11 @@ static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, 
   p.k_blocks2 = (int)(k_pad2 / BK);
   p.n_groups = (int)(n_pad / 128);
   p.status = status;
-  p.vec_ok = aligned16(y) && ldy % 8 == 0 && (!bias || aligned16(bias)) &&
+  p.vec_ok = (chunk_dst ? true : aligned16(y) && ldy % 8 == 0) && (!bias || aligned16(bias)) &&
              (!resid || (aligned16(resid) && ldr % 8 == 0 && aligned16(gate)));
+  p.chunk_dst = chunk_dst;
+  p.dst_ld = dst_ld;
+  p.dst_row0 = dst_row0;
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < info->sms ? tiles : info->sms;
   mxfp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, p);
@@ -463,4 +476,14 @@ extern "C" int vdn_mxfp8_gemm_fused(const uint8_t* xq, const uint8_t* xs, const 
                                     cudaStream_t stream) {
   return launch_gemm(xq, xs, wq, ws, k_pad, xq2, xs2, wq2, ws2, k_pad2, bias, m_pad, n, n_pad,
                      rows_out, y, ldy, resid, ldr, gate, status, stream);
+}
+
+extern "C" int vdn_mxfp8_gemm_scatter(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq,
+                                      const uint8_t* ws, int64_t k_pad, const void* bias, int64_t m_pad,
+                                      int64_t n, int64_t n_pad, int64_t rows_out,
+                                      const uint64_t* chunk_dst, int64_t dst_ld, int64_t dst_row0,
+                                      int* status, cudaStream_t stream) {
+  if (!chunk_dst) return vdn::set_error(VDN_ERR_VALUE, "chunk_dst must not be null");
+  return launch_gemm(xq, xs, wq, ws, k_pad, nullptr, nullptr, nullptr, nullptr, 0, bias, m_pad, n, n_pad,
+                     rows_out, nullptr, 0, nullptr, 0, nullptr, status, stream, chunk_dst, dst_ld, dst_row0);
 }

@@ -1,13 +1,19 @@
-"""Ulysses sequence parallelism: sequence <-> head all-to-all over NCCL.
+"""Ulysses sequence parallelism: sequence <-> head exchange around attention.
 
 Mirrors ec-jt/vdn src/inference/utils/ulysses_runtime.py (sequence_splits,
 balanced_splits, UlyssesRuntime.configure / sequence_to_heads /
 heads_to_sequence / gather_sequence / video_frame_mean_async, init_ulysses)
-for the standard (head-sharded) exchange.  One process per GPU; the exchange is
-one torch.distributed all_to_all_single per direction on the NCCL process
-group (NVLink / NVSwitch inside a node).  Exact routing: every row / head
-arrives where the reference sends it.  Timeouts are short by default so that a
-rank that never joins ends the others' next collective with an error.
+for the standard (head-sharded) exchange.  One process per GPU.  Two exchange
+modes with identical routing (every row / head arrives where the reference
+sends it):
+
+  "alltoall"  the reference's form: one torch.distributed all_to_all_single per
+              direction on the NCCL process group;
+  "peer"      (default for the block) the producers store into the consumers'
+              memory over NVLink: see vdn_b200.peer.
+
+Timeouts are short by default so that a rank that never joins ends the others'
+next collective with an error.
 """
 from __future__ import annotations
 
@@ -60,6 +66,10 @@ class UlyssesRuntime:
     num_heads: int = 0
     profile_enabled: bool = False
     profile_events: dict = field(default_factory=dict)
+    # "peer": producers store into peer memory (vdn_b200.peer); "alltoall": the
+    # reference's NCCL all-to-all exchange (sequence_to_heads / heads_to_sequence).
+    exchange_mode: str = "peer"
+    _exchanges: dict = field(default_factory=dict)
 
     @property
     def is_main(self) -> bool:
@@ -85,6 +95,23 @@ class UlyssesRuntime:
         self.local_end = self.local_start + splits[self.rank]
         self.num_heads = num_heads
         self.heads_per_rank = num_heads // self.world_size
+
+    def exchange(self, num_heads: int, head_dim: int):
+        """The peer-memory exchange of the configured geometry (built once, cached)."""
+        from .peer import PeerExchange
+        key = (self.sequence_length, num_heads, head_dim)
+        ex = self._exchanges.get(key)
+        if ex is None:
+            if not self.sequence_length:
+                raise RuntimeError("configure() the runtime before building an exchange")
+            ex = self._exchanges[key] = PeerExchange(self, self.sequence_length, num_heads, head_dim)
+        return ex
+
+    def close(self) -> None:
+        """Release peer mappings (collective: every rank calls it before destroy_process_group)."""
+        for ex in self._exchanges.values():
+            ex.close()
+        self._exchanges.clear()
 
     def profile_start(self):
         if not self.profile_enabled:
