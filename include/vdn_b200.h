@@ -175,6 +175,9 @@ int vdn_ipc_handle(const void* ptr, void* handle);
 int vdn_ipc_open(const void* handle, void** ptr);
 int vdn_ipc_close(void* ptr);
 
+/* Stream-ordered device copy (local or peer memory; a copy engine, no SM). */
+int vdn_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+
 /* Heads -> sequence return of a head-sharded bf16 output as MXFP8: element
  * (t, j, e) of src (t < rows, j < heads_local, e < d) sits at t*row_stride +
  * j*head_stride + e.  Each 32-element block is quantised with the MXFP8 rule

@@ -145,3 +145,31 @@ def test_config1_shapes_sampled_rows(cuda, n, k):
     xd = dequant(xq, xs)[rows]
     want = (xd.double() @ dequant(wq, ws).double().T).float().bfloat16()
     torch.testing.assert_close(y[rows], want, rtol=.01, atol=.016)
+
+
+@pytest.mark.parametrize("rows,row0", [(300, 0), (257, 41)])
+def test_scatter_epilogue_routes_chunks(cuda, rows, row0):
+    """vdn_mxfp8_gemm_scatter: every 128-column chunk lands at its table address,
+    row by row, identical to the plain GEMM output (bias included; ragged rows)."""
+    from vdn_b200 import _lib
+    n, k = 768, 256                       # 6 chunks
+    xq, xs = quantised(rows, k, cuda, 31)
+    wq, ws = quantised(n, k, cuda, 32, scale=0.05)
+    bias = torch.randn(n, device=cuda).bfloat16()
+    ref = torch.empty(rows, n, device=cuda, dtype=torch.bfloat16)
+    _lib.call("vdn_mxfp8_gemm", _lib.ptr(xq), _lib.ptr(xs), _lib.ptr(wq), _lib.ptr(ws), _lib.ptr(bias),
+              xq.shape[0], n, wq.shape[0], k, rows, _lib.ptr(ref), n, None, _lib.stream_of(cuda))
+    # destination: [row0 + rows, 3, 2, 128] with chunk c -> slot perm[c]
+    total = row0 + rows + 5
+    dst = torch.full((total, 6, 128), -7.0, device=cuda).bfloat16()
+    perm = [4, 1, 5, 0, 3, 2]
+    table = torch.tensor([dst.data_ptr() + perm[c] * 128 * 2 for c in range(6)], dtype=torch.int64,
+                         device=cuda)
+    _lib.call("vdn_mxfp8_gemm_scatter", _lib.ptr(xq), _lib.ptr(xs), _lib.ptr(wq), _lib.ptr(ws), k,
+              _lib.ptr(bias), xq.shape[0], n, wq.shape[0], rows, _lib.ptr(table), 6 * 128, row0, None,
+              _lib.stream_of(cuda))
+    torch.cuda.synchronize()
+    for c in range(6):
+        assert torch.equal(dst[row0:row0 + rows, perm[c]], ref[:, c * 128:(c + 1) * 128]), c
+    untouched = torch.cat([dst[:row0], dst[row0 + rows:]])
+    assert bool((untouched.float() == -7.0).all())

@@ -135,3 +135,41 @@ def test_quantiser_full_size_properties(cuda):
     assert np.array_equal(scales[rows], mx.unswizzle(rs, 256, 5120))
     back = torch.from_numpy(mx.dequantize(q[:4096].cpu().numpy(), mx.swizzle(scales[:4096])))
     torch.testing.assert_close(back[:4096].float(), x[:4096].float().cpu(), rtol=.063, atol=.001 * 50)
+
+
+@pytest.mark.parametrize("d,hl", [(128, 3), (64, 2)])
+def test_quantize_scatter_routes_to_owners(cuda, d, hl):
+    """vdn_mxfp8_quantize_scatter: a head-sharded [T, hl, d] output lands, as MXFP8,
+    in each owner's padded operand exactly as quantize_activation of the owner's
+    rows of the full [T, H*d] matrix (three emulated owners with ragged rows)."""
+    import ctypes as C
+    from vdn_b200 import _lib
+    from vdn_b200.mxfp8_quant import quantize_activation
+    T, H = 300, 2 * hl
+    head0 = hl                            # this "rank" holds heads [hl, 2 hl)
+    full = torch.randn(T, H, d, device=cuda).bfloat16()
+    src = full[:, head0:head0 + hl]       # strided view [T, hl, d]
+    starts = [0, 130, 250, 300]
+    kp = H * d
+    owners = []
+    for p in range(3):
+        rp = (starts[p + 1] - starts[p] + 127) // 128 * 128
+        owners.append((torch.zeros(rp, kp, dtype=torch.uint8, device=cuda),
+                       torch.zeros(rp * kp // 32, dtype=torch.uint8, device=cuda)))
+    _lib.call("vdn_mxfp8_quantize_scatter", _lib.ptr(src), T, hl, d, src.stride(0), src.stride(1), head0,
+              kp, 3, (C.c_int64 * 4)(*starts), (C.c_void_p * 3)(*[o[0].data_ptr() for o in owners]),
+              (C.c_void_p * 3)(*[o[1].data_ptr() for o in owners]), None, _lib.stream_of(cuda))
+    torch.cuda.synchronize()
+    cols = slice(head0 * d, (head0 + hl) * d)
+    for p in range(3):
+        rows = full[starts[p]:starts[p + 1]].reshape(-1, kp)
+        masked = torch.zeros_like(rows)
+        masked[:, cols] = rows[:, cols]
+        q, s = quantize_activation(masked)
+        assert torch.equal(owners[p][0][:, cols], q[:, cols]), p
+        # scale bytes of this rank's column blocks only (others stay untouched)
+        r = torch.arange(q.shape[0], device=cuda)[:, None]
+        c = torch.arange(kp // 32, device=cuda)[None, :]
+        idx = ((r // 128) * (kp // 128) + c // 4) * 512 + r % 32 * 16 + (r % 128 // 32) * 4 + c % 4
+        blk = slice(head0 * d // 32, (head0 + hl) * d // 32)
+        assert torch.equal(owners[p][1][idx[:, blk]], s[idx[:, blk]]), p

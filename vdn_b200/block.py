@@ -223,30 +223,32 @@ class HybridBlock(nn.Module):
         The QKV GEMM stores every head's slice into its owner's receive buffer;
         the softmax / VDA outputs return as MXFP8 through the scatter quantiser.
         The small per-token gate inputs (softmax gate, beta, the output gate's
-        low-rank hidden) travel by one all-gather, and the frame sums for alpha
-        by one all-reduce, both overlapping the QKV GEMM.
+        low-rank hidden) and the per-rank frame sums for alpha are copied into
+        every rank by the copy engines while the QKV GEMM runs.
         """
         from .linear_attention import vda_forward
         cfg = self.cfg
         hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
         T = frames * tokens
-        ex = rt.exchange(H, d)
-        hl, h0 = ex.hl, ex.head0
         og = self.output_gate
-        sums, work = rt.video_frame_mean_async(y1, frames, tokens)
-        small = torch.cat([torch.sigmoid(self.softmax_gate(y1)), torch.sigmoid(self.beta_proj(y1)),
-                           og.down(y1)], dim=1)                           # [rows, 2H + r]
-        gathered, gwork = ex.gather_rows_async(small)
+        r = og.down.weight.shape[0]
+        ex = rt.exchange(H, d, frames, 2 * H + r)
+        hl, h0 = ex.hl, ex.head0
+        # Side inputs into this rank's slot of every rank's buffers (copy engines).
+        sums = rt.local_frame_sums(y1, frames, tokens)
+        ex.sums()[rt.rank].copy_(sums)
+        ex.publish_sums()
+        torch.cat([torch.sigmoid(self.softmax_gate(y1)), torch.sigmoid(self.beta_proj(y1)),
+                   og.down(y1)], dim=1, out=ex.local_rows())              # [rows, 2H + r]
+        ex.publish_rows()
         w = self.qkv
         _lib.call("vdn_mxfp8_gemm_scatter", _lib.ptr(q1), _lib.ptr(s1), _lib.ptr(w.q), _lib.ptr(w.s),
                   w.k_pad, _lib.ptr(w.bias), q1.shape[0], w.n, w.n_pad, y1.shape[0],
                   _lib.ptr(ex.chunk_dst), ex.dst_ld, rt.local_start, _lib.ptr(self._status),
                   _lib.stream_of(y1.device))
         ex.fence()
-        work.wait()
-        gwork.wait()
-        gathered = ex.finish_rows(gathered)                               # [T, 2H + r]
-        frame_mean = sums / tokens
+        gathered = ex.rows()                                              # [T, 2H + r]
+        frame_mean = ex.sums().sum(0) / tokens                            # fixed rank order
         recv = ex.qkv()                                                   # [T, hl, 3d]
         q, k, v = recv[:, :, 0:d], recv[:, :, d:2 * d], recv[:, :, 2 * d:3 * d]
         cols = slice(h0 * d, (h0 + hl) * d)

@@ -40,8 +40,13 @@ constexpr int ACC_COL = 0;
 constexpr int SF_COL = 256;                   // 12 columns per stage: SFA 4, SFB 8
 constexpr int GROUP_M = 16;
 constexpr int THREADS = 320;
+constexpr int STAGE_PITCH = 80;                // staged epilogue row: 64 B + 16 B pad
+constexpr int STAGE_BYTES = 32 * STAGE_PITCH;  // per epilogue warp
+constexpr size_t BAR_BYTES = 256;              // mbarriers, TMEM address, abort flag
 constexpr size_t SMEM_BYTES =
-    1024 + STAGES * (A_BYTES + B_BYTES + SF_STAGE) + (2 * STAGES + 3) * 8 + 16;
+    1024 + STAGES * (A_BYTES + B_BYTES + SF_STAGE) + BAR_BYTES + 8 * STAGE_BYTES;
+static_assert((2 * STAGES + 3) * 8 + 8 <= BAR_BYTES, "barrier region");
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 
 struct Params {
   const uint8_t* xs;
@@ -89,8 +94,7 @@ __device__ __forceinline__ void prefetch_l2_row(const uint16_t* ptr, int64_t col
 // overlap them.
 __device__ __forceinline__ void store_row(const Params& p, const uint32_t (&r)[128], int64_t row,
                                           int64_t col0) {
-  uint16_t* dst = p.chunk_dst ? reinterpret_cast<uint16_t*>(p.chunk_dst[col0 >> 7]) + (p.dst_row0 + row) * p.dst_ld
-                             : p.y + row * p.ldy + col0;
+  uint16_t* dst = p.y + row * p.ldy + col0;
   if (p.vec_ok && col0 + 128 <= p.n) {
     const uint4* rrow = p.resid ? reinterpret_cast<const uint4*>(p.resid + row * p.ldr + col0) : nullptr;
     const uint4* bias = p.bias ? reinterpret_cast<const uint4*>(p.bias + col0) : nullptr;
@@ -144,6 +148,53 @@ __device__ __forceinline__ void store_row(const Params& p, const uint32_t (&r)[1
   }
 }
 
+// Scatter epilogue of one warp (32 consecutive rows from row0, 128 columns from
+// col0): bf16(acc) (+ bias), then the rows leave through a 32 x 32-column
+// shared-memory transpose so that every store instruction writes 64-byte row
+// pieces (four lanes x 16 B) of the destination instead of 16 bytes of 32
+// different rows: peer stores over NVLink want contiguous runs.  Host checks
+// guarantee n % 128 == 0 and 16-byte alignment.
+__device__ __forceinline__ void store_rows_staged(const Params& p, const uint32_t (&r)[128], int64_t row0,
+                                                  int lane, int64_t col0, uint8_t* stage) {
+  const uint4* bias = p.bias ? reinterpret_cast<const uint4*>(p.bias + col0) : nullptr;
+  uint16_t* base = reinterpret_cast<uint16_t*>(p.chunk_dst[col0 >> 7]);
+  uint4* mine = reinterpret_cast<uint4*>(stage + lane * STAGE_PITCH);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      v[i] = __uint_as_float(r[8 * j + i]);
+      v[i + 1] = __uint_as_float(r[8 * j + i + 1]);
+      round_bf16_pair(v[i], v[i + 1]);
+    }
+    if (bias) {
+      float b[8];
+      unpack8(__ldg(bias + j), b);
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        v[i] += b[i];
+        v[i + 1] += b[i + 1];
+        round_bf16_pair(v[i], v[i + 1]);
+      }
+    }
+    mine[j & 3] = pack8(v);
+    if ((j & 3) == 3) {
+      __syncwarp();
+      const int q = lane & 3;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int rl = i * 8 + (lane >> 2);
+        const uint4 val = *reinterpret_cast<const uint4*>(stage + rl * STAGE_PITCH + q * 16);
+        const int64_t row = row0 + rl;
+        if (row < p.rows_out)
+          *reinterpret_cast<uint4*>(base + (p.dst_row0 + row) * p.dst_ld + (j >> 2) * 32 + q * 8) = val;
+      }
+      __syncwarp();
+    }
+  }
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -161,6 +212,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* mma_done = acc_empty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint8_t* stage_base = sSF + STAGES * SF_STAGE + BAR_BYTES;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -316,7 +368,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       mbar_arrive(acc_empty);
       acc_phase ^= 1;
-      if (live) store_row(p, r, row, col0);
+      if (p.chunk_dst) {
+        if (col0 < p.n)  // warp-uniform
+          store_rows_staged(p, r, (int64_t)mb * BM + quad * 32, lane, col0,
+                            stage_base + (warp - 2) * STAGE_BYTES);
+      } else if (live) {
+        store_row(p, r, row, col0);
+      }
     }
   }
 

@@ -144,6 +144,13 @@ int vdn_ipc_close(void* ptr) {
   return VDN_OK;
 }
 
+int vdn_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+  if (bytes == 0) return VDN_OK;
+  VDN_CHECK_ARG(dst && src, "null pointer");
+  VDN_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, stream));
+  return VDN_OK;
+}
+
 int vdn_mxfp8_quantize_scatter(const void* src, int64_t rows, int heads_local, int d,
                                int64_t row_stride, int64_t head_stride, int head0, int64_t kp,
                                int nranks, const int64_t* row_starts, void* const* dst_codes,

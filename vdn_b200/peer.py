@@ -101,7 +101,7 @@ class PeerExchange:
     and swizzled scales of the softmax output and of the VDA output.
     """
 
-    def __init__(self, runtime, T: int, H: int, d: int):
+    def __init__(self, runtime, T: int, H: int, d: int, frames: int = 0, row_width: int = 0):
         rt = runtime
         if H % rt.world_size:
             raise ValueError("heads must divide over the ranks")
@@ -117,7 +117,7 @@ class PeerExchange:
         for n in rt.splits:
             self.row_starts.append(self.row_starts[-1] + n)
         rows = rt.splits[rt.rank]
-        self.rows = rows
+
         self.rp = (rows + 127) // 128 * 128
         dev = rt.device
         # heads side
@@ -138,6 +138,14 @@ class PeerExchange:
         self.chunk_dst = torch.tensor(table, dtype=torch.int64, device=dev)
         self.dst_ld = self.hl * 3 * d
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        # Per-token side inputs gathered on every rank ([T, row_width] bf16) and the
+        # per-rank frame sums ([P, frames, hidden] fp32), published by copy-engine
+        # copies into every peer (no SM time taken from the overlapping GEMM).
+        self.frames, self.row_width = frames, row_width
+        rows_bytes = _up(max(1, T * row_width * 2))
+        sums_bytes = _up(max(1, self.P * frames * self.hidden * 4))
+        self.side = PeerBuffer(rows_bytes + sums_bytes, rt.rank, self.P, dev, rt.group)
+        self._sums_off = rows_bytes
         # sequence-side destinations of every rank, for the scatter quantiser
         seq_ptrs = self.seq.ptrs
         self.att_dst = [(p + self.off[0], p + self.off[1]) for p in seq_ptrs]
@@ -155,6 +163,40 @@ class PeerExchange:
         lin = (self.seq.view(torch.uint8, (self.rp, self.hidden), self.off[2]),
                self.seq.view(torch.uint8, (s,), self.off[3]))
         return att, lin
+
+    def rows(self) -> torch.Tensor:
+        """[T, row_width] bf16: every rank's published side rows (valid after a fence)."""
+        return self.side.view(torch.bfloat16, (self.T, self.row_width))
+
+    def local_rows(self) -> torch.Tensor:
+        """This rank's slot [rows, row_width] of rows(); write it, then publish_rows()."""
+        lo = self.row_starts[self.rt.rank]
+        return self.rows()[lo:lo + self.rows_local]
+
+    @property
+    def rows_local(self) -> int:
+        return self.rt.splits[self.rt.rank]
+
+    def sums(self) -> torch.Tensor:
+        """[P, frames, hidden] fp32: every rank's published frame sums (valid after a fence)."""
+        return self.side.view(torch.float32, (self.P, self.frames, self.hidden), self._sums_off)
+
+    def publish_rows(self) -> None:
+        lo = self.row_starts[self.rt.rank]
+        off = lo * self.row_width * 2
+        self._publish(off, self.rows_local * self.row_width * 2)
+
+    def publish_sums(self) -> None:
+        slot = self.frames * self.hidden * 4
+        self._publish(self._sums_off + self.rt.rank * slot, slot)
+
+    def _publish(self, offset: int, nbytes: int) -> None:
+        stream = _lib.stream_of(self.rt.device)
+        src = C.c_void_p(self.side.local + offset)
+        for p in range(self.P):
+            if p != self.rt.rank:
+                _lib.call("vdn_copy_async", C.c_void_p(self.side.ptrs[p] + offset), src,
+                          C.c_size_t(nbytes), stream)
 
     # ------------------------------------------------------------ operations
     def gather_rows_async(self, x: torch.Tensor):
@@ -200,3 +242,4 @@ class PeerExchange:
             dist.barrier(group=self.rt.group)
         self.heads.close()
         self.seq.close()
+        self.side.close()

@@ -96,15 +96,16 @@ class UlyssesRuntime:
         self.num_heads = num_heads
         self.heads_per_rank = num_heads // self.world_size
 
-    def exchange(self, num_heads: int, head_dim: int):
+    def exchange(self, num_heads: int, head_dim: int, frames: int = 0, row_width: int = 0):
         """The peer-memory exchange of the configured geometry (built once, cached)."""
         from .peer import PeerExchange
-        key = (self.sequence_length, num_heads, head_dim)
+        key = (self.sequence_length, num_heads, head_dim, frames, row_width)
         ex = self._exchanges.get(key)
         if ex is None:
             if not self.sequence_length:
                 raise RuntimeError("configure() the runtime before building an exchange")
-            ex = self._exchanges[key] = PeerExchange(self, self.sequence_length, num_heads, head_dim)
+            ex = self._exchanges[key] = PeerExchange(self, self.sequence_length, num_heads, head_dim,
+                                                     frames, row_width)
         return ex
 
     def close(self) -> None:
