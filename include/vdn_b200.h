@@ -146,6 +146,20 @@ int vdn_mxfp8_gemm_scatter(const uint8_t* xq, const uint8_t* xs, const uint8_t* 
                            int64_t rows_out, const uint64_t* chunk_dst, int64_t dst_ld,
                            int64_t dst_row0, int* status, cudaStream_t stream);
 
+/* vdn_mxfp8_gemm whose epilogue applies an activation and quantises: with
+ * r = bf16(bf16(dequant(x) dequant(w)^T) + bias), the bf16 value act(r)
+ * (act = VDN_ACT_GELU_TANH or 0 for none) is stored as
+ * MXFP8: codes q [m_pad, n] and swizzled scales s [m_pad * n / 32], rows in
+ * [rows_out, m_pad) zero.  n % 128 == 0; q, bias 16-byte aligned.  Bit-identical
+ * to vdn_mxfp8_gemm followed by vdn_mxfp8_act_quantize, without the bf16
+ * round trip through HBM: the FFN up projection feeding the down projection.
+ * Replaces MXFP8Linear + the GELU/SwiGLU producer of src/models/ops/fused_block.py:82-105
+ * and src/models/ops/mxfp8_kernels.py:61-124. */
+int vdn_mxfp8_gemm_act_quantize(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq,
+                                const uint8_t* ws, int64_t k_pad, const void* bias, int64_t m_pad,
+                                int64_t n, int64_t n_pad, int64_t rows_out, int act, uint8_t* q,
+                                uint8_t* s, int* status, cudaStream_t stream);
+
 /* Window-softmax combine: merges n_partials dense attentions of query frame f
  * against key frame f + delta_j (outs[j] bf16 [rows_j, H*d] token-major, lses[j]
  * fp32 [batches_j, H, S]; batch = f - batch0[j], valid for frame_lo[j] <= f <=
@@ -177,6 +191,21 @@ int vdn_ipc_close(void* ptr);
 
 /* Stream-ordered device copy (local or peer memory; a copy engine, no SM). */
 int vdn_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+
+/* Copies `bytes` (a multiple of 16, 16-byte aligned) from src to each of the
+ * ndst <= 8 destinations (host array of device pointers, local or peer) in one
+ * launch: the all-gather of small per-token side inputs. */
+int vdn_peer_broadcast(const void* src, size_t bytes, int ndst, void* const* dsts, cudaStream_t stream);
+
+/* Cross-GPU rendezvous on the stream: publishes `epoch` (> 0, increasing by
+ * call) into slot `rank` of every rank's uint64 flag array (flag_arrays[p],
+ * host array of device pointers, p < nranks <= 8; a system-scope release after
+ * all earlier work of the stream) and waits until all nranks slots of this
+ * rank's array (my_flags) hold at least `epoch`.  Later work on the stream then
+ * sees every rank's stores made before its matching call.  Each wait gives up
+ * after 2 s and sets *status (optional device int) to VDN_ERR_TIMEOUT. */
+int vdn_peer_fence(int nranks, void* const* flag_arrays, const void* my_flags, int rank,
+                   uint64_t epoch, int* status, cudaStream_t stream);
 
 /* Heads -> sequence return of a head-sharded bf16 output as MXFP8: element
  * (t, j, e) of src (t < rows, j < heads_local, e < d) sits at t*row_stride +

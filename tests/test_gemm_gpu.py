@@ -173,3 +173,31 @@ def test_scatter_epilogue_routes_chunks(cuda, rows, row0):
         assert torch.equal(dst[row0:row0 + rows, perm[c]], ref[:, c * 128:(c + 1) * 128]), c
     untouched = torch.cat([dst[:row0], dst[row0 + rows:]])
     assert bool((untouched.float() == -7.0).all())
+
+
+@pytest.mark.parametrize("act", ["tanh", "none"])
+def test_gemm_act_quantize_matches_unfused(cuda, act):
+    """vdn_mxfp8_gemm_act_quantize == vdn_mxfp8_gemm (bf16 + bias) followed by the
+    GELU quantiser, bit for bit; padded rows come out as zero codes and scales."""
+    from vdn_b200 import _lib
+    from vdn_b200.mxfp8_kernels import launch_gelu_quantize
+    rows, n, k = 300, 384, 512
+    xq, xs = quantised(rows, k, cuda, 41)
+    wq, ws = quantised(n, k, cuda, 42, scale=0.05)
+    bias = torch.randn(n, device=cuda).bfloat16()
+    y = torch.empty(rows, n, device=cuda, dtype=torch.bfloat16)
+    _lib.call("vdn_mxfp8_gemm", _lib.ptr(xq), _lib.ptr(xs), _lib.ptr(wq), _lib.ptr(ws), _lib.ptr(bias),
+              xq.shape[0], n, wq.shape[0], k, rows, _lib.ptr(y), n, None, _lib.stream_of(cuda))
+    q = torch.full((xq.shape[0], n), 0x5A, dtype=torch.uint8, device=cuda)
+    s = torch.full((xq.shape[0] * n // 32,), 0x5A, dtype=torch.uint8, device=cuda)
+    code = _lib.ACT_GELU_TANH if act == "tanh" else 0
+    _lib.call("vdn_mxfp8_gemm_act_quantize", _lib.ptr(xq), _lib.ptr(xs), _lib.ptr(wq), _lib.ptr(ws), k,
+              _lib.ptr(bias), xq.shape[0], n, wq.shape[0], rows, code, _lib.ptr(q), _lib.ptr(s), None,
+              _lib.stream_of(cuda))
+    if act == "tanh":
+        rq, rs, _ = launch_gelu_quantize(y, approximate="tanh")
+    else:
+        from vdn_b200.mxfp8_quant import quantize_activation
+        rq, rs = quantize_activation(y)
+    torch.cuda.synchronize()
+    assert torch.equal(q, rq) and torch.equal(s, rs)

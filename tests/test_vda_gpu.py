@@ -170,6 +170,22 @@ def test_scan_and_gather_vs_fp64(cuda, frames, text, decay):
         torch.testing.assert_close(got.double().cpu(), torch.from_numpy(want), atol=4e-6, rtol=5e-5)
 
 
+@pytest.mark.parametrize("heads,d", [(40, 128), (20, 128), (3, 128), (80, 64), (5, 64)])
+def test_scan_row_blocking_vs_fp64(cuda, heads, d):
+    """The scan picks 64, 32 or 16 state rows per CTA from the head count; every
+    blocking gives the fp64 recurrence (seeded, 5 frames, both directions)."""
+    from vdn_b200.linear_attention import vda_scan
+    g = torch.Generator().manual_seed(heads * 7 + d)
+    frames = 5
+    t = (torch.randn(frames, heads, d, d, generator=g) * (0.9 / d ** 0.5)).to(cuda)
+    inj = (torch.randn(frames, heads, d, d, generator=g) * 0.1).to(cuda)
+    seed = torch.randn(heads, d, d, generator=g) * .3
+    prefix, suffix = vda_scan(t, inj, seed.to(cuda))
+    op, osf = ovda.run_scans(t.double().cpu().numpy(), inj.double().cpu().numpy(), seed.double().numpy())
+    torch.testing.assert_close(prefix.double().cpu(), torch.from_numpy(op), atol=3e-6, rtol=3e-5)
+    torch.testing.assert_close(suffix.double().cpu(), torch.from_numpy(osf), atol=3e-6, rtol=3e-5)
+
+
 @torch.no_grad()
 def test_gather_vs_reference_stages(cuda, vda_stages_golden):
     from vdn_b200.linear_attention import vda_gather

@@ -53,6 +53,8 @@ def main():
             gathered = rt.gather_sequence(shard)
             if gathered.shape != full.shape:
                 failures.append(("gather shape", tuple(gathered.shape)))
+        for ex in rt._exchanges.values():
+            ex.check()                              # no device fence timed out
         # The two exchanges move the same bytes: identical block outputs.
         if not torch.equal(shards["alltoall"], shards["peer"]):
             d = (shards["alltoall"].float() - shards["peer"].float()).abs().max().item()

@@ -32,7 +32,7 @@ from torch import nn
 
 from . import _lib
 from .linear_attention import FrameKDAAlpha, OutputGate, window_bounds
-from .mxfp8_kernels import launch_gelu_quantize, launch_prenorm_quantize
+from .mxfp8_kernels import launch_prenorm_quantize
 from .mxfp8_quant import quantize_cpu, quantize_activation
 from .window import window_softmax
 
@@ -65,6 +65,8 @@ class HybridBlock(nn.Module):
         hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
         if H * d != hd:
             raise ValueError("heads * head_dim must equal hidden")
+        if hd % 128 or cfg.ffn % 128:
+            raise ValueError("hidden and ffn must be multiples of 128 (MXFP8 epilogues)")
         g = torch.Generator().manual_seed(seed)
         dev = torch.device(device)
 
@@ -120,9 +122,9 @@ class HybridBlock(nn.Module):
     def launches_per_forward(self, world_size=1):
         """Kernels of this library launched per block forward (for bench accounting)."""
         # prenorm, QKV GEMM, window merge, VDA (5), quantise VDA out, O GEMM, prenorm,
-        # FFN up, GELU quantise, FFN down; the peer exchange quantises both
-        # outputs with two scatter launches instead of one local quantiser
-        return 14 + (1 if world_size > 1 else 0)
+        # FFN up (+GELU quantise), FFN down; the peer exchange adds a second scatter
+        # quantiser, two side-input broadcasts and two fences
+        return 13 if world_size == 1 else 17
 
     # ---------------------------------------------------------------- forward
     @torch.no_grad()
@@ -158,9 +160,18 @@ class HybridBlock(nn.Module):
                    bias=self.o_bias, resid=x, gate=gate_msa.contiguous())
         _, q2, s2, _ = launch_prenorm_quantize(x1, self.norm2, cfg.eps, scale_mlp.view(1, hd),
                                                shift_mlp.view(1, hd), idx, write_bf16=False)
-        up = torch.empty(rows, cfg.ffn, device=dev, dtype=torch.bfloat16)
-        self._gemm(q2, s2, self.up, rows, up, bias=self.up.bias)
-        q3, s3, _ = launch_gelu_quantize(up, approximate=cfg.gelu)
+        # FFN up with GELU and the MXFP8 quantisation of the down projection's
+        # input fused into the GEMM epilogue (bit-identical to GEMM -> bf16 ->
+        # launch_gelu_quantize).
+        w = self.up
+        q3 = torch.empty(q2.shape[0], w.n, device=dev, dtype=torch.uint8)
+        s3 = torch.empty(q2.shape[0] * w.n // 32, device=dev, dtype=torch.uint8)
+        if cfg.gelu != "tanh":
+            raise ValueError("the fused FFN epilogue implements GELU (tanh)")
+        act = _lib.ACT_GELU_TANH
+        _lib.call("vdn_mxfp8_gemm_act_quantize", _lib.ptr(q2), _lib.ptr(s2), _lib.ptr(w.q), _lib.ptr(w.s),
+                  w.k_pad, _lib.ptr(w.bias), q2.shape[0], w.n, w.n_pad, rows, act, _lib.ptr(q3),
+                  _lib.ptr(s3), _lib.ptr(self._status), _lib.stream_of(dev))
         x2 = torch.empty_like(x)
         self._gemm(q3, s3, self.down, rows, x2, bias=self.down.bias, resid=x1, gate=gate_mlp.contiguous())
         return x2
@@ -235,8 +246,7 @@ class HybridBlock(nn.Module):
         ex = rt.exchange(H, d, frames, 2 * H + r)
         hl, h0 = ex.hl, ex.head0
         # Side inputs into this rank's slot of every rank's buffers (copy engines).
-        sums = rt.local_frame_sums(y1, frames, tokens)
-        ex.sums()[rt.rank].copy_(sums)
+        rt.local_frame_sums(y1, frames, tokens, out=ex.sums()[rt.rank])
         ex.publish_sums()
         torch.cat([torch.sigmoid(self.softmax_gate(y1)), torch.sigmoid(self.beta_proj(y1)),
                    og.down(y1)], dim=1, out=ex.local_rows())              # [rows, 2H + r]

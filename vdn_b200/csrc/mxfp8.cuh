@@ -43,10 +43,17 @@ __device__ __forceinline__ int64_t scale_offset(int64_t r, int64_t c, int64_t kp
 
 enum Act { ACT_NONE = 0, ACT_GELU_TANH = 1, ACT_GELU_ERF = 2, ACT_SWIGLU = 3 };
 
+// GELU, tanh form: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), with
+// tanh(u) = 1 - 2 / (exp(2u) + 1) evaluated by the hardware exponential and a
+// fast division (a handful of instructions, so the GEMM epilogue that fuses it
+// stays small).  Saturates correctly: exp overflow gives tanh = 1, underflow -1.
+// The result is rounded to bf16 by every caller; the fp32 error (a few ulp)
+// moves that rounding only for values within a few fp32 ulp of a bf16 tie.
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
-  const float inner = k0 * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(inner));
+  const float u = k0 * (x + 0.044715f * x * x * x);
+  const float t = 1.0f - __fdividef(2.0f, __expf(2.0f * u) + 1.0f);
+  return 0.5f * x * (1.0f + t);
 }
 
 __device__ __forceinline__ float gelu_erf(float x) {

@@ -19,6 +19,7 @@
 // timeout aborts all roles, drains copies in flight, frees TMEM and reports
 // VDN_ERR_TIMEOUT through `status`.  No TMA multicast is used.
 #include "common.cuh"
+#include "mxfp8.cuh"
 #include "sm100.cuh"
 
 #include <cudaTypedefs.h>
@@ -69,6 +70,12 @@ struct Params {
   const uint64_t* chunk_dst;
   int64_t dst_ld;
   int64_t dst_row0;
+  // Activation-quantise epilogue (q_out != null): y = act(bf16(acc + bias)) rounded
+  // to bf16, then MXFP8 codes q_out [m_pad, n] and swizzled scales s_out; rows
+  // in [rows_out, m_pad) get zero codes and scales.
+  int act;
+  uint8_t* q_out;
+  uint8_t* s_out;
   int* status;
 };
 
@@ -148,6 +155,64 @@ __device__ __forceinline__ void store_row(const Params& p, const uint32_t (&r)[1
   }
 }
 
+// Activation-quantise epilogue of one thread's row segment (128 columns = four
+// MXFP8 blocks): the same arithmetic as the unfused bf16 store followed by the
+// activation quantiser, so codes and scales are bit-identical to that path.
+template <bool GELU>
+__device__ __forceinline__ void store_row_quant(const Params& p, const uint32_t (&r)[128], int64_t row,
+                                                int64_t col0) {
+  const bool valid = row < p.rows_out;
+  const uint4* bias = p.bias ? reinterpret_cast<const uint4*>(p.bias + col0) : nullptr;
+  uint32_t word = 0;
+#pragma unroll
+  for (int blk = 0; blk < 4; ++blk) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float* w = v + 8 * j;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        w[i] = __uint_as_float(r[32 * blk + 8 * j + i]);
+        w[i + 1] = __uint_as_float(r[32 * blk + 8 * j + i + 1]);
+        round_bf16_pair(w[i], w[i + 1]);
+      }
+      if (bias) {
+        float b[8];
+        unpack8(__ldg(bias + 4 * blk + j), b);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          w[i] += b[i];
+          w[i + 1] += b[i + 1];
+          round_bf16_pair(w[i], w[i + 1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float a = v[i];
+      if (GELU) a = round_bf16(gelu_tanh(a));
+      v[i] = valid ? a : 0.f;
+    }
+    uint32_t amax_bits = 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const uint32_t b = __float_as_uint(v[i]) & 0x7FFFFFFFu;
+      amax_bits = b > amax_bits ? b : amax_bits;
+    }
+    float inv;
+    const uint32_t sbyte = e8m0_from_amax_bits(amax_bits, &inv);
+    word |= sbyte << (8 * blk);
+    uint32_t packed[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      packed[i] = e4m3x4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv, v[4 * i + 3] * inv);
+    uint4* qp = reinterpret_cast<uint4*>(p.q_out + row * p.n + col0 + 32 * blk);
+    qp[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    qp[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  }
+  *reinterpret_cast<uint32_t*>(p.s_out + scale_offset(row, col0 >> 5, p.n)) = word;
+}
+
 // Scatter epilogue of one warp (32 consecutive rows from row0, 128 columns from
 // col0): bf16(acc) (+ bias), then the rows leave through a 32 x 32-column
 // shared-memory transpose so that every store instruction writes 64-byte row
@@ -195,6 +260,10 @@ __device__ __forceinline__ void store_rows_staged(const Params& p, const uint32_
   }
 }
 
+// Epilogue kinds, one kernel instantiation each (keeps every variant's code small).
+enum Epilogue { EPI_STORE = 0, EPI_SCATTER = 1, EPI_QUANT = 2, EPI_QUANT_GELU = 3 };
+
+template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -368,12 +437,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       mbar_arrive(acc_empty);
       acc_phase ^= 1;
-      if (p.chunk_dst) {
+      if constexpr (EPI == EPI_QUANT || EPI == EPI_QUANT_GELU) {
+        if (col0 < p.n) store_row_quant<EPI == EPI_QUANT_GELU>(p, r, row, col0);  // zeros past rows_out
+      } else if constexpr (EPI == EPI_SCATTER) {
         if (col0 < p.n)  // warp-uniform
           store_rows_staged(p, r, (int64_t)mb * BM + quad * 32, lane, col0,
                             stage_base + (warp - 2) * STAGE_BYTES);
-      } else if (live) {
-        store_row(p, r, row, col0);
+      } else {
+        if (live) store_row(p, r, row, col0);
       }
     }
   }
@@ -431,8 +502,14 @@ static int device_info(DeviceInfo** out) {
   DeviceInfo& d = info[dev];
   if (!d.smem_set) {
     VDN_CUDA_TRY(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
-    VDN_CUDA_TRY(cudaFuncSetAttribute(mxfp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)SMEM_BYTES));
+    VDN_CUDA_TRY(cudaFuncSetAttribute(mxfp8_gemm_kernel<EPI_STORE>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    VDN_CUDA_TRY(cudaFuncSetAttribute(mxfp8_gemm_kernel<EPI_SCATTER>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    VDN_CUDA_TRY(cudaFuncSetAttribute(mxfp8_gemm_kernel<EPI_QUANT>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    VDN_CUDA_TRY(cudaFuncSetAttribute(mxfp8_gemm_kernel<EPI_QUANT_GELU>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
     d.smem_set = true;
   }
   *out = &d;
@@ -450,18 +527,22 @@ static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, 
                        int64_t n, int64_t n_pad, int64_t rows_out, void* y, int64_t ldy,
                        const void* resid, int64_t ldr, const void* gate, int* status,
                        cudaStream_t stream, const uint64_t* chunk_dst = nullptr,
-                       int64_t dst_ld = 0, int64_t dst_row0 = 0) {
+                       int64_t dst_ld = 0, int64_t dst_row0 = 0, int act = 0,
+                       uint8_t* q_out = nullptr, uint8_t* s_out = nullptr) {
   using namespace vdn::gemm;
   VDN_CHECK_ARG(m_pad >= 0 && n > 0 && n_pad > 0 && k_pad > 0 && k_pad2 >= 0, "bad GEMM extents");
   VDN_CHECK_ARG(m_pad % 128 == 0 && n_pad % 128 == 0 && k_pad % 128 == 0 && k_pad2 % 128 == 0,
                 "m_pad, n_pad and k_pad must be multiples of 128");
   VDN_CHECK_ARG(n <= n_pad && rows_out >= 0 && rows_out <= m_pad, "crop exceeds the padded extents");
-  VDN_CHECK_ARG(chunk_dst || ldy >= n, "ldy must be at least n");
+  VDN_CHECK_ARG(chunk_dst || q_out || ldy >= n, "ldy must be at least n");
+  VDN_CHECK_ARG(!q_out || (s_out && n % 128 == 0 && !resid && !chunk_dst && aligned16(q_out) &&
+                           (reinterpret_cast<uintptr_t>(s_out) & 3) == 0),
+                "activation-quantise epilogue needs n % 128 == 0, aligned q / s and no residual");
   VDN_CHECK_ARG(!chunk_dst || (n % 128 == 0 && dst_ld % 8 == 0 && dst_ld >= 128 && dst_row0 >= 0 && !resid),
                 "scatter epilogue needs n % 128 == 0, dst_ld % 8 == 0 and no residual");
   VDN_CHECK_ARG(!resid || (gate && ldr >= n), "a residual needs a gate vector and ldr >= n");
   if (rows_out == 0 || m_pad == 0) return VDN_OK;
-  VDN_CHECK_ARG(xq && xs && wq && ws && (y || chunk_dst), "null pointer");
+  VDN_CHECK_ARG(xq && xs && wq && ws && (y || chunk_dst || q_out), "null pointer");
   VDN_CHECK_ARG(aligned16(xq) && aligned16(xs) && aligned16(wq) && aligned16(ws),
                 "codes and scales must be 16-byte aligned");
   VDN_CHECK_ARG(k_pad2 == 0 || (xq2 && xs2 && wq2 && ws2 && aligned16(xq2) && aligned16(xs2) &&
@@ -505,14 +586,24 @@ static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, 
   p.k_blocks2 = (int)(k_pad2 / BK);
   p.n_groups = (int)(n_pad / 128);
   p.status = status;
-  p.vec_ok = (chunk_dst ? true : aligned16(y) && ldy % 8 == 0) && (!bias || aligned16(bias)) &&
+  p.vec_ok = (chunk_dst || q_out ? true : aligned16(y) && ldy % 8 == 0) && (!bias || aligned16(bias)) &&
              (!resid || (aligned16(resid) && ldr % 8 == 0 && aligned16(gate)));
   p.chunk_dst = chunk_dst;
   p.dst_ld = dst_ld;
   p.dst_row0 = dst_row0;
+  p.act = act;
+  p.q_out = q_out;
+  p.s_out = s_out;
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < info->sms ? tiles : info->sms;
-  mxfp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, p);
+  if (q_out && act == VDN_ACT_GELU_TANH)
+    mxfp8_gemm_kernel<EPI_QUANT_GELU><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, p);
+  else if (q_out)
+    mxfp8_gemm_kernel<EPI_QUANT><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, p);
+  else if (chunk_dst)
+    mxfp8_gemm_kernel<EPI_SCATTER><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, p);
+  else
+    mxfp8_gemm_kernel<EPI_STORE><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, p);
   VDN_LAUNCH_CHECK("mxfp8 gemm");
   return VDN_OK;
 }
@@ -544,4 +635,17 @@ extern "C" int vdn_mxfp8_gemm_scatter(const uint8_t* xq, const uint8_t* xs, cons
   if (!chunk_dst) return vdn::set_error(VDN_ERR_VALUE, "chunk_dst must not be null");
   return launch_gemm(xq, xs, wq, ws, k_pad, nullptr, nullptr, nullptr, nullptr, 0, bias, m_pad, n, n_pad,
                      rows_out, nullptr, 0, nullptr, 0, nullptr, status, stream, chunk_dst, dst_ld, dst_row0);
+}
+
+extern "C" int vdn_mxfp8_gemm_act_quantize(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq,
+                                           const uint8_t* ws, int64_t k_pad, const void* bias,
+                                           int64_t m_pad, int64_t n, int64_t n_pad, int64_t rows_out,
+                                           int act, uint8_t* q, uint8_t* s, int* status,
+                                           cudaStream_t stream) {
+  if (act != VDN_ACT_GELU_TANH && act != 0)
+    return vdn::set_error(VDN_ERR_VALUE, "act must be 0 (none) or VDN_ACT_GELU_TANH");
+  if (!q || !s) return vdn::set_error(VDN_ERR_VALUE, "q and s must not be null");
+  if (bias && !aligned16(bias)) return vdn::set_error(VDN_ERR_VALUE, "bias must be 16-byte aligned");
+  return launch_gemm(xq, xs, wq, ws, k_pad, nullptr, nullptr, nullptr, nullptr, 0, bias, m_pad, n, n_pad,
+                     rows_out, nullptr, 0, nullptr, 0, nullptr, status, stream, nullptr, 0, 0, act, q, s);
 }

@@ -96,6 +96,52 @@ __global__ void __launch_bounds__(256) quantize_scatter_kernel(
   if (bad && nonfinite) atomicAdd(nonfinite, 1);
 }
 
+struct PeerSet {
+  int n;
+  uint8_t* ptr[kMaxRanks];
+};
+
+// Copies `bytes` (a multiple of 16) from src to every destination: each thread
+// loads one 16-byte vector and stores it to all of them.
+__global__ void __launch_bounds__(256) broadcast_kernel(const uint4* __restrict__ src, int64_t n16,
+                                                        const PeerSet dst) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 v = __ldg(src + i);
+#pragma unroll 1
+    for (int p = 0; p < dst.n; ++p) reinterpret_cast<uint4*>(dst.ptr[p])[i] = v;
+  }
+}
+
+// Cross-GPU rendezvous: thread p publishes `epoch` into slot `rank` of rank p's
+// flag array (a system-scope release, ordered after every earlier kernel of this
+// stream), then waits (acquire, bounded by kFenceLimitNs) until every rank has
+// published `epoch` into this rank's array.  A timeout sets *status.
+constexpr uint64_t kFenceLimitNs = 2000000000ull;
+
+__global__ void peer_fence_kernel(const PeerSet flags, const uint64_t* my_flags, int rank,
+                                  uint64_t epoch, int* status) {
+  const int p = threadIdx.x;
+  if (p < flags.n) {
+    uint64_t* slot = reinterpret_cast<uint64_t*>(flags.ptr[p]) + rank;
+    asm volatile("fence.sc.sys;\n\tst.release.sys.global.u64 [%0], %1;" ::"l"(slot), "l"(epoch) : "memory");
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    while (true) {
+      uint64_t v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(my_flags + p) : "memory");
+      if (v >= epoch) break;
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > kFenceLimitNs) {
+        if (status) atomicExch(status, VDN_ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 }  // namespace vdn
 
 using namespace vdn;
@@ -148,6 +194,43 @@ int vdn_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream
   if (bytes == 0) return VDN_OK;
   VDN_CHECK_ARG(dst && src, "null pointer");
   VDN_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, stream));
+  return VDN_OK;
+}
+
+int vdn_peer_broadcast(const void* src, size_t bytes, int ndst, void* const* dsts, cudaStream_t stream) {
+  VDN_CHECK_ARG(ndst >= 0 && ndst <= kMaxRanks, "at most %d destinations", kMaxRanks);
+  if (bytes == 0 || ndst == 0) return VDN_OK;
+  VDN_CHECK_ARG(src && dsts && aligned16(src) && bytes % 16 == 0,
+                "source must be 16-byte aligned with a size that is a multiple of 16");
+  PeerSet set;
+  set.n = ndst;
+  for (int p = 0; p < kMaxRanks; ++p) set.ptr[p] = nullptr;
+  for (int p = 0; p < ndst; ++p) {
+    VDN_CHECK_ARG(dsts[p] && aligned16(dsts[p]), "destinations must be non-null and 16-byte aligned");
+    set.ptr[p] = static_cast<uint8_t*>(dsts[p]);
+  }
+  const int64_t n16 = (int64_t)(bytes / 16);
+  const int64_t want = (n16 + 255) / 256;
+  const unsigned grid = (unsigned)(want < 1184 ? want : 1184);
+  broadcast_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(src), n16, set);
+  VDN_LAUNCH_CHECK("peer broadcast");
+  return VDN_OK;
+}
+
+int vdn_peer_fence(int nranks, void* const* flag_arrays, const void* my_flags, int rank,
+                   uint64_t epoch, int* status, cudaStream_t stream) {
+  VDN_CHECK_ARG(nranks >= 1 && nranks <= kMaxRanks, "nranks must lie in [1, %d]", kMaxRanks);
+  VDN_CHECK_ARG(rank >= 0 && rank < nranks && flag_arrays && my_flags && epoch > 0, "bad fence arguments");
+  PeerSet set;
+  set.n = nranks;
+  for (int p = 0; p < kMaxRanks; ++p) set.ptr[p] = nullptr;
+  for (int p = 0; p < nranks; ++p) {
+    VDN_CHECK_ARG(flag_arrays[p] && (reinterpret_cast<uintptr_t>(flag_arrays[p]) & 7) == 0,
+                  "flag arrays must be non-null and 8-byte aligned");
+    set.ptr[p] = static_cast<uint8_t*>(flag_arrays[p]);
+  }
+  peer_fence_kernel<<<1, 32, 0, stream>>>(set, static_cast<const uint64_t*>(my_flags), rank, epoch, status);
+  VDN_LAUNCH_CHECK("peer fence");
   return VDN_OK;
 }
 

@@ -257,39 +257,45 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
 }
 
 // ----------------------------------------------------------------------- scan
-// grid (H, 2 directions, D/64 row blocks); 256 threads in a 16 x 16 grid, each
-// owning 4 state rows x D/16 columns.  Rows of the state evolve independently,
-// so a CTA carries 64 rows through all F steps.  T_f arrives by a 64 KB bulk copy
-// issued as soon as every thread is done with the previous frame's T (two CTAs
-// share an SM, so one computes while the other waits), the 64-row state sits
-// transposed in shared memory
-// (k-major), and each thread accumulates its 4 x D/16 tile with packed fp32 FMAs
-// (fma.rn.f32x2) on top of J_f.  Waits are bounded (2 s).
-template <int D>
+// grid (H, 2 directions, D/R row blocks); 256 threads in a 16 x 16 grid.  Rows of
+// the state evolve independently, so a CTA carries R rows through all F steps;
+// R (64, 32 or 16) is picked at launch so that small head counts (Ulysses
+// shards) still fill the GPU.  Thread (rg, cg) owns the R/16 consecutive rows
+// from rg * R/16 and the column pairs {2 cg + 32 m, 2 cg + 1 + 32 m}: for a fixed
+// m the 16 column groups read one contiguous 128-byte line of T, so the shared
+// memory reads are conflict-free.  T_f is double-buffered: the 64 KB bulk copy of
+// T_{f+1} is issued at the start of step f and lands while step f computes.  The
+// R-row state sits transposed in shared memory (k-major) and each thread
+// accumulates on top of J_f with packed fp32 FMAs (fma.rn.f32x2).  Waits are
+// bounded (2 s).
+template <int D, int R>
 __global__ void __launch_bounds__(256) scan_kernel(const float* __restrict__ Tm,
                                                    const float* __restrict__ Jm,
                                                    const float* __restrict__ seed, int F, int H,
                                                    float* __restrict__ prefix,
                                                    float* __restrict__ suffix,
                                                    int* __restrict__ status) {
-  constexpr int R = 64, TC = D / 16;
+  constexpr int RT = R / 16, CP = D / 32;  // rows per thread, column pairs per thread
   extern __shared__ __align__(128) float sm[];
-  float* t_s = sm;                 // [D][D]  T_f
-  float* st_s = sm + D * D;        // [D][R]  state, transposed (k-major)
-  __shared__ __align__(8) uint64_t bar[1];
+  float* t_s = sm;                 // [2][D][D]  T_f, double buffer
+  float* st_s = sm + 2 * D * D;    // [D][R]     state, transposed (k-major)
+  __shared__ __align__(8) uint64_t bar[2];
   __shared__ int abort_flag;
   const int h = blockIdx.x, dir = blockIdx.y, rb = blockIdx.z;
   const int tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
-  const int r0 = rg * 4, c0 = cg * TC;
+  const int r0 = rg * RT;
   const int row0 = rb * R + r0;
   auto frame = [&](int step) { return dir == 0 ? step : F - 1 - step; };
+  auto col = [&](int m) { return 2 * cg + 32 * m; };
   auto issue = [&](int step) {
     const int64_t base = ((int64_t)frame(step) * H + h) * D * D;
-    sm100::mbar_arrive_expect_tx(&bar[0], D * D * 4);
-    sm100::bulk_load(t_s, Tm + base, D * D * 4, &bar[0]);
+    uint64_t* b = &bar[step & 1];
+    sm100::mbar_arrive_expect_tx(b, D * D * 4);
+    sm100::bulk_load(t_s + (step & 1) * D * D, Tm + base, D * D * 4, b);
   };
   if (tid == 0) {
     sm100::mbar_init(&bar[0], 1);
+    sm100::mbar_init(&bar[1], 1);
     abort_flag = 0;
     sm100::fence_barrier_init();
   }
@@ -300,60 +306,75 @@ __global__ void __launch_bounds__(256) scan_kernel(const float* __restrict__ Tm,
   __syncthreads();
   if (tid == 0) issue(0);
   float* bank = dir == 0 ? prefix : suffix;
-  float2 jn[4][TC / 2];
+  float2 jn[RT][CP];
   {
     const int64_t base = ((int64_t)frame(0) * H + h) * D * D;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RT; ++i)
 #pragma unroll
-      for (int j = 0; j < TC / 2; ++j)
-        jn[i][j] = *reinterpret_cast<const float2*>(Jm + base + (int64_t)(row0 + i) * D + c0 + 2 * j);
+      for (int m = 0; m < CP; ++m)
+        jn[i][m] = *reinterpret_cast<const float2*>(Jm + base + (int64_t)(row0 + i) * D + col(m));
   }
+  int issued = 1;
   for (int step = 0; step < F; ++step) {
     const int64_t base = ((int64_t)frame(step) * H + h) * D * D;
-    float2 acc[4][TC / 2];
+    if (tid == 0 && step + 1 < F) {  // buffer (step+1)&1 was last read in step-1: all done
+      issue(step + 1);
+      ++issued;
+    }
+    float2 acc[RT][CP];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RT; ++i)
 #pragma unroll
-      for (int j = 0; j < TC / 2; ++j) acc[i][j] = jn[i][j];
+      for (int m = 0; m < CP; ++m) acc[i][m] = jn[i][m];
     if (step + 1 < F) {  // J of the next frame, in flight during this step
       const int64_t nb = ((int64_t)frame(step + 1) * H + h) * D * D;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < RT; ++i)
 #pragma unroll
-        for (int j = 0; j < TC / 2; ++j)
-          jn[i][j] = *reinterpret_cast<const float2*>(Jm + nb + (int64_t)(row0 + i) * D + c0 + 2 * j);
+        for (int m = 0; m < CP; ++m)
+          jn[i][m] = *reinterpret_cast<const float2*>(Jm + nb + (int64_t)(row0 + i) * D + col(m));
     }
-    if (!__syncthreads_and(sm100::mbar_wait(&bar[0], step & 1, &abort_flag))) break;
-    const float* tb = t_s;
-#pragma unroll 2
+    if (!__syncthreads_and(sm100::mbar_wait(&bar[step & 1], (step >> 1) & 1, &abort_flag))) break;
+    const float* tb = t_s + (step & 1) * D * D;
+#pragma unroll 4
     for (int kk = 0; kk < D; ++kk) {
-      const float4 sv = *reinterpret_cast<const float4*>(st_s + kk * R + r0);
-      const float svv[4] = {sv.x, sv.y, sv.z, sv.w};
-      float2 tv[TC / 2];
+      float sv[RT];
+      if constexpr (RT == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(st_s + kk * R + r0);
+        sv[0] = v.x; sv[1] = v.y; sv[2] = v.z; sv[3] = v.w;
+      } else if constexpr (RT == 2) {
+        const float2 v = *reinterpret_cast<const float2*>(st_s + kk * R + r0);
+        sv[0] = v.x; sv[1] = v.y;
+      } else {
+        sv[0] = st_s[kk * R + r0];
+      }
+      float2 tv[CP];
 #pragma unroll
-      for (int j = 0; j < TC / 2; ++j) tv[j] = *reinterpret_cast<const float2*>(tb + kk * D + c0 + 2 * j);
+      for (int m = 0; m < CP; ++m) tv[m] = *reinterpret_cast<const float2*>(tb + kk * D + col(m));
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < RT; ++i)
 #pragma unroll
-        for (int j = 0; j < TC / 2; ++j) acc[i][j] = __ffma2_rn(make_float2(svv[i], svv[i]), tv[j], acc[i][j]);
+        for (int m = 0; m < CP; ++m) acc[i][m] = __ffma2_rn(make_float2(sv[i], sv[i]), tv[m], acc[i][m]);
     }
-    __syncthreads();  // every thread is done with T and st_s
-    if (tid == 0 && step + 1 < F) issue(step + 1);
+    __syncthreads();  // every thread is done with T_f and the old state
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RT; ++i)
 #pragma unroll
-      for (int j = 0; j < TC / 2; ++j) {
-        st_s[(c0 + 2 * j) * R + r0 + i] = acc[i][j].x;
-        st_s[(c0 + 2 * j + 1) * R + r0 + i] = acc[i][j].y;
-        *reinterpret_cast<float2*>(bank + base + (int64_t)(row0 + i) * D + c0 + 2 * j) = acc[i][j];
+      for (int m = 0; m < CP; ++m) {
+        st_s[col(m) * R + r0 + i] = acc[i][m].x;
+        st_s[(col(m) + 1) * R + r0 + i] = acc[i][m].y;
+        *reinterpret_cast<float2*>(bank + base + (int64_t)(row0 + i) * D + col(m)) = acc[i][m];
       }
     __syncthreads();
   }
-  if (abort_flag) {  // let an issued copy land before the CTA exits
-    const uint64_t t0 = sm100::globaltimer();
-    while (!sm100::mbar_try_wait(&bar[0], 0) && !sm100::mbar_try_wait(&bar[0], 1) &&
-           sm100::globaltimer() - t0 < sm100::kWaitLimitNs) {
+  if (abort_flag) {  // let every issued copy land before the CTA exits
+    for (int s = 0; s < issued && s < 2; ++s) {
+      const int last = issued - 1 - s;  // the newest copy on barrier last & 1
+      const uint64_t t0 = sm100::globaltimer();
+      while (!sm100::mbar_try_wait(&bar[last & 1], (last >> 1) & 1) &&
+             sm100::globaltimer() - t0 < sm100::kWaitLimitNs) {
+      }
     }
     if (tid == 0 && status) atomicExch(status, VDN_ERR_TIMEOUT);
   }
@@ -578,15 +599,29 @@ int launch_scan(const float* T, const float* J, const float* seed, int F, int H,
   VDN_CHECK_ARG(T && J && prefix && suffix, "null pointer");
   VDN_CHECK_ARG(aligned16(T) && aligned16(J) && aligned16(prefix) && aligned16(suffix),
                 "scan banks must be 16-byte aligned");
-  const dim3 grid(H, 2, d / 64);
-  const size_t smem = ((size_t)d * d + (size_t)d * 64) * sizeof(float);
+  int dev = 0, sms = 148;
+  VDN_CUDA_TRY(cudaGetDevice(&dev));
+  VDN_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  // Fewest rows per CTA (most CTAs) only when the head count leaves SMs idle.
+  int R = 64;
+  while (R > 16 && (int64_t)H * 2 * (d / R) < sms) R /= 2;
+  const dim3 grid(H, 2, d / R);
+  const size_t smem = ((size_t)2 * d * d + (size_t)d * R) * sizeof(float);
+#define VDN_SCAN(DD, RR)                                                                    \
+  do {                                                                                      \
+    if (int rc = set_smem(scan_kernel<DD, RR>, smem)) return rc;                            \
+    scan_kernel<DD, RR><<<grid, 256, smem, stream>>>(T, J, seed, F, H, prefix, suffix, nullptr); \
+  } while (0)
   if (d == 128) {
-    if (int rc = set_smem(scan_kernel<128>, smem)) return rc;
-    scan_kernel<128><<<grid, 256, smem, stream>>>(T, J, seed, F, H, prefix, suffix, nullptr);
+    if (R == 64) VDN_SCAN(128, 64);
+    else if (R == 32) VDN_SCAN(128, 32);
+    else VDN_SCAN(128, 16);
   } else {
-    if (int rc = set_smem(scan_kernel<64>, smem)) return rc;
-    scan_kernel<64><<<grid, 256, smem, stream>>>(T, J, seed, F, H, prefix, suffix, nullptr);
+    if (R == 64) VDN_SCAN(64, 64);
+    else if (R == 32) VDN_SCAN(64, 32);
+    else VDN_SCAN(64, 16);
   }
+#undef VDN_SCAN
   VDN_LAUNCH_CHECK("vda scan");
   return VDN_OK;
 }

@@ -144,8 +144,13 @@ class PeerExchange:
         self.frames, self.row_width = frames, row_width
         rows_bytes = _up(max(1, T * row_width * 2))
         sums_bytes = _up(max(1, self.P * frames * self.hidden * 4))
-        self.side = PeerBuffer(rows_bytes + sums_bytes, rt.rank, self.P, dev, rt.group)
+        self.side = PeerBuffer(rows_bytes + sums_bytes + _ALIGN, rt.rank, self.P, dev, rt.group)
         self._sums_off = rows_bytes
+        # device fence: one uint64 flag per rank in every rank's buffer
+        self._flags_off = rows_bytes + sums_bytes
+        self._epoch = 0
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.fence_mode = "device"
         # sequence-side destinations of every rank, for the scatter quantiser
         seq_ptrs = self.seq.ptrs
         self.att_dst = [(p + self.off[0], p + self.off[1]) for p in seq_ptrs]
@@ -191,12 +196,18 @@ class PeerExchange:
         self._publish(self._sums_off + self.rt.rank * slot, slot)
 
     def _publish(self, offset: int, nbytes: int) -> None:
+        """This rank's bytes [offset, offset + nbytes) of `side` into every peer, one launch."""
+        peers = [self.side.ptrs[p] + offset for p in range(self.P) if p != self.rt.rank]
         stream = _lib.stream_of(self.rt.device)
-        src = C.c_void_p(self.side.local + offset)
-        for p in range(self.P):
-            if p != self.rt.rank:
-                _lib.call("vdn_copy_async", C.c_void_p(self.side.ptrs[p] + offset), src,
-                          C.c_size_t(nbytes), stream)
+        src = self.side.local + offset
+        body = nbytes // 16 * 16
+        if body:
+            _lib.call("vdn_peer_broadcast", C.c_void_p(src), C.c_size_t(body), len(peers),
+                      (C.c_void_p * len(peers))(*peers), stream)
+        if nbytes > body:  # a ragged tail (odd row widths): copy engines
+            for dst in peers:
+                _lib.call("vdn_copy_async", C.c_void_p(dst + body), C.c_void_p(src + body),
+                          C.c_size_t(nbytes - body), stream)
 
     # ------------------------------------------------------------ operations
     def gather_rows_async(self, x: torch.Tensor):
@@ -221,8 +232,23 @@ class PeerExchange:
 
     def fence(self) -> None:
         """Stream-ordered rendezvous: every rank's earlier kernels (and their peer
-        stores) complete before any rank's later kernels run."""
-        dist.all_reduce(self._flag, group=self.rt.group)
+        stores) complete before any rank's later kernels run.  "device": one
+        vdn_peer_fence launch (flags in peer memory, bounded waits); "nccl": a
+        one-element NCCL all-reduce."""
+        if self.fence_mode == "nccl":
+            dist.all_reduce(self._flag, group=self.rt.group)
+            return
+        self._epoch += 1
+        flags = (C.c_void_p * self.P)(*[p + self._flags_off for p in self.side.ptrs])
+        _lib.call("vdn_peer_fence", self.P, flags, C.c_void_p(self.side.local + self._flags_off),
+                  self.rt.rank, C.c_uint64(self._epoch), _lib.ptr(self.status),
+                  _lib.stream_of(self.rt.device))
+
+    def check(self) -> None:
+        """Raise RuntimeError if a device fence timed out (reads a device flag: syncs)."""
+        if int(self.status.item()):
+            self.status.zero_()
+            raise RuntimeError("Ulysses peer fence timed out waiting for another rank")
 
     def scatter_quantize(self, src: torch.Tensor, dst) -> None:
         """src [T, H/P, d] bf16 view (last dim contiguous) -> owners' MXFP8 operands."""

@@ -182,10 +182,14 @@ class UlyssesRuntime:
         return torch.cat([chunks[r, :n] for r, n in enumerate(self.splits)], dim=0)
 
     def local_frame_sums(self, local_x: torch.Tensor, num_frames: int, tokens_per_frame: int,
-                         video_start: int = 0) -> torch.Tensor:
+                         video_start: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
         """Per-frame fp32 sums of this rank's rows, one contiguous slice per frame
-        (deterministic; ulysses_runtime.py:606-635)."""
-        sums = torch.zeros(num_frames, local_x.shape[-1], device=local_x.device, dtype=torch.float32)
+        (deterministic; ulysses_runtime.py:606-635).  `out` [num_frames, W] fp32."""
+        if out is None:
+            sums = torch.zeros(num_frames, local_x.shape[-1], device=local_x.device, dtype=torch.float32)
+        else:
+            sums = out
+            sums.zero_()
         v0, v1 = video_start, video_start + num_frames * tokens_per_frame
         lo, hi = max(self.local_start, v0), min(self.local_end, v1)
         if hi <= lo:
@@ -195,7 +199,8 @@ class UlyssesRuntime:
         for frame in range(first, last + 1):
             a = max(lo, v0 + frame * tokens_per_frame)
             b = min(hi, v0 + (frame + 1) * tokens_per_frame)
-            sums[frame] = local_x[a - self.local_start:b - self.local_start].sum(0, dtype=torch.float32)
+            torch.sum(local_x[a - self.local_start:b - self.local_start], 0, dtype=torch.float32,
+                      out=sums[frame])
         return sums
 
     def video_frame_mean_async(self, local_x, num_frames, tokens_per_frame, video_start=0):
