@@ -87,12 +87,13 @@ def test_window_softmax_matches_exact_window(cuda):
     assert np.array_equal(codes[0].cpu().numpy(), rq) and np.array_equal(codes[1].cpu().numpy(), rs)
 
 
+@pytest.mark.parametrize("m", [300, 500])   # 500 rows pad to 512: the CTA-pair kernel
 @torch.no_grad()
-def test_fused_gemm_dual_k_and_gated_residual(cuda):
+def test_fused_gemm_dual_k_and_gated_residual(cuda, m):
     from vdn_b200 import _lib
     from vdn_b200.mxfp8_quant import quantize_activation
     g = torch.Generator(device=cuda).manual_seed(9)
-    m, n, k1, k2 = 300, 384, 256, 512
+    n, k1, k2 = 384, 256, 512
     x1 = torch.randn(m, k1, device=cuda, generator=g).bfloat16()
     x2 = torch.randn(m, k2, device=cuda, generator=g).bfloat16()
     w1 = (torch.randn(n, k1, device=cuda, generator=g) * 0.05).bfloat16()

@@ -147,7 +147,7 @@ def test_config1_shapes_sampled_rows(cuda, n, k):
     torch.testing.assert_close(y[rows], want, rtol=.01, atol=.016)
 
 
-@pytest.mark.parametrize("rows,row0", [(300, 0), (257, 41)])
+@pytest.mark.parametrize("rows,row0", [(300, 0), (257, 41), (500, 3)])   # 500: CTA-pair kernel
 def test_scatter_epilogue_routes_chunks(cuda, rows, row0):
     """vdn_mxfp8_gemm_scatter: every 128-column chunk lands at its table address,
     row by row, identical to the plain GEMM output (bias included; ragged rows)."""
@@ -175,13 +175,14 @@ def test_scatter_epilogue_routes_chunks(cuda, rows, row0):
     assert bool((untouched.float() == -7.0).all())
 
 
+@pytest.mark.parametrize("rows", [300, 500])   # 500 rows pad to 512: the CTA-pair kernel
 @pytest.mark.parametrize("act", ["tanh", "none"])
-def test_gemm_act_quantize_matches_unfused(cuda, act):
+def test_gemm_act_quantize_matches_unfused(cuda, act, rows):
     """vdn_mxfp8_gemm_act_quantize == vdn_mxfp8_gemm (bf16 + bias) followed by the
     GELU quantiser, bit for bit; padded rows come out as zero codes and scales."""
     from vdn_b200 import _lib
     from vdn_b200.mxfp8_kernels import launch_gelu_quantize
-    rows, n, k = 300, 384, 512
+    n, k = 384, 512
     xq, xs = quantised(rows, k, cuda, 41)
     wq, ws = quantised(n, k, cuda, 42, scale=0.05)
     bias = torch.randn(n, device=cuda).bfloat16()

@@ -25,6 +25,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <stdlib.h>
 
 namespace vdn {
 namespace gemm {
@@ -78,6 +79,17 @@ struct Params {
   uint8_t* s_out;
   int* status;
 };
+
+__device__ __forceinline__ void tile_coords_g(int t, int m_tiles, int n_tiles, int group, int& mb,
+                                              int& nb) {
+  const int per_group = group * n_tiles;
+  const int g = t / per_group;
+  const int first = g * group;
+  const int gsize = min(group, m_tiles - first);
+  const int local = t - g * per_group;
+  mb = first + local % gsize;
+  nb = local / gsize;
+}
 
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mb, int& nb) {
   const int per_group = GROUP_M * n_tiles;
@@ -459,6 +471,260 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0 && *abort_flag && p.status) atomicExch(p.status, VDN_ERR_TIMEOUT);
 }
 
+// ------------------------------------------------------------ CTA-pair kernel
+// The same GEMM with a 256 x 256 tile per CTA pair (a cluster of two CTAs on
+// neighbouring SMs, tcgen05 cta_group::2): each CTA stages its 128 rows of A and
+// its 128-row half of B per 256-deep K block (64 KB; per FLOP a third fewer bytes
+// from L2 than the single-CTA tile), the even CTA issues one 256 x 256 x 32
+// block-scaled MMA over both CTAs' shared memory per 32 K, and each CTA's TMEM
+// receives its own 128 x 256 accumulator.  The 256-deep stage carries six scale
+// atoms copied to TMEM back to back ahead of eight MMAs: scale copies and MMAs
+// share the tensor pipe in order, and every switch between them costs a bubble.
+// Both CTAs' TMA loads (operands and scale atoms, no multicast) signal the
+// leader's full barrier; the leader's MMA commits free the stage in both CTAs;
+// both CTAs' epilogues drain their own accumulator and report to the leader.
+constexpr int P_BK = 256;             // K per stage: two 128-byte swizzled sub-tiles
+constexpr int P_STAGES = 3;
+constexpr int P_SUB = 128 * 128;      // one 128-row x 128-byte sub-tile
+constexpr int P_A_BYTES = 2 * P_SUB;  // 32 KB
+constexpr int P_B_BYTES = 2 * P_SUB;  // 32 KB
+constexpr int P_SF_STAGE = 512 * 6;   // SFA: 2 K-atoms; SFB: 2 N-halves x 2 K-atoms
+constexpr int P_SF_COLS = 24;         // TMEM scale columns per stage
+constexpr int P_GROUP_M = 8;         // 256-row tiles per group
+constexpr size_t P_SMEM_BYTES =
+    1024 + P_STAGES * (P_A_BYTES + P_B_BYTES + P_SF_STAGE) + BAR_BYTES + 8 * STAGE_BYTES;
+static_assert(P_SMEM_BYTES <= 232448, "shared memory per CTA");
+static_assert((2 * P_STAGES + 3) * 8 + 8 <= BAR_BYTES, "barrier region");
+static_assert(256 + P_STAGES * P_SF_COLS <= TMEM_COLS, "scale columns");
+constexpr uint64_t kDrainNs = 200000;  // abort path: time for a CTA's own copies to land
+
+struct PairMaps {
+  CUtensorMap sfa, sfb, sfa2, sfb2;  // scale atoms as [atoms, 128] uint32 rows
+};
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    mxfp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                           const __grid_constant__ CUtensorMap tmap_b,
+                           const __grid_constant__ CUtensorMap tmap_a2,
+                           const __grid_constant__ CUtensorMap tmap_b2,
+                           const __grid_constant__ PairMaps sf, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + P_STAGES * P_A_BYTES;
+  uint8_t* sSF = sB + P_STAGES * P_B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSF + P_STAGES * P_SF_STAGE);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* acc_full = empty + P_STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* mma_done = acc_empty + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint8_t* stage_base = sSF + P_STAGES * P_SF_STAGE + BAR_BYTES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair_id = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 16);  // one arrival per epilogue warp of both CTAs
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tmap_a);
+    prefetch_tensormap(&tmap_b);
+    prefetch_tensormap(&sf.sfa);
+    prefetch_tensormap(&sf.sfb);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_holder, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barrier inits visible to the peer before any remote arrive / copy
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int num_tiles = p.m_tiles * p.n_tiles;  // m_tiles counts 256-row tiles here
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      const uint32_t full_leader = mapa_shared(full, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t pending = 0, pending_phase = 0;
+      bool issued = false;
+      for (int t = pair_id; t < num_tiles && !*abort_flag; t += npairs) {
+        int mb, nb;
+        tile_coords_g(t, p.m_tiles, p.n_tiles, P_GROUP_M, mb, nb);
+        const bool has_b1 = 2 * nb + 1 < p.n_groups;
+        const int kb_total = p.k_blocks + p.k_blocks2;
+        for (int kbt = 0; kbt < kb_total; ++kbt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
+          const bool second = kbt >= p.k_blocks;
+          const int kb = second ? kbt - p.k_blocks : kbt;
+          const int kbn = 2 * (second ? p.k_blocks2 : p.k_blocks);  // 128-deep atoms per row block
+          const CUtensorMap* ma = second ? &tmap_a2 : &tmap_a;
+          const CUtensorMap* mbm = second ? &tmap_b2 : &tmap_b;
+          const CUtensorMap* msa = second ? &sf.sfa2 : &sf.sfa;
+          const CUtensorMap* msb = second ? &sf.sfb2 : &sf.sfb;
+          // kbn counts 128-deep scale atoms; this stage covers atoms 2 kb, 2 kb + 1.
+          const uint32_t bytes = P_A_BYTES + P_B_BYTES + (has_b1 ? 6 : 4) * 512;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * bytes);
+          const uint32_t fb = full_leader + stage * 8;
+          const int arow = (mb * 2 + (int)rank) * 128, brow = (nb * 2 + (int)rank) * 128;
+          uint8_t* a_s = sA + stage * P_A_BYTES;
+          uint8_t* b_s = sB + stage * P_B_BYTES;
+          tma_load_2d_pair(a_s, ma, fb, kb * P_BK, arow);
+          tma_load_2d_pair(a_s + P_SUB, ma, fb, kb * P_BK + 128, arow);
+          tma_load_2d_pair(b_s, mbm, fb, kb * P_BK, brow);
+          tma_load_2d_pair(b_s + P_SUB, mbm, fb, kb * P_BK + 128, brow);
+          uint8_t* sfs = sSF + stage * P_SF_STAGE;
+          tma_load_2d_pair(sfs, msa, fb, 0, (mb * 2 + (int)rank) * kbn + 2 * kb);
+          tma_load_2d_pair(sfs + 1024, msb, fb, 0, (2 * nb) * kbn + 2 * kb);
+          if (has_b1) tma_load_2d_pair(sfs + 2048, msb, fb, 0, (2 * nb + 1) * kbn + 2 * kb);
+          issued = true;
+          pending |= 1u << stage;
+          pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag && issued) {
+        // Let copies already issued land before the CTA can exit.  The leader
+        // watches its full barriers; the peer's copies signal the leader's
+        // barriers, so it waits a fixed bounded time instead.
+        if (leader) {
+          for (int s = 0; s < P_STAGES; ++s) {
+            if (!(pending >> s & 1)) continue;
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(&full[s], (pending_phase >> s) & 1) && globaltimer() - t0 < kWaitLimitNs) {
+            }
+          }
+        } else {
+          const uint64_t t0 = globaltimer();
+          while (globaltimer() - t0 < kDrainNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ----------------------------------------------------------------- MMA
+      // Per 256-deep stage: six scale-atom copies to TMEM, then eight MMAs.
+      // (Copying the next stage's scales ahead of the current MMAs was measured
+      // slower: it makes every MMA batch wait for the following stage's data.)
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool issued = false;
+      for (int t = pair_id; t < num_tiles; t += npairs) {
+        if (!mbar_wait(acc_empty, acc_phase ^ 1, abort_flag)) break;
+        tc_fence_after();
+        bool ok = true;
+        const int kb_total = p.k_blocks + p.k_blocks2;
+        for (int kb = 0; kb < kb_total; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // TMEM scale columns of the stage: SFA atom h at +4h; SFB of K-atom h at
+          // +8 + 8h (N rows 0-127) and +12 + 8h (N rows 128-255).
+          const uint32_t sf = tmem + SF_COL + stage * P_SF_COLS;
+          const uint32_t sf_smem = smem_u32(sSF + stage * P_SF_STAGE);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            tmem_cp_pair_32x128_x4(sf + 4 * h, desc_sf_atom(sf_smem + 512 * h));
+            tmem_cp_pair_32x128_x4(sf + 8 + 8 * h, desc_sf_atom(sf_smem + 1024 + 512 * h));
+            tmem_cp_pair_32x128_x4(sf + 12 + 8 * h, desc_sf_atom(sf_smem + 2048 + 512 * h));
+          }
+          const uint32_t a0 = smem_u32(sA + stage * P_A_BYTES), b0 = smem_u32(sB + stage * P_B_BYTES);
+#pragma unroll
+          for (int k = 0; k < P_BK / 32; ++k) {
+            const int h = k >> 2, kk = k & 3;
+            const uint64_t adesc = desc_k_sw128(a0 + h * P_SUB) + 2 * kk;
+            const uint64_t bdesc = desc_k_sw128(b0 + h * P_SUB) + 2 * kk;
+            mma_mxf8_pair(tmem + ACC_COL, adesc, bdesc, idesc_mxf8(256, BN, kk),
+                          (sf + 4 * h) | ((uint32_t)kk << 30), (sf + 8 + 8 * h) | ((uint32_t)kk << 30),
+                          (kb | k) != 0);
+          }
+          issued = true;
+          tc_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(acc_full, 0x3);
+        acc_phase ^= 1;
+      }
+      if (*abort_flag && issued) {
+        tc_commit_pair(mma_done, 0x1);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(mma_done, 0) && globaltimer() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = quad * 32 + lane;
+    const uint32_t acc_empty_leader = mapa_shared(acc_empty, 0);
+    uint32_t acc_phase = 0;
+    for (int t = pair_id; t < num_tiles; t += npairs) {
+      int mb, nb;
+      tile_coords_g(t, p.m_tiles, p.n_tiles, P_GROUP_M, mb, nb);
+      const int64_t row_base = (int64_t)(mb * 2 + (int)rank) * 128;
+      const int64_t row = row_base + row_in_tile;
+      const int64_t col0 = (int64_t)nb * BN + half * 128;
+      const bool live = row < p.rows_out && col0 < p.n;
+      if (EPI == EPI_STORE && live && p.resid)
+        prefetch_l2_row(p.resid + row * p.ldr + col0, p.n - col0 < 128 ? p.n - col0 : 128);
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, acc_phase, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t r[128];
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + ACC_COL + half * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(taddr + c * 32, r + 32 * c);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(acc_empty);
+        else mbar_arrive_cluster(acc_empty_leader);
+      }
+      acc_phase ^= 1;
+      if constexpr (EPI == EPI_QUANT || EPI == EPI_QUANT_GELU) {
+        if (col0 < p.n) store_row_quant<EPI == EPI_QUANT_GELU>(p, r, row, col0);
+      } else if constexpr (EPI == EPI_SCATTER) {
+        if (col0 < p.n) store_rows_staged(p, r, row_base + quad * 32, lane, col0, stage_base + (warp - 2) * STAGE_BYTES);
+      } else {
+        if (live) store_row(p, r, row, col0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs and every remote arrive are done in both CTAs
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+  cluster_sync();  // neither CTA leaves while the pair's TMEM or barriers are in use
+  if (threadIdx.x == 0 && *abort_flag && p.status) atomicExch(p.status, VDN_ERR_TIMEOUT);
+}
+
 // -------------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -487,8 +753,25 @@ static int make_map(CUtensorMap* map, const void* base, int64_t k_pad, int64_t r
   return VDN_OK;
 }
 
+// Scale atoms of a padded operand as a 2D tensor: [atoms, 128] uint32 rows of
+// 512 bytes (one SWIZZLE_32_4_4 atom per row), loaded two atoms per copy.
+static int make_sf_map(CUtensorMap* map, const void* base, int64_t atoms) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(VDN_ERR_RUNTIME, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {128, (cuuint64_t)atoms};
+  cuuint64_t strides[1] = {512};
+  cuuint32_t box[2] = {128, 2};  // two consecutive K atoms: one 256-deep stage
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VDN_ERR_RUNTIME, "cuTensorMapEncodeTiled (scales) failed (%d)", (int)r);
+  return VDN_OK;
+}
+
 struct DeviceInfo {
   int sms = 0;
+  int pairs = 0;  // co-resident CTA pairs of the pair kernel (0: pair kernel unavailable)
   bool smem_set = false;
 };
 
@@ -510,6 +793,30 @@ static int device_info(DeviceInfo** out) {
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
     VDN_CUDA_TRY(cudaFuncSetAttribute(mxfp8_gemm_kernel<EPI_QUANT_GELU>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    const void* pair_kernels[4] = {(const void*)mxfp8_gemm_pair_kernel<EPI_STORE>,
+                                   (const void*)mxfp8_gemm_pair_kernel<EPI_SCATTER>,
+                                   (const void*)mxfp8_gemm_pair_kernel<EPI_QUANT>,
+                                   (const void*)mxfp8_gemm_pair_kernel<EPI_QUANT_GELU>};
+    for (const void* k : pair_kernels)
+      VDN_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM_BYTES));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, (const void*)mxfp8_gemm_pair_kernel<EPI_STORE>, &cfg) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      clusters = 0;
+    }
+    d.pairs = clusters;
     d.smem_set = true;
   }
   *out = &d;
@@ -594,6 +901,45 @@ static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, 
   p.act = act;
   p.q_out = q_out;
   p.s_out = s_out;
+  static const bool pair_off = [] {
+    const char* e = getenv("VDN_GEMM_PAIR");
+    return e && e[0] == '0';
+  }();
+  if (!pair_off && info->pairs > 0 && m_pad % 256 == 0 && k_pad % 256 == 0 && k_pad2 % 256 == 0) {
+    PairMaps sf;
+    const int64_t kb1 = k_pad / BK, kb2 = k_pad2 / BK;
+    if (int rc = make_map(&ma, xq, k_pad, m_pad, 128)) return rc;
+    if (int rc = make_map(&mb, wq, k_pad, n_pad, 128)) return rc;
+    if (int rc = make_sf_map(&sf.sfa, xs, (m_pad / 128) * kb1)) return rc;
+    if (int rc = make_sf_map(&sf.sfb, ws, (n_pad / 128) * kb1)) return rc;
+    if (k_pad2) {
+      if (int rc = make_map(&ma2, xq2, k_pad2, m_pad, 128)) return rc;
+      if (int rc = make_map(&mb2, wq2, k_pad2, n_pad, 128)) return rc;
+      if (int rc = make_sf_map(&sf.sfa2, xs2, (m_pad / 128) * kb2)) return rc;
+      if (int rc = make_sf_map(&sf.sfb2, ws2, (n_pad / 128) * kb2)) return rc;
+    } else {
+      ma2 = ma;
+      mb2 = mb;
+      sf.sfa2 = sf.sfa;
+      sf.sfb2 = sf.sfb;
+    }
+    p.m_tiles = (int)(m_pad / 256);
+    p.k_blocks = (int)(k_pad / P_BK);
+    p.k_blocks2 = (int)(k_pad2 / P_BK);
+    const int tiles = p.m_tiles * p.n_tiles;
+    const int pairs = tiles < info->pairs ? tiles : info->pairs;
+    const dim3 grid(2 * pairs);
+    if (q_out && act == VDN_ACT_GELU_TANH)
+      mxfp8_gemm_pair_kernel<EPI_QUANT_GELU><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, p);
+    else if (q_out)
+      mxfp8_gemm_pair_kernel<EPI_QUANT><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, p);
+    else if (chunk_dst)
+      mxfp8_gemm_pair_kernel<EPI_SCATTER><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, p);
+    else
+      mxfp8_gemm_pair_kernel<EPI_STORE><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, p);
+    VDN_LAUNCH_CHECK("mxfp8 gemm (CTA pairs)");
+    return VDN_OK;
+  }
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < info->sms ? tiles : info->sms;
   if (q_out && act == VDN_ACT_GELU_TANH)
