@@ -435,8 +435,15 @@ def bench_block(args, torch, dist, rank, world):
     del x_full
     rows = hi - lo
 
-    def step():
-        return block(x, temb, F, S, runtime)
+    if args.eager:
+        def step():
+            return block(x, temb, F, S, runtime)
+    else:
+        from vdn_b200.block import BlockGraph
+        graph = BlockGraph(block, x, temb, F, S, runtime)
+
+        def step():
+            return graph.replay()
 
     with ClockSampler(dev.index) as clk:
         ms = time_steps(torch, step, args.steps, args.warmup, dist, stream)
@@ -472,8 +479,12 @@ def bench_block(args, torch, dist, rank, world):
     x_dev = torch.empty_like(x)
 
     def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        y = block(x_dev, temb, F, S, runtime)
+        if args.eager:
+            x_dev.copy_(x_host, non_blocking=True)
+            y = block(x_dev, temb, F, S, runtime)
+        else:  # the public graph API: host rows into the graph's static input
+            graph.x.copy_(x_host, non_blocking=True)
+            y = graph.replay()
         out_host.copy_(y, non_blocking=True)
 
     e2e_steps = max(2, args.steps // 2)
@@ -493,6 +504,7 @@ def bench_block(args, torch, dist, rank, world):
         "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2},
         "gpu_launches": block.launches_per_forward(world) * args.steps,
+        "launch": "eager" if args.eager else "cuda_graph",
         "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (QKV, %d x 15360 x 5120)" % rows,
                      "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / fp8_peak, 4), "traffic": None,
@@ -552,6 +564,7 @@ def main():
     ap.add_argument("--frames", type=int, default=0, help="vda: frame-count override (small case)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="block: launch eagerly instead of a CUDA graph")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -197,15 +197,18 @@ int vdn_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream
  * launch: the all-gather of small per-token side inputs. */
 int vdn_peer_broadcast(const void* src, size_t bytes, int ndst, void* const* dsts, cudaStream_t stream);
 
-/* Cross-GPU rendezvous on the stream: publishes `epoch` (> 0, increasing by
- * call) into slot `rank` of every rank's uint64 flag array (flag_arrays[p],
- * host array of device pointers, p < nranks <= 8; a system-scope release after
- * all earlier work of the stream) and waits until all nranks slots of this
- * rank's array (my_flags) hold at least `epoch`.  Later work on the stream then
- * sees every rank's stores made before its matching call.  Each wait gives up
- * after 2 s and sets *status (optional device int) to VDN_ERR_TIMEOUT. */
+/* Cross-GPU rendezvous on the stream: the epoch is *counter + 1 (counter: this
+ * rank's uint64 on the device, zero-initialised, advanced by each call, so the
+ * launch can be replayed from a CUDA graph).  Publishes the epoch into slot
+ * `rank` of every rank's uint64 flag array (flag_arrays[p], host array of device
+ * pointers, p < nranks <= 8; a system-scope release after all earlier work of
+ * the stream) and waits until all nranks slots of this rank's array (my_flags)
+ * hold at least the epoch.  Later work on the stream then sees every rank's
+ * stores made before its matching call.  Every rank makes the same sequence of
+ * calls.  Each wait gives up after 2 s and sets *status (optional device int) to
+ * VDN_ERR_TIMEOUT. */
 int vdn_peer_fence(int nranks, void* const* flag_arrays, const void* my_flags, int rank,
-                   uint64_t epoch, int* status, cudaStream_t stream);
+                   uint64_t* counter, int* status, cudaStream_t stream);
 
 /* Heads -> sequence return of a head-sharded bf16 output as MXFP8: element
  * (t, j, e) of src (t < rows, j < heads_local, e < d) sits at t*row_stride +

@@ -114,3 +114,23 @@ def test_fused_gemm_dual_k_and_gated_residual(cuda, m):
     r = (acc.float().bfloat16().float() + bias.float().cpu()).bfloat16().float()
     want = (resid.float().cpu() + (gate.float().cpu() * r).bfloat16().float()).bfloat16()
     torch.testing.assert_close(y.cpu(), want, rtol=.01, atol=.02)
+
+
+@torch.no_grad()
+def test_block_graph_replay_matches_eager(cuda):
+    """BlockGraph: replays of the captured forward equal eager forwards, for
+    new inputs copied into the static buffer."""
+    from vdn_b200.block import BlockGraph
+    cfg, block = _small_block(cuda, seed=2)
+    frames, tokens = 4, 64
+    g = torch.Generator().manual_seed(77)
+    xs = [torch.randn(frames * tokens, cfg.hidden, generator=g).bfloat16().to(cuda) for _ in range(2)]
+    temb = torch.randn(cfg.hidden, generator=g).to(cuda)
+    want = [block(x, temb, frames, tokens).clone() for x in xs]
+    static = xs[0].clone()
+    graph = BlockGraph(block, static, temb, frames, tokens)
+    for x, w in zip(xs, want):
+        static.copy_(x)
+        out = graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, w)

@@ -53,6 +53,17 @@ def main():
             gathered = rt.gather_sequence(shard)
             if gathered.shape != full.shape:
                 failures.append(("gather shape", tuple(gathered.shape)))
+        # The peer path replayed from a CUDA graph (device-counter fences).
+        from vdn_b200.block import BlockGraph
+        local = x[rt.local_start:rt.local_end].contiguous()
+        graph = BlockGraph(block, local, temb, frames, tokens, rt)
+        for _ in range(2):
+            out = graph.replay()
+            torch.cuda.synchronize()
+            if not torch.equal(out, shards["peer"]):
+                d = (out.float() - shards["peer"].float()).abs().max().item()
+                failures.append(("graph replay", frames, tokens, d))
+        del graph
         for ex in rt._exchanges.values():
             ex.check()                              # no device fence timed out
         # The two exchanges move the same bytes: identical block outputs.

@@ -50,7 +50,7 @@ SIGNATURES = {
     "vdn_ipc_close": (_i32, [_p]),
     "vdn_copy_async": (_i32, [_p, _p, C.c_size_t, _p]),
     "vdn_peer_broadcast": (_i32, [_p, C.c_size_t, _i32, _p, _p]),
-    "vdn_peer_fence": (_i32, [_i32, _p, _p, _i32, C.c_uint64, _p, _p]),
+    "vdn_peer_fence": (_i32, [_i32, _p, _p, _i32, _p, _p, _p]),
     "vdn_mxfp8_quantize_scatter": (_i32, [_p, _i64, _i32, _i32, _i64, _i64, _i32, _i64, _i32, _p, _p, _p,
                                           _p, _p]),
     "vdn_window_merge": (_i32, [_i32, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _p, _i64, _i64, _p,

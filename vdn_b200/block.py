@@ -36,7 +36,7 @@ from .mxfp8_kernels import launch_prenorm_quantize
 from .mxfp8_quant import quantize_cpu, quantize_activation
 from .window import window_softmax
 
-__all__ = ["HybridBlock", "BlockConfig"]
+__all__ = ["HybridBlock", "BlockConfig", "BlockGraph"]
 
 
 class BlockConfig:
@@ -284,3 +284,37 @@ class HybridBlock(nn.Module):
                   flat.stride(0), d, 2 * d, _lib.ptr(q), _lib.ptr(s), None,
                   _lib.stream_of(flat.device))
         return q, s
+
+
+class BlockGraph:
+    """One block forward captured as a CUDA graph: the launch-bound host work of
+    the ~50 launches per forward is replayed by the driver in one call.
+
+    Inputs and output are static tensors: copy new rows into `x` (and `temb`),
+    call replay(), read `out`.  The eager forwards run first on a side stream
+    create every lazily built resource (library state, cuDNN plans, the Ulysses
+    peer exchange), which must not happen during capture.  Only the peer
+    exchange runs under a graph at world_size > 1 (its fences take their epoch
+    from a device counter, so replays stay in step across ranks).
+    """
+
+    def __init__(self, block: HybridBlock, x, temb, frames, tokens, runtime=None, warmup=2):
+        if runtime is not None and runtime.world_size > 1 and runtime.exchange_mode != "peer":
+            raise ValueError("CUDA-graph capture needs the peer exchange at world_size > 1")
+        self.block, self.x, self.temb = block, x, temb
+        self.frames, self.tokens, self.runtime = frames, tokens, runtime
+        dev = x.device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                block(x, temb, frames, tokens, runtime)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = block(x, temb, frames, tokens, runtime)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out

@@ -113,15 +113,18 @@ __global__ void __launch_bounds__(256) broadcast_kernel(const uint4* __restrict_
   }
 }
 
-// Cross-GPU rendezvous: thread p publishes `epoch` into slot `rank` of rank p's
-// flag array (a system-scope release, ordered after every earlier kernel of this
-// stream), then waits (acquire, bounded by kFenceLimitNs) until every rank has
-// published `epoch` into this rank's array.  A timeout sets *status.
+// Cross-GPU rendezvous: the epoch is this rank's counter + 1 (a device word, so
+// the same launch can be replayed from a CUDA graph).  Thread p publishes it into
+// slot `rank` of rank p's flag array (a system-scope release, ordered after every
+// earlier kernel of this stream), then waits (acquire, bounded by kFenceLimitNs)
+// until every rank has published it into this rank's array; thread 0 then
+// stores the new epoch into the counter.  A timeout sets *status.
 constexpr uint64_t kFenceLimitNs = 2000000000ull;
 
 __global__ void peer_fence_kernel(const PeerSet flags, const uint64_t* my_flags, int rank,
-                                  uint64_t epoch, int* status) {
+                                  uint64_t* counter, int* status) {
   const int p = threadIdx.x;
+  const uint64_t epoch = *counter + 1;
   if (p < flags.n) {
     uint64_t* slot = reinterpret_cast<uint64_t*>(flags.ptr[p]) + rank;
     asm volatile("fence.sc.sys;\n\tst.release.sys.global.u64 [%0], %1;" ::"l"(slot), "l"(epoch) : "memory");
@@ -140,6 +143,7 @@ __global__ void peer_fence_kernel(const PeerSet flags, const uint64_t* my_flags,
     }
   }
   __syncthreads();
+  if (p == 0) *counter = epoch;
 }
 
 }  // namespace vdn
@@ -218,9 +222,10 @@ int vdn_peer_broadcast(const void* src, size_t bytes, int ndst, void* const* dst
 }
 
 int vdn_peer_fence(int nranks, void* const* flag_arrays, const void* my_flags, int rank,
-                   uint64_t epoch, int* status, cudaStream_t stream) {
+                   uint64_t* counter, int* status, cudaStream_t stream) {
   VDN_CHECK_ARG(nranks >= 1 && nranks <= kMaxRanks, "nranks must lie in [1, %d]", kMaxRanks);
-  VDN_CHECK_ARG(rank >= 0 && rank < nranks && flag_arrays && my_flags && epoch > 0, "bad fence arguments");
+  VDN_CHECK_ARG(rank >= 0 && rank < nranks && flag_arrays && my_flags && counter, "bad fence arguments");
+  VDN_CHECK_ARG((reinterpret_cast<uintptr_t>(counter) & 7) == 0, "counter must be 8-byte aligned");
   PeerSet set;
   set.n = nranks;
   for (int p = 0; p < kMaxRanks; ++p) set.ptr[p] = nullptr;
@@ -229,7 +234,7 @@ int vdn_peer_fence(int nranks, void* const* flag_arrays, const void* my_flags, i
                   "flag arrays must be non-null and 8-byte aligned");
     set.ptr[p] = static_cast<uint8_t*>(flag_arrays[p]);
   }
-  peer_fence_kernel<<<1, 32, 0, stream>>>(set, static_cast<const uint64_t*>(my_flags), rank, epoch, status);
+  peer_fence_kernel<<<1, 32, 0, stream>>>(set, static_cast<const uint64_t*>(my_flags), rank, counter, status);
   VDN_LAUNCH_CHECK("peer fence");
   return VDN_OK;
 }

@@ -146,9 +146,9 @@ class PeerExchange:
         sums_bytes = _up(max(1, self.P * frames * self.hidden * 4))
         self.side = PeerBuffer(rows_bytes + sums_bytes + _ALIGN, rt.rank, self.P, dev, rt.group)
         self._sums_off = rows_bytes
-        # device fence: one uint64 flag per rank in every rank's buffer
+        # device fence: one uint64 flag per rank in every rank's buffer (bytes 0-63)
+        # and this rank's epoch counter (bytes 128-135), zero-initialised
         self._flags_off = rows_bytes + sums_bytes
-        self._epoch = 0
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.fence_mode = "device"
         # sequence-side destinations of every rank, for the scatter quantiser
@@ -238,10 +238,9 @@ class PeerExchange:
         if self.fence_mode == "nccl":
             dist.all_reduce(self._flag, group=self.rt.group)
             return
-        self._epoch += 1
         flags = (C.c_void_p * self.P)(*[p + self._flags_off for p in self.side.ptrs])
         _lib.call("vdn_peer_fence", self.P, flags, C.c_void_p(self.side.local + self._flags_off),
-                  self.rt.rank, C.c_uint64(self._epoch), _lib.ptr(self.status),
+                  self.rt.rank, C.c_void_p(self.side.local + self._flags_off + 128), _lib.ptr(self.status),
                   _lib.stream_of(self.rt.device))
 
     def check(self) -> None:
