@@ -119,6 +119,36 @@ class HybridBlock(nn.Module):
                   _lib.ptr(self._status), _lib.stream_of(out.device))
         return out
 
+    def _side(self, device):
+        """The branch-overlap stream of this device (the reference's vda_on_side_stream,
+        src/inference/utils/vda_overlap.py:7-44): the VDA branch runs there while the
+        window softmax runs on the caller's stream."""
+        st = getattr(self, "_side_streams", None)
+        if st is None:
+            st = self._side_streams = {}
+        if device.index not in st:
+            st[device.index] = torch.cuda.Stream(device)
+        return st[device.index]
+
+    def _vda_side(self, fn, device):
+        """Run fn() on the side stream after the caller's pending work; returns
+        (result, join) where join() makes the caller's stream wait for it."""
+        main = torch.cuda.current_stream(device)
+        side = self._side(device)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            out = fn()
+        done = torch.cuda.Event()
+        done.record(side)
+
+        def join():
+            main.wait_event(done)
+            for t in (out if isinstance(out, tuple) else (out,)):
+                if isinstance(t, torch.Tensor):
+                    t.record_stream(main)
+            return out
+        return join
+
     def launches_per_forward(self, world_size=1):
         """Kernels of this library launched per block forward (for bench accounting)."""
         # prenorm, QKV GEMM, window merge, VDA (5), quantise VDA out, O GEMM, prenorm,
@@ -185,12 +215,17 @@ class HybridBlock(nn.Module):
         q = qkv[:, :hd].view(T, H, d)
         k = qkv[:, hd:2 * hd].view(T, H, d)
         v = qkv[:, 2 * hd:].view(T, H, d)
-        att = window_softmax(q, k, v, sgate, frames, tokens, cfg.radius, quantize=True)
-        alpha = self.alpha(frame_mean, heads=heads)
         bounds = window_bounds(frames, cfg.radius)
-        lin = vda_forward(q, k, v, beta, lgate.view(T, H, d), alpha, bounds, frames, tokens,
-                          self.vda_norm)
-        return att, quantize_activation(lin, check_finite=False)
+
+        def branch():
+            alpha = self.alpha(frame_mean, heads=heads)
+            lin = vda_forward(q, k, v, beta, lgate.view(T, H, d), alpha, bounds, frames, tokens,
+                              self.vda_norm)
+            return quantize_activation(lin, check_finite=False)
+
+        join = self._vda_side(branch, qkv.device)
+        att = window_softmax(q, k, v, sgate, frames, tokens, cfg.radius, quantize=True)
+        return att, join()
 
     def _attention_ulysses(self, qkv, sgate, beta, lgate, y1, frames, tokens, rt):
         """Head-sharded attention between the two Ulysses exchanges."""
@@ -263,13 +298,20 @@ class HybridBlock(nn.Module):
         q, k, v = recv[:, :, 0:d], recv[:, :, d:2 * d], recv[:, :, 2 * d:3 * d]
         cols = slice(h0 * d, (h0 + hl) * d)
         lgate = torch.sigmoid(F.linear(gathered[:, 2 * H:], og.up.weight[cols], og.up.bias[cols]))
+        bounds = window_bounds(frames, cfg.radius)
+
+        def branch():  # VDA and its return scatter, on the side stream
+            alpha = self.alpha(frame_mean, heads=slice(h0, h0 + hl))
+            lin = vda_forward(q, k, v, gathered[:, H + h0:H + h0 + hl], lgate.view(T, hl, d), alpha,
+                              bounds, frames, tokens, self.vda_norm)
+            ex.scatter_quantize(lin.view(T, hl, d), ex.lin_dst)
+            return lin
+
+        join = self._vda_side(branch, y1.device)
         att = torch.empty(T, hl, d, device=y1.device, dtype=torch.bfloat16)
         window_softmax(q, k, v, gathered[:, h0:h0 + hl], frames, tokens, cfg.radius, out=att)
-        alpha = self.alpha(frame_mean, heads=slice(h0, h0 + hl))
-        lin = vda_forward(q, k, v, gathered[:, H + h0:H + h0 + hl], lgate.view(T, hl, d), alpha,
-                          window_bounds(frames, cfg.radius), frames, tokens, self.vda_norm)
         ex.scatter_quantize(att, ex.att_dst)
-        ex.scatter_quantize(lin.view(T, hl, d), ex.lin_dst)
+        join()
         ex.fence()
         return ex.operands()
 
