@@ -227,6 +227,17 @@ int vdn_mxfp8_quantize_scatter(const void* src, int64_t rows, int heads_local, i
 
 /* -------------------------------------------------------------------- VDA */
 
+/* FrameKDAAlpha: alpha [F, heads, d] fp32 = exp(-exp(a_log[h]) * softplus(
+ * (frame_mean @ down_w^T) @ up_w^T + dt_bias)), softplus threshold 20.
+ * frame_mean [F, hidden], down_w [r, hidden], up_w [heads*d, r], dt_bias
+ * [heads*d], a_log [heads] (fp32, contiguous; pass the selected heads' rows for
+ * a head shard); scratch holds F*r floats.
+ * Replaces FrameKDAAlpha.forward, src/models/linear_attention/layers.py:36-69. */
+int vdn_frame_alpha(const float* frame_mean, int F, int hidden, const float* down_w, int r,
+                    const float* up_w, const float* dt_bias, const float* a_log, int heads, int d,
+                    float* scratch, float* out, cudaStream_t stream);
+
+
 /* Per (frame, head) delta-rule factors, d in {64, 128}, n matrices:
  *   T = diag(alpha) (I + A)^-1,  J = B (I + A)^-1    (alpha NULL = ones)
  * A, B, T, J fp32 [n, d, d]; alpha fp32 [n, d].  I + A must be SPD.

@@ -134,3 +134,15 @@ def test_block_graph_replay_matches_eager(cuda):
         out = graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(out, w)
+
+
+@pytest.mark.parametrize("heads", [None, (2, 5)])
+@torch.no_grad()
+def test_frame_alpha_native_matches_module(cuda, heads):
+    """vdn_frame_alpha == FrameKDAAlpha.forward (fp32, reference layers.py:36-69)."""
+    from vdn_b200.linear_attention import FrameKDAAlpha
+    torch.manual_seed(3)
+    mod = FrameKDAAlpha(1024, 8, 128).to(cuda)
+    fm = torch.randn(21, 1024, device=cuda)
+    sl = None if heads is None else slice(*heads)
+    torch.testing.assert_close(mod.forward_native(fm, heads=sl), mod(fm, heads=sl), rtol=2e-5, atol=1e-6)

@@ -218,7 +218,7 @@ class HybridBlock(nn.Module):
         bounds = window_bounds(frames, cfg.radius)
 
         def branch():
-            alpha = self.alpha(frame_mean, heads=heads)
+            alpha = self.alpha.forward_native(frame_mean, heads=heads)
             lin = vda_forward(q, k, v, beta, lgate.view(T, H, d), alpha, bounds, frames, tokens,
                               self.vda_norm)
             return quantize_activation(lin, check_finite=False)
@@ -252,7 +252,7 @@ class HybridBlock(nn.Module):
         q, k, v = recv[:, :, 0:d], recv[:, :, d:2 * d], recv[:, :, 2 * d:3 * d]
         ret = torch.empty(T, hl, 2 * d, device=qkv.device, dtype=torch.bfloat16)
         window_softmax(q, k, v, recv[:, :, 4 * d], frames, tokens, cfg.radius, out=ret[:, :, :d])
-        alpha = self.alpha(frame_mean, heads=heads)
+        alpha = self.alpha.forward_native(frame_mean, heads=heads)
         bounds = window_bounds(frames, cfg.radius)
         lin = vda_forward(q, k, v, recv[:, :, 4 * d + 1], recv[:, :, 3 * d:4 * d], alpha, bounds,
                           frames, tokens, self.vda_norm)
@@ -301,7 +301,7 @@ class HybridBlock(nn.Module):
         bounds = window_bounds(frames, cfg.radius)
 
         def branch():  # VDA and its return scatter, on the side stream
-            alpha = self.alpha(frame_mean, heads=slice(h0, h0 + hl))
+            alpha = self.alpha.forward_native(frame_mean, heads=slice(h0, h0 + hl))
             lin = vda_forward(q, k, v, gathered[:, H + h0:H + h0 + hl], lgate.view(T, hl, d), alpha,
                               bounds, frames, tokens, self.vda_norm)
             ex.scatter_quantize(lin.view(T, hl, d), ex.lin_dst)

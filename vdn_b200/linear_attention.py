@@ -90,6 +90,27 @@ class FrameKDAAlpha(nn.Module):
                        * (math.log(0.1) - math.log(0.001)) + math.log(0.001)).clamp(min=1e-4)
         self.dt_bias = nn.Parameter(dt + torch.log(-torch.expm1(-dt)))
 
+    def forward_native(self, frame_mean_x, heads=None):
+        """The same alpha from two library launches (vdn_frame_alpha), no host sync."""
+        if heads is None:
+            heads = slice(0, self.num_heads)
+        rows = slice(heads.start * self.head_dim, heads.stop * self.head_dim)
+        n_heads = heads.stop - heads.start
+        fm = frame_mean_x.float().contiguous()
+        f, hidden = fm.shape
+        down = self.down.weight.float().contiguous()
+        up = self.up.weight[rows].float().contiguous()
+        dt = self.dt_bias[rows].float().contiguous()
+        a_log = self.A_log[heads].float().contiguous()
+        r = down.shape[0]
+        scratch = torch.empty(f, r, device=fm.device, dtype=torch.float32)
+        out = torch.empty(f, n_heads, self.head_dim, device=fm.device, dtype=torch.float32)
+        _lib.require_device(fm, "frame_mean")
+        _lib.call("vdn_frame_alpha", _lib.ptr(fm), f, hidden, _lib.ptr(down), r, _lib.ptr(up),
+                  _lib.ptr(dt), _lib.ptr(a_log), n_heads, self.head_dim, _lib.ptr(scratch),
+                  _lib.ptr(out), _lib.stream_of(fm.device))
+        return out
+
     def forward(self, frame_mean_x, heads=None):
         if heads is None:
             up_w, dt_bias, a_log, n_heads = self.up.weight, self.dt_bias, self.A_log, self.num_heads
