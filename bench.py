@@ -107,6 +107,19 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+# DRAM bytes (read + write) per launch of the dominant kernels at the full
+# BASELINE shapes, from one single-pass ncu capture of the block bench (see the
+# block launch-list summary under profiles/); reported as roofline "traffic".
+NCU_TRAFFIC_BYTES = {
+    "mxfp8_gemm_qkv": 1471.4e6 + 981.8e6,
+    "statistics": 674.4e6 + 89.9e6,
+    "factors": 110.6e6 + 52.4e6,
+    "scan": 190.7e6 + 76.6e6,
+    "gather": 100.1e6 + 8.3e6,
+    "readout": 698.8e6 + 297.0e6,
+}
+
+
 # ------------------------------------------------------------------ timing
 def time_steps(torch, fn, steps, warmup, dist, stream):
     for _ in range(warmup):
@@ -262,7 +275,8 @@ def bench_vda(args, torch, dist, rank, world):
         "gpu_launches": 5 * args.steps,
         "roofline": {"bound": "hbm", "kernel": top, "achieved": round(achieved, 1),
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                     "traffic": None, "peak_source": src,
+                     "traffic": NCU_TRAFFIC_BYTES.get(top) if F == VDA_CFG["F"] else None,
+                     "traffic_unit": "bytes per launch (ncu dram read + write)", "peak_source": src,
                      "algorithmic_bytes_per_launch": algo[top]},
         "kernels_ms": {k_: round(v_, 4) for k_, v_ in kt.items()},
         "clocks": clk.summary(),
@@ -382,7 +396,9 @@ def bench_gemm(args, torch, dist, rank, world):
         "gpu_launches": 2 * len(cases) * args.steps,
         "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (qkv, %d x 15360 x 5120)" % M,
                      "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
-                     "frac": round(achieved / fp8_peak, 4), "traffic": None,
+                     "frac": round(achieved / fp8_peak, 4),
+                     "traffic": NCU_TRAFFIC_BYTES["mxfp8_gemm_qkv"] if M == GEMM_ROWS else None,
+                     "traffic_unit": "bytes per launch (ncu dram read + write)",
                      "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']}): the FP8 rate",
                      "algorithmic_flops_per_launch": top["flops"]},
         "shapes": per_shape,
@@ -507,7 +523,9 @@ def bench_block(args, torch, dist, rank, world):
         "launch": "eager" if args.eager else "cuda_graph",
         "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (QKV, %d x 15360 x 5120)" % rows,
                      "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
-                     "frac": round(achieved / fp8_peak, 4), "traffic": None,
+                     "frac": round(achieved / fp8_peak, 4),
+                     "traffic": NCU_TRAFFIC_BYTES["mxfp8_gemm_qkv"] if world == 1 else None,
+                     "traffic_unit": "bytes per launch (ncu dram read + write)",
                      "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']}): the FP8 rate",
                      "algorithmic_flops_per_launch": gemm_flops},
         "comparators": comp,
