@@ -33,6 +33,22 @@ __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t c) {
   return row * 128u + ((c ^ (row & 7u)) << 4);
 }
 
+// Named-barrier AND vote over `count` threads: every participant gets the same
+// answer, so a group of warps leaves a loop together (a warp that left alone
+// would strand the others at the group's next barrier).
+__device__ __forceinline__ bool bar_and(uint32_t id, uint32_t count, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
+}
+
 // x * sigmoid(x).  VDN_SILU selects the formulation (timed variants):
 //   0: __expf + __fdividef (two MUFU ops)
 //   1: ex2.approx + rcp.approx (two MUFU ops, no range handling)
@@ -297,7 +313,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     int k = 0;
     for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x, ++k) {
       const int b = k & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (k >> 1) & 1, abort_flag))) break;
+      if (!bar_and(1, 128, mbar_wait(&acc_full[b], (k >> 1) & 1, abort_flag))) break;
       tc_fence_after();
       const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + b * 256;
       float* b_out = p.B + ((int64_t)item * 128 + mrow) * 128;
