@@ -83,17 +83,19 @@ __device__ __forceinline__ float silu_fast(float x) {
 // ------------------------------------------------------------------ statistics
 // Persistent, warp-specialised: grid = min(F*H, SMs), one CTA per SM walking
 // (frame, head) items.  Warp 0 lane 0 streams 32-token raw k / v chunks by TMA
-// into a 4-stage ring; warps 2-9 (8 threads per token) apply features and beta
-// and write kf / vb in place plus the khi / klo split; warp 1 lane 0 issues
-// A += khi.kf^T + klo.kf^T and B += vb.kf^T into one of two TMEM accumulator
-// pairs (512 columns); warps 10-13 drain an item's A (symmetrised through
-// shared memory) and B (bf16-rounded) while the next item streams.
+// into a 4-stage ring; warps 2-17 (16 threads per token, one 8-element chunk of
+// k and of v each) apply features and beta and write kf / vb in place plus the
+// khi / klo split; warp 1 lane 0 issues A += khi.kf^T + klo.kf^T and
+// B += vb.kf^T into one of two TMEM accumulator pairs (512 columns); warps
+// 18-21 drain an item's A (symmetrised through shared memory) and B
+// (bf16-rounded) while the next item streams.  The transform is the kernel's
+// critical stage (MUFU-heavy SiLU), hence its sixteen warps.
 constexpr int ST_CH = 32;                       // tokens per chunk
 constexpr int ST_STAGES = 4;
 constexpr int ST_REGION = ST_CH * 128;          // 4 KB: 32 rows x 128 B
 constexpr int ST_STAGE_BYTES = 8 * ST_REGION;   // k(kf), v(vb), khi, klo: 2 regions each
 constexpr int ST_RAW_BYTES = 4 * ST_REGION;     // what TMA writes per stage
-constexpr int ST_THREADS = 448;
+constexpr int ST_THREADS = 704;             // 2 + 16 transform + 4 epilogue warps
 constexpr int ST_TRANS_BYTES = 128 * 129 * 4;
 constexpr int ST_NBAR = 3 * ST_STAGES + 2 * 2 + 1;
 constexpr size_t ST_SMEM = 1024 + ST_STAGES * ST_STAGE_BYTES + ST_TRANS_BYTES + ST_NBAR * 8 + 64;
@@ -131,7 +133,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
   if (tid == 0) {
     for (int s = 0; s < ST_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], 256);
+      mbar_init(&ready[s], 512);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -223,10 +225,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         }
       }
     }
-  } else if (warp < 10) {
+  } else if (warp < 18) {
     // ----------------------------------------------------------- transform
-    const uint32_t t = tid - 64;                 // 0..255
-    const uint32_t row = t >> 3, e = t & 7, r = e >> 2, cc = (e & 3) * 2;
+    const uint32_t t = tid - 64;                 // 0..511
+    const uint32_t row = t >> 4, e = t & 15, r = e >> 3, cc = e & 7;
     int g = 0;
     for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
       const int f = item / p.H, h = item % p.H;
@@ -246,17 +248,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
           break;
         }
         uint8_t* st = stages + s * ST_STAGE_BYTES;
-        float kv[16], vv[16];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const uint32_t off = r * ST_REGION + swz(row, cc + j);
-          unpack8(*reinterpret_cast<const uint4*>(st + off), kv + 8 * j);
-          unpack8(*reinterpret_cast<const uint4*>(st + 2 * ST_REGION + off), vv + 8 * j);
-        }
+        const uint32_t off = r * ST_REGION + swz(row, cc);
+        float kv[8], vv[8];
+        unpack8(*reinterpret_cast<const uint4*>(st + off), kv);
+        unpack8(*reinterpret_cast<const uint4*>(st + 2 * ST_REGION + off), vv);
         if (FEATURES) {
           float ss = 0.f;
 #pragma unroll
-          for (int i = 0; i < 16; i += 2) {
+          for (int i = 0; i < 8; i += 2) {
             kv[i] = silu_fast(kv[i]);
             kv[i + 1] = silu_fast(kv[i + 1]);
             round_bf16_pair(kv[i], kv[i + 1]);
@@ -269,10 +268,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
           ss += __shfl_xor_sync(0xffffffffu, ss, 1);
           ss += __shfl_xor_sync(0xffffffffu, ss, 2);
           ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+          ss += __shfl_xor_sync(0xffffffffu, ss, 8);
           const float nrm = fmaxf(round_bf16(sqrtf(ss)), round_bf16(1e-6f));
           const float inv = __fdiv_rn(1.0f, nrm);
 #pragma unroll
-          for (int i = 0; i < 16; i += 2) {
+          for (int i = 0; i < 8; i += 2) {
             kv[i] *= inv;
             kv[i + 1] *= inv;
             round_bf16_pair(kv[i], kv[i + 1]);
@@ -280,9 +280,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         }
         // kf * beta is exact in fp32 (two bf16 factors, 16 significant bits); its
         // bf16 rounding hi leaves a residual that is itself exactly a bf16 value.
-        uint32_t hi2[8], lo2[8], vb2[8];
+        uint32_t hi2[4], lo2[4], vb2[4];
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
+        for (int i = 0; i < 8; i += 2) {
           const float p0 = kv[i] * bt, p1 = kv[i + 1] * bt;
           float h0 = p0, h1 = p1;
           round_bf16_pair(h0, h1);
@@ -290,17 +290,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
           lo2[i / 2] = pack_exact2(p0 - h0, p1 - h1);
           vb2[i / 2] = pack_bf16x2(vv[i] * bt, vv[i + 1] * bt);
         }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const uint32_t off = r * ST_REGION + swz(row, cc + j);
-          *reinterpret_cast<uint4*>(st + off) = pack_exact8(kv + 8 * j);
-          *reinterpret_cast<uint4*>(st + 2 * ST_REGION + off) =
-              make_uint4(vb2[4 * j], vb2[4 * j + 1], vb2[4 * j + 2], vb2[4 * j + 3]);
-          *reinterpret_cast<uint4*>(st + 4 * ST_REGION + off) =
-              make_uint4(hi2[4 * j], hi2[4 * j + 1], hi2[4 * j + 2], hi2[4 * j + 3]);
-          *reinterpret_cast<uint4*>(st + 6 * ST_REGION + off) =
-              make_uint4(lo2[4 * j], lo2[4 * j + 1], lo2[4 * j + 2], lo2[4 * j + 3]);
-        }
+        *reinterpret_cast<uint4*>(st + off) = pack_exact8(kv);
+        *reinterpret_cast<uint4*>(st + 2 * ST_REGION + off) = make_uint4(vb2[0], vb2[1], vb2[2], vb2[3]);
+        *reinterpret_cast<uint4*>(st + 4 * ST_REGION + off) = make_uint4(hi2[0], hi2[1], hi2[2], hi2[3]);
+        *reinterpret_cast<uint4*>(st + 6 * ST_REGION + off) = make_uint4(lo2[0], lo2[1], lo2[2], lo2[3]);
         fence_proxy_async_smem();
         mbar_arrive(&ready[s]);
       }
@@ -308,7 +301,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;                   // warps 10..13 -> quadrants 2,3,0,1
+    const int quad = warp & 3;                   // warps 18..21 -> quadrants 2,3,0,1
     const int mrow = quad * 32 + lane;
     int k = 0;
     for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x, ++k) {
@@ -562,13 +555,21 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
       bool ok = true;
       for (int i = 0; i < nt; ++i, ++g) {
         const int b = g & 1;
+        const int s = i * RO_TOK + (int)erow;
+        const bool valid = s < p.S;
+        // The gate row does not depend on the accumulator: load all of it before
+        // waiting, so its DRAM latency overlaps the MMA instead of the epilogue.
+        const uint16_t* grow = p.gate + (int64_t)f * p.g_sf + (int64_t)s * p.g_ss + (int64_t)h * p.g_sh;
+        uint4 gv[16];
+        if (valid) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) gv[e] = *reinterpret_cast<const uint4*>(grow + 8 * e);
+        }
         if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (g >> 1) & 1, abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int s = i * RO_TOK + (int)erow;
-        const bool valid = s < p.S;
         const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + b * 128;
         float ss = 0.f;
 #pragma unroll 1
@@ -586,37 +587,33 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
         }
         const float nrm = sqrtf(ss);
         const float inv = round_bf16(__fdiv_rn(1.0f, sqrtf(nrm * nrm / 128.0f + p.eps)));
-        const uint16_t* grow = p.gate + (int64_t)f * p.g_sf + (int64_t)s * p.g_ss + (int64_t)h * p.g_sh;
         uint16_t* orow = p.out + ((int64_t)f * p.S + s) * ((int64_t)p.H * 128) + (int64_t)h * 128;
-#pragma unroll 1
+#pragma unroll
         for (int cb = 0; cb < 4; ++cb) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(taddr + cb * 32, v);
-          uint4 gv[4];
-          if (valid) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) gv[e] = *reinterpret_cast<const uint4*>(grow + cb * 32 + 8 * e);
-          }
           tmem_ld_wait();
           if (!valid) continue;
-          float gf[32], y[32];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) unpack8(gv[e], gf + 8 * e);
+          for (int e4 = 0; e4 < 4; ++e4) {
+            float gf[8], y[8];
+            unpack8(gv[4 * cb + e4], gf);
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float r0 = __uint_as_float(v[e]), r1 = __uint_as_float(v[e + 1]);
-            round_bf16_pair(r0, r1);
-            r0 *= inv;
-            r1 *= inv;
-            round_bf16_pair(r0, r1);
-            r0 *= w_s[cb * 32 + e];
-            r1 *= w_s[cb * 32 + e + 1];
-            round_bf16_pair(r0, r1);
-            y[e] = r0 * gf[e];
-            y[e + 1] = r1 * gf[e + 1];
+            for (int e = 0; e < 8; e += 2) {
+              const int c = 8 * e4 + e;
+              float r0 = __uint_as_float(v[c]), r1 = __uint_as_float(v[c + 1]);
+              round_bf16_pair(r0, r1);
+              r0 *= inv;
+              r1 *= inv;
+              round_bf16_pair(r0, r1);
+              r0 *= w_s[cb * 32 + c];
+              r1 *= w_s[cb * 32 + c + 1];
+              round_bf16_pair(r0, r1);
+              y[e] = r0 * gf[e];
+              y[e + 1] = r1 * gf[e + 1];
+            }
+            *reinterpret_cast<uint4*>(orow + cb * 32 + 8 * e4) = pack8(y);
           }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) *reinterpret_cast<uint4*>(orow + cb * 32 + 8 * e) = pack8(y + 8 * e);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[b]);
