@@ -146,14 +146,18 @@ __global__ void __launch_bounds__(256) stats_kernel(
 }
 
 // -------------------------------------------------------------------- factors
-// One CTA per matrix; thread (ty, tx) holds rows ty*T.., cols tx*T.. of the
-// working matrix in registers. T may alias A and J may alias B (each CTA reads
-// its whole matrix before the first store), so those pointers are not restrict.
-// Non-pivoting in-place Gauss-Jordan inversion of the SPD M = I + A: at pivot p
-// the owners publish row p and column p through double-buffered shared vectors,
-// every thread applies the rank-1 update with one FMA per element, and the
-// owners of row / column p then overwrite those entries.  J = B inv reads B
-// rows from global (L2) and inv from shared memory.
+// One CTA per matrix; thread (ty, tx) holds rows {ty + 16 i} and columns
+// {tx + 16 j} (i, j < D/16) of the working matrix in registers: for a fixed j
+// the sixteen column groups of a warp touch sixteen consecutive words of a
+// shared vector, so every shared-memory access is conflict-free.  T may alias A
+// and J may alias B (each CTA reads its whole matrix before the first store),
+// so those pointers are not restrict.  Non-pivoting in-place Gauss-Jordan
+// inversion of the SPD M = I + A, pivots in natural order p = o + 16 jj: at
+// pivot p the owners publish row p and column p through double-buffered shared
+// vectors (and the pivot's owner its reciprocal, computed once), every thread
+// applies the rank-1 update with one FMA per element, and the owners of row /
+// column p then overwrite those entries.  J = B inv reads B rows from global
+// (L2) and inv from shared memory.
 template <int D>
 __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const float* B,
                                                         const float* __restrict__ alpha,
@@ -163,6 +167,7 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
   float* rowbuf = smem;            // [2][D]
   float* colbuf = smem + 2 * D;    // [2][D]
   float* inv_s = smem + 4 * D;     // [D][D]
+  __shared__ float piv[2];
   const int64_t mat = blockIdx.x;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const float* a_in = A + mat * D * D;
@@ -172,44 +177,45 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
   for (int i = 0; i < T; ++i)
 #pragma unroll
     for (int j = 0; j < T; ++j) {
-      const int r = ty * T + i, c = tx * T + j;
+      const int r = ty + 16 * i, c = tx + 16 * j;
       m[i][j] = a_in[r * D + c] + (r == c ? 1.0f : 0.0f);
     }
-  // Outer loop over pivot blocks, inner loop unrolled so the pivot's position
-  // inside a thread's tile is a compile-time index (m stays in registers).
-  for (int pb = 0; pb < D / T; ++pb) {
+  // Pivot p = o + 16 jj lives in row slot jj of threads ty == o and column slot
+  // jj of threads tx == o: the slot is a compile-time index (m stays in registers).
 #pragma unroll
-    for (int pi = 0; pi < T; ++pi) {
-      const int p = pb * T + pi;
+  for (int jj = 0; jj < T; ++jj) {
+    for (int o = 0; o < 16; ++o) {
+      const int p = o + 16 * jj;
       float* rb = rowbuf + (p & 1) * D;
       float* cb = colbuf + (p & 1) * D;
-      if (ty == pb) {
+      if (ty == o) {
 #pragma unroll
-        for (int j = 0; j < T; ++j) rb[tx * T + j] = m[pi][j];
+        for (int j = 0; j < T; ++j) rb[tx + 16 * j] = m[jj][j];
+        if (tx == o) piv[p & 1] = __fdiv_rn(1.0f, m[jj][jj]);
       }
-      if (tx == pb) {
+      if (tx == o) {
 #pragma unroll
-        for (int i = 0; i < T; ++i) cb[ty * T + i] = m[i][pi];
+        for (int i = 0; i < T; ++i) cb[ty + 16 * i] = m[i][jj];
       }
       __syncthreads();
-      const float ip = __fdiv_rn(1.0f, rb[p]);
+      const float ip = piv[p & 1];
       float prow[T], pcol[T];
 #pragma unroll
-      for (int j = 0; j < T; ++j) prow[j] = rb[tx * T + j] * ip;
+      for (int j = 0; j < T; ++j) prow[j] = rb[tx + 16 * j] * ip;
 #pragma unroll
-      for (int i = 0; i < T; ++i) pcol[i] = cb[ty * T + i];
+      for (int i = 0; i < T; ++i) pcol[i] = cb[ty + 16 * i];
 #pragma unroll
       for (int i = 0; i < T; ++i)
 #pragma unroll
         for (int j = 0; j < T; ++j) m[i][j] = fmaf(-pcol[i], prow[j], m[i][j]);
-      if (ty == pb) {
+      if (ty == o) {
 #pragma unroll
-        for (int j = 0; j < T; ++j) m[pi][j] = prow[j];
+        for (int j = 0; j < T; ++j) m[jj][j] = prow[j];
       }
-      if (tx == pb) {
+      if (tx == o) {
 #pragma unroll
-        for (int i = 0; i < T; ++i) m[i][pi] = -pcol[i] * ip;
-        if (ty == pb) m[pi][pi] = ip;
+        for (int i = 0; i < T; ++i) m[i][jj] = -pcol[i] * ip;
+        if (ty == o) m[jj][jj] = ip;
       }
     }
   }
@@ -220,7 +226,7 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
   for (int i = 0; i < T; ++i)
 #pragma unroll
     for (int j = 0; j < T; ++j) {
-      const int r = ty * T + i, c = tx * T + j;
+      const int r = ty + 16 * i, c = tx + 16 * j;
       inv_s[r * D + c] = m[i][j];
       t_out[r * D + c] = al ? al[r] * m[i][j] : m[i][j];
     }
@@ -234,12 +240,12 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
   for (int k4 = 0; k4 < D; k4 += 4) {
     float4 bv[T];
 #pragma unroll
-    for (int i = 0; i < T; ++i) bv[i] = *reinterpret_cast<const float4*>(b_in + (ty * T + i) * D + k4);
+    for (int i = 0; i < T; ++i) bv[i] = *reinterpret_cast<const float4*>(b_in + (ty + 16 * i) * D + k4);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       float iv[T];
 #pragma unroll
-      for (int j = 0; j < T; ++j) iv[j] = inv_s[(k4 + kk) * D + tx * T + j];
+      for (int j = 0; j < T; ++j) iv[j] = inv_s[(k4 + kk) * D + tx + 16 * j];
 #pragma unroll
       for (int i = 0; i < T; ++i) {
         const float b = kk == 0 ? bv[i].x : kk == 1 ? bv[i].y : kk == 2 ? bv[i].z : bv[i].w;
@@ -253,7 +259,7 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
 #pragma unroll
   for (int i = 0; i < T; ++i)
 #pragma unroll
-    for (int j = 0; j < T; ++j) j_out[(ty * T + i) * D + tx * T + j] = acc[i][j];
+    for (int j = 0; j < T; ++j) j_out[(ty + 16 * i) * D + tx + 16 * j] = acc[i][j];
 }
 
 // ----------------------------------------------------------------------- scan
