@@ -2,7 +2,8 @@
 
     x -> RMSNorm * (1 + scale_msa) + shift_msa -> [bf16 y1, MXFP8]      prenorm producer
       -> QKV (MXFP8 GEMM, N = 3 * hidden)
-      -> gates from y1: softmax gate [T,H], beta [T,H], linear gate [T,H*d] (bf16 linears)
+      -> gates from y1: softmax gate [T,H], beta [T,H], output-gate hidden [T,r]
+         (one bf16 GEMM), linear gate [T,H*d] = sigmoid(up(hidden))
       -> frame mean of y1 -> alpha (FrameKDAAlpha)
       -> [Ulysses: sequence -> heads all-to-all]
       -> window softmax (+-radius frames) * softmax gate     cuDNN legs + vdn_window_merge
@@ -119,6 +120,28 @@ class HybridBlock(nn.Module):
                   _lib.ptr(self._status), _lib.stream_of(out.device))
         return out
 
+    def _gate_projections(self, y1, out=None):
+        """[rows, 2H + r]: sigmoid(softmax gate) | sigmoid(beta) | output-gate hidden, from
+        ONE bf16 GEMM over y1 (the three projections share their input; their weights
+        are concatenated once and re-concatenated only when a weight changes)."""
+        og = self.output_gate
+        ws = (self.softmax_gate.weight, self.beta_proj.weight, og.down.weight)
+        key = tuple((w.data_ptr(), w._version) for w in ws) + (self.softmax_gate.bias._version,)
+        if getattr(self, "_gate_key", None) != key:
+            H = self.cfg.heads
+            self._gate_w = torch.cat(ws, dim=0).contiguous()
+            bias = torch.zeros(self._gate_w.shape[0], dtype=self._gate_w.dtype, device=self._gate_w.device)
+            bias[:H] = self.softmax_gate.bias
+            self._gate_b = bias
+            self._gate_key = key
+        H = self.cfg.heads
+        z = F.linear(y1, self._gate_w, self._gate_b)
+        z[:, :2 * H].sigmoid_()
+        if out is None:
+            return z
+        out.copy_(z)
+        return out
+
     def _side(self, device):
         """The branch-overlap stream of this device (the reference's vda_on_side_stream,
         src/inference/utils/vda_overlap.py:7-44): the VDA branch runs there while the
@@ -175,9 +198,10 @@ class HybridBlock(nn.Module):
         else:
             qkv = torch.empty(rows, 3 * hd, device=dev, dtype=torch.bfloat16)
             self._gemm(q1, s1, self.qkv, rows, qkv, bias=self.qkv.bias)
-            sgate = torch.sigmoid(self.softmax_gate(y1))                  # [rows, H]
-            beta = torch.sigmoid(self.beta_proj(y1))                      # [rows, H]
-            lgate = self.output_gate(y1).reshape(rows, hd)                # [rows, H*d]
+            g3 = self._gate_projections(y1)                               # [rows, 2H + r]
+            sgate, beta = g3[:, :H], g3[:, H:2 * H]                       # [rows, H] each
+            og = self.output_gate
+            lgate = torch.sigmoid(F.linear(g3[:, 2 * H:], og.up.weight, og.up.bias))  # [rows, H*d]
             if runtime is None:
                 frame_mean = y1.view(frames, tokens, hd).mean(1, dtype=torch.float32)
                 first, second = self._attention(qkv, sgate, beta, lgate, frame_mean, frames, tokens,
@@ -283,8 +307,7 @@ class HybridBlock(nn.Module):
         # Side inputs into this rank's slot of every rank's buffers (copy engines).
         rt.local_frame_sums(y1, frames, tokens, out=ex.sums()[rt.rank])
         ex.publish_sums()
-        torch.cat([torch.sigmoid(self.softmax_gate(y1)), torch.sigmoid(self.beta_proj(y1)),
-                   og.down(y1)], dim=1, out=ex.local_rows())              # [rows, 2H + r]
+        self._gate_projections(y1, out=ex.local_rows())                  # [rows, 2H + r]
         ex.publish_rows()
         w = self.qkv
         _lib.call("vdn_mxfp8_gemm_scatter", _lib.ptr(q1), _lib.ptr(s1), _lib.ptr(w.q), _lib.ptr(w.s),
