@@ -353,14 +353,16 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 // --------------------------------------------------------------------- readout
 // Persistent, warp-specialised: grid = min(F*H, SMs), one CTA per SM walking
 // (frame, head) items.  Warp 0 lane 0 streams the item's bf16 state (double
-// buffered) and its 128-token q tiles (4-stage ring) by TMA; warps 2-5 turn
-// their tile row into features in place; warp 1 lane 0 issues q.state^T into
-// one of two TMEM accumulators; warps 6-9 drain them (thread = TMEM lane =
+// buffered) and its 128-token q tiles (4-stage ring) by TMA; warps 2-9 turn the
+// tile into features in place (two threads per token row, 64 columns each:
+// measured 10% faster than four warps); warp 1 lane 0 issues q.state^T into one
+// of two TMEM accumulators; warps 10-13 drain them (thread = TMEM lane =
 // token): bf16 readout, RMSNorm over the row, * w, * gate, token-major store.
-// Hand-offs are mbarriers; every wait is bounded.
+// (Splitting the drain over eight warps, two per TMEM lane quadrant, measured
+// 27% slower.)  Hand-offs are mbarriers; every wait is bounded.
 constexpr int RO_TOK = 128;
 constexpr int RO_STAGES = 4;
-constexpr int RO_THREADS = 320;
+constexpr int RO_THREADS = 448;
 constexpr int RO_TILE = 2 * RO_TOK * 128;       // 2 regions x 128 rows x 128 B = 32 KB
 constexpr int RO_NBAR = 3 * RO_STAGES + 2 * 2 + 2 * 2 + 1;
 constexpr size_t RO_SMEM = 1024 + 2 * RO_TILE + RO_STAGES * RO_TILE + 128 * 4 + RO_NBAR * 8 + 64;
@@ -401,7 +403,7 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
   if (tid == 0) {
     for (int s = 0; s < RO_STAGES; ++s) {
       mbar_init(&q_full[s], 1);
-      mbar_init(&q_ready[s], 128);
+      mbar_init(&q_ready[s], 256);
       mbar_init(&q_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -499,9 +501,10 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
         }
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ----------------------------------------------------------- transform
-    const uint32_t row = tid - 64;               // 0..127
+    const uint32_t t = tid - 64;                 // 0..255
+    const uint32_t row = t >> 1, half = t & 1;   // lanes 2k, 2k+1 share a token row
     int g = 0;
     for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
       bool ok = true;
@@ -511,12 +514,12 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
           ok = false;
           break;
         }
-        uint8_t* tile = q_s + s * RO_TILE;
+        uint8_t* region = q_s + s * RO_TILE + half * (RO_TILE / 2);
         // Pass 1: bf16(silu) written back in place, sum of squares; pass 2: / norm.
         float ssum = 0.f;
 #pragma unroll 4
-        for (int c = 0; c < 16; ++c) {
-          uint4* ptr = reinterpret_cast<uint4*>(tile + (c >> 3) * (RO_TILE / 2) + swz(row, c & 7));
+        for (int c = 0; c < 8; ++c) {
+          uint4* ptr = reinterpret_cast<uint4*>(region + swz(row, c));
           float x[8];
           unpack8(*ptr, x);
 #pragma unroll
@@ -529,11 +532,12 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
           }
           *ptr = pack_exact8(x);
         }
+        ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);
         const float nrm = fmaxf(round_bf16(sqrtf(ssum)), round_bf16(1e-6f));
         const float inv = __fdiv_rn(1.0f, nrm);
 #pragma unroll 4
-        for (int c = 0; c < 16; ++c) {
-          uint4* ptr = reinterpret_cast<uint4*>(tile + (c >> 3) * (RO_TILE / 2) + swz(row, c & 7));
+        for (int c = 0; c < 8; ++c) {
+          uint4* ptr = reinterpret_cast<uint4*>(region + swz(row, c));
           float x[8];
           unpack8(*ptr, x);
 #pragma unroll
@@ -547,7 +551,7 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;                   // warps 6,7,8,9 -> lane quadrants 2,3,0,1
+    const int quad = warp & 3;                   // warps 10..13
     const uint32_t erow = quad * 32 + lane;
     int g = 0;
     for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
