@@ -489,22 +489,34 @@ def bench_block(args, torch, dist, rank, world):
     except Exception as e:  # comparator only
         comp["cublas_fp8_per_tensor_error"] = repr(e)[:120]
 
-    # End to end through the public API: pinned host rows in, block output back to the host.
-    x_host = x.cpu().pin_memory()
-    out_host = torch.empty_like(x_host).pin_memory()
-    x_dev = torch.empty_like(x)
+    # End to end through the public API: pinned host rows in, block output back to the host,
+    # every step.  Graph launch (default): BlockPipeline overlaps batch i's compute with the
+    # host copies of its neighbours; eager: copy in, forward, copy out, in order.
+    x_host = [x.cpu().pin_memory() for _ in range(2)]
+    out_host = [torch.empty_like(x_host[0]).pin_memory() for _ in range(2)]
+    e2e_steps = max(2, args.steps)
+    if args.eager:
+        x_dev = torch.empty_like(x)
 
-    def e2e_step():
-        if args.eager:
-            x_dev.copy_(x_host, non_blocking=True)
+        def e2e_step():
+            x_dev.copy_(x_host[0], non_blocking=True)
             y = block(x_dev, temb, F, S, runtime)
-        else:  # the public graph API: host rows into the graph's static input
-            graph.x.copy_(x_host, non_blocking=True)
-            y = graph.replay()
-        out_host.copy_(y, non_blocking=True)
+            out_host[0].copy_(y, non_blocking=True)
 
-    e2e_steps = max(2, args.steps // 2)
-    e2e_ms = time_steps(torch, e2e_step, e2e_steps, 1, dist, stream) / e2e_steps
+        e2e_ms = time_steps(torch, e2e_step, e2e_steps, 1, dist, stream) / e2e_steps
+    elif world == 1:
+        from vdn_b200.block import BlockPipeline
+        pipe = BlockPipeline(block, rows, temb, F, S, runtime)
+        ins = [x_host[i & 1] for i in range(e2e_steps)]
+        outs = [out_host[i & 1] for i in range(e2e_steps)]
+        e2e_ms = time_steps(torch, lambda: pipe.run(ins, outs), 1, 1, dist, stream) / e2e_steps
+        del pipe
+    else:  # Ulysses ranks: the captured forward with its copies in order
+        def e2e_step():
+            graph.x.copy_(x_host[0], non_blocking=True)
+            out_host[0].copy_(graph.replay(), non_blocking=True)
+
+        e2e_ms = time_steps(torch, e2e_step, e2e_steps, 1, dist, stream) / e2e_steps
     rec = {
         "metric": "hybrid-block tokens/s (BASELINE config 3, 32760 tokens)",
         "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -518,7 +530,9 @@ def bench_block(args, torch, dist, rank, world):
                    "l2": "per-step working set (activations > 1 GB) larger than L2",
                    "gemm_tflops_per_step": round(flops / 1e12, 3)},
         "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2},
+                "h2d_bytes_per_step": x_host[0].numel() * 2, "d2h_bytes_per_step": out_host[0].numel() * 2,
+                "steps": e2e_steps, "copies": "per step; overlapped with neighbouring steps"
+                if not args.eager and world == 1 else "per step; serial"},
         "gpu_launches": block.launches_per_forward(world) * args.steps,
         "launch": "eager" if args.eager else "cuda_graph",
         "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (QKV, %d x 15360 x 5120)" % rows,

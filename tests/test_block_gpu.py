@@ -146,3 +146,23 @@ def test_frame_alpha_native_matches_module(cuda, heads):
     fm = torch.randn(21, 1024, device=cuda)
     sl = None if heads is None else slice(*heads)
     torch.testing.assert_close(mod.forward_native(fm, heads=sl), mod(fm, heads=sl), rtol=2e-5, atol=1e-6)
+
+
+@torch.no_grad()
+def test_block_pipeline_matches_eager(cuda):
+    """BlockPipeline: batches streamed from pinned host memory (copies overlapped with
+    the neighbouring batches' compute) give the eager forward's outputs."""
+    from vdn_b200.block import BlockPipeline
+    cfg, block = _small_block(cuda, seed=4)
+    frames, tokens = 4, 64
+    T = frames * tokens
+    g = torch.Generator().manual_seed(91)
+    temb = torch.randn(cfg.hidden, generator=g).to(cuda)
+    xs = [torch.randn(T, cfg.hidden, generator=g).bfloat16().pin_memory() for _ in range(5)]
+    want = [block(x.to(cuda), temb, frames, tokens).cpu() for x in xs]
+    outs = [torch.empty(T, cfg.hidden, dtype=torch.bfloat16).pin_memory() for _ in xs]
+    pipe = BlockPipeline(block, T, temb, frames, tokens)
+    pipe.run(xs, outs)
+    torch.cuda.synchronize()
+    for o, w in zip(outs, want):
+        assert torch.equal(o, w)

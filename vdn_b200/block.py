@@ -37,7 +37,7 @@ from .mxfp8_kernels import launch_prenorm_quantize
 from .mxfp8_quant import quantize_cpu, quantize_activation
 from .window import window_softmax
 
-__all__ = ["HybridBlock", "BlockConfig", "BlockGraph"]
+__all__ = ["HybridBlock", "BlockConfig", "BlockGraph", "BlockPipeline"]
 
 
 class BlockConfig:
@@ -383,3 +383,55 @@ class BlockGraph:
     def replay(self) -> torch.Tensor:
         self.graph.replay()
         return self.out
+
+
+class BlockPipeline:
+    """Streams batches from pinned host memory through one block and back.
+
+    Two CUDA graphs (each with its own static input / output) alternate, so the
+    host-to-device copy of batch i+1 and the device-to-host copy of batch i-1
+    run on the copy engines (two extra streams) while batch i computes.  Every
+    batch still makes both of its copies; only their overlap with the compute
+    of the neighbouring batches changes.
+    """
+
+    def __init__(self, block: HybridBlock, rows: int, temb, frames, tokens, runtime=None):
+        dev = temb.device
+        hidden = block.cfg.hidden
+        self.graphs = [BlockGraph(block, torch.zeros(rows, hidden, device=dev, dtype=torch.bfloat16), temb,
+                                  frames, tokens, runtime) for _ in range(2)]
+        self.device = dev
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        self.in_ready = [torch.cuda.Event() for _ in range(2)]
+        self.computed = [torch.cuda.Event() for _ in range(2)]
+        self.out_free = [torch.cuda.Event() for _ in range(2)]
+
+    def run(self, host_inputs, host_outputs) -> None:
+        """Enqueue len(host_inputs) batches (pinned [rows, hidden] bf16 host tensors;
+        results into the matching host_outputs).  Returns once everything is queued on
+        the caller's stream: synchronise before reading the outputs."""
+        if len(host_inputs) != len(host_outputs):
+            raise ValueError("one output buffer per input batch")
+        main = torch.cuda.current_stream(self.device)
+        self.h2d.wait_stream(main)
+        self.d2h.wait_stream(main)
+        for i, (src, dst) in enumerate(zip(host_inputs, host_outputs)):
+            b = i & 1
+            g = self.graphs[b]
+            with torch.cuda.stream(self.h2d):
+                if i >= 2:
+                    self.h2d.wait_event(self.computed[b])      # batch i-2 no longer reads g.x
+                g.x.copy_(src, non_blocking=True)
+                self.in_ready[b].record(self.h2d)
+            main.wait_event(self.in_ready[b])
+            if i >= 2:
+                main.wait_event(self.out_free[b])              # batch i-2's result has left g.out
+            g.replay()
+            self.computed[b].record(main)
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self.computed[b])
+                dst.copy_(g.out, non_blocking=True)
+                self.out_free[b].record(self.d2h)
+        main.wait_stream(self.d2h)
+        main.wait_stream(self.h2d)
