@@ -227,6 +227,19 @@ int vdn_mxfp8_quantize_scatter(const void* src, int64_t rows, int heads_local, i
 
 /* -------------------------------------------------------------------- VDA */
 
+/* Separable short conv of one projection (depthwise 5x5 spatial per frame, then
+ * depthwise 5-tap temporal across frames, zero padding, no bias): x [F*gh*gw, C]
+ * bf16 rows (stride x_ld, frame-major, (y, x) row-major in a frame) ->
+ * out [F*gh*gw, C] bf16 (stride out_ld).  w_spatial [25, C] and w_temporal [5, C]
+ * bf16, tap-major; scratch holds F*gh*gw*C bf16 (the spatial half).  C % 8 == 0,
+ * pointers 16-byte aligned, strides % 8 == 0.  The spatial half is rounded to
+ * bf16; the temporal half sums its five exact products in fp32 (taps in order)
+ * and rounds once.
+ * Replaces LinearAttentionSepConv.spatial + _temporal_conv,
+ * src/models/linear_attention/features.py:133-209 and :12-40. */
+int vdn_sepconv(const void* x, int64_t x_ld, int F, int gh, int gw, int C, const void* w_spatial,
+                const void* w_temporal, void* scratch, void* out, int64_t out_ld, cudaStream_t stream);
+
 /* FrameKDAAlpha: alpha [F, heads, d] fp32 = exp(-exp(a_log[h]) * softplus(
  * (frame_mean @ down_w^T) @ up_w^T + dt_bias)), softplus threshold 20.
  * frame_mean [F, hidden], down_w [r, hidden], up_w [heads*d, r], dt_bias

@@ -13,7 +13,10 @@ It imports the reference (ec-jt/vdn) and records, on seeded synthetic inputs:
     BASELINE config-0 geometry (F=4, S=64, H=4, d=64) and at d=128 with and
     without the text seed and the anchor frames;
   * the stage functions frame_statistics, VdnDelta.factor_apply, _run_scans and
-    gather_linear_state (scan.py, delta_rule.py) on one d=128 case.
+    gather_linear_state (scan.py, delta_rule.py) on one d=128 case;
+  * the separable short conv LinearAttentionSepConv (features.py:133-209): its
+    spatial 5x5 half, the eager temporal 5-tap shift and the activated k / v
+    features, on two grids (--sepconv-only regenerates just these).
 
 Nothing at test time reads the reference; the tests read only these .npz files.
 """
@@ -124,8 +127,45 @@ def stage_fixtures(scan, delta):
         gathered_noseed=gathered0.numpy())
 
 
-def main(ref_root: str):
+def sepconv_fixtures(features_mod):
+    """Reference short conv on CPU: spatial half (bf16 conv2d), eager temporal shift,
+    and prepare_linear_features (conv -> SiLU [-> L2Norm]) for k and v."""
+    out = {}
+    cases = {"small": dict(f=4, gh=6, gw=8, h=2, d=64, seed=21),
+             "d128": dict(f=5, gh=5, gw=7, h=2, d=128, seed=22)}
+    for name, c in cases.items():
+        torch.manual_seed(c["seed"])
+        ch = c["h"] * c["d"]
+        conv = features_mod.LinearAttentionSepConv(ch, ("k", "v")).to(torch.bfloat16)
+        s = c["gh"] * c["gw"]
+        g = torch.Generator().manual_seed(c["seed"] + 100)
+        for proj in ("k", "v"):
+            tokens = torch.randn(c["f"] * s, c["h"], c["d"], generator=g).bfloat16()
+            with torch.no_grad():
+                x, w_tm = conv.spatial(proj, tokens, c["f"], (c["gh"], c["gw"]))
+                tm = features_mod._temporal_shift(x, w_tm, 5, 2)
+                feat = features_mod.prepare_linear_features(
+                    tokens, l2norm=(proj != "v"), conv=conv, proj=proj, num_frames=c["f"],
+                    frame_size=(c["gh"], c["gw"]))
+            key = f"{name}_{proj}"
+            out[f"{key}_x"] = bits(tokens)
+            out[f"{key}_wsp"] = bits(getattr(conv, f"{proj}_sp").weight.detach())
+            out[f"{key}_wtm"] = bits(getattr(conv, f"{proj}_tm").weight.detach())
+            out[f"{key}_spatial"] = bits(x)
+            out[f"{key}_temporal"] = bits(tm)
+            out[f"{key}_features"] = bits(feat)
+        out[f"{name}_geom"] = np.array([c["f"], c["gh"], c["gw"], c["h"], c["d"]], dtype=np.int64)
+    np.savez_compressed(HERE / "sepconv_golden.npz", **out)
+
+
+def main(ref_root: str, sepconv_only: bool = False):
     sys.path.insert(0, ref_root)
+    torch.set_num_threads(8)
+    from src.models.linear_attention import features as features_mod
+    sepconv_fixtures(features_mod)
+    if sepconv_only:
+        print("wrote sepconv_golden.npz")
+        return
     from src.models.ops.mxfp8_quant import quantize_cpu
     from src.models.linear_attention import scan, delta_rule
     from src.models.linear_attention.branch import BidirectionalLinearBranch
@@ -149,6 +189,7 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        raise SystemExit("usage: make_golden.py <path to the ec-jt/vdn checkout>")
-    main(sys.argv[1])
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    if len(args) != 1:
+        raise SystemExit("usage: make_golden.py <path to the ec-jt/vdn checkout> [--sepconv-only]")
+    main(args[0], sepconv_only="--sepconv-only" in sys.argv)

@@ -109,7 +109,14 @@ def test_branch_module_contracts():
     with pytest.raises(ValueError):
         BidirectionalLinearBranch(16, 2, 128, delta_rule="sana_scaled")
     with pytest.raises(ValueError):
-        BidirectionalLinearBranch(16, 2, 128, short_conv=("k", "v"))
+        BidirectionalLinearBranch(16, 2, 128, short_conv=("k", "k"))
+    with pytest.raises(ValueError):
+        BidirectionalLinearBranch(16, 2, 128, short_conv=("x",))
+    conv = BidirectionalLinearBranch(16, 2, 128, short_conv=("k", "v"))
+    assert {"short_conv.k_sp.weight", "short_conv.k_tm.weight", "short_conv.v_sp.weight",
+            "short_conv.v_tm.weight"} <= set(dict(conv.named_parameters()))
+    assert conv.short_conv.k_sp.weight.shape == (256, 1, 5, 5)
+    assert conv.short_conv.k_tm.weight.shape == (256, 1, 5)
     b = BidirectionalLinearBranch(16, 2, 128)
     names = set(dict(b.named_parameters()))
     assert {"alpha.A_log", "alpha.dt_bias", "alpha.down.weight", "alpha.up.weight",

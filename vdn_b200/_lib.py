@@ -55,6 +55,7 @@ SIGNATURES = {
                                           _p, _p]),
     "vdn_window_merge": (_i32, [_i32, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _p, _i64, _i64, _p,
                                 _i64, _i64, _p, _p, _p]),
+    "vdn_sepconv": (_i32, [_p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _i64, _p]),
     "vdn_frame_alpha": (_i32, [_p, _i32, _i32, _p, _i32, _p, _p, _p, _i32, _i32, _p, _p, _p]),
     "vdn_delta_factors": (_i32, [_p, _p, _p, _i64, _i32, _p, _p, _p]),
     "vdn_vda_statistics": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,

@@ -255,8 +255,8 @@ class BidirectionalLinearBranch(nn.Module):
     """NoPE linear-attention branch, native B200 body (branch.py:47-402).
 
     Supports the released-checkpoint rule (delta_rule="vdn_solve", a_fp32) with
-    bridge "alpha" or "none", the text seed and anchor frames.  Short conv is a
-    later addition and raises here.
+    bridge "alpha" or "none", the text seed, the anchor frames and the separable
+    short conv (short_conv=("k", "v") as released; any subset of q / k / v).
     """
 
     TEXT_STATE_SCALE = 0.5
@@ -272,13 +272,17 @@ class BidirectionalLinearBranch(nn.Module):
             raise ValueError(f"bridge must be one of {BRIDGE_MODES}")
         if head_dim not in (64, 128):
             raise ValueError("head_dim must be 64 or 128")
-        if tuple(short_conv or ()):
-            raise ValueError("short_conv is not supported by the B200 branch yet")
+        targets = tuple(short_conv) if isinstance(short_conv, (list, tuple)) else None
+        if targets is None or any(t not in ("q", "k", "v") for t in targets) or len(set(targets)) != len(targets):
+            raise ValueError(f"short_conv={short_conv!r}; expected a distinct subset of ('q', 'k', 'v')")
         self.num_heads, self.head_dim = num_heads, head_dim
         self.bridge = bridge
         self.a_fp32 = a_fp32
         self.delta_rule = delta_rule
-        self.short_conv = None
+        # None rather than a disabled module when off, so conv-less checkpoints keep
+        # their exact parameter set (branch.py:68-78).
+        from .short_conv import LinearAttentionSepConv
+        self.short_conv = LinearAttentionSepConv(num_heads * head_dim, targets) if targets else None
         self.alpha = FrameKDAAlpha(hidden_size, num_heads, head_dim)
         self.beta_proj = nn.Linear(hidden_size, num_heads, bias=False)
         self.output_gate = OutputGate(hidden_size, num_heads, head_dim,
@@ -308,12 +312,14 @@ class BidirectionalLinearBranch(nn.Module):
         if any(t.device.type != "cuda" or t.dtype != torch.bfloat16 for t in qkv_raw):
             raise ValueError("the B200 VDA branch requires CUDA BF16 Q/K/V")
         self._validate_sharded(heads, beta, gate, frame_mean, text_beta, text_qkv_raw)
+        if self.short_conv is not None and frame_size is None:
+            raise ValueError("short_conv needs the spatial grid; pass frame_size=(H, W)")
         n_heads = self.num_heads if heads is None else heads.stop - heads.start
         ref = xv if xv is not None else gate
         f, s = num_frames, tokens_per_frame
         if not skip_ends:
             return self._readout(xv, f, s, bounds, qkv_raw, text_x, text_qkv_raw, heads, beta,
-                                 gate, frame_mean, text_beta)
+                                 gate, frame_mean, text_beta, frame_size)
         if f <= 2:
             return ref.new_zeros(f * s, n_heads * self.head_dim, dtype=torch.bfloat16)
         inner = slice(s, (f - 1) * s)
@@ -322,7 +328,7 @@ class BidirectionalLinearBranch(nn.Module):
             [(lo - 1, hi - 1) for lo, hi in bounds[1:f - 1]], tuple(t[inner] for t in qkv_raw),
             text_x, text_qkv_raw, heads, None if beta is None else beta[inner],
             None if gate is None else gate[inner], None if frame_mean is None else frame_mean[1:-1],
-            text_beta)
+            text_beta, frame_size)
         out = readout.new_empty(f * s, readout.shape[-1])
         out[:s].zero_()
         out[(f - 1) * s:].zero_()
@@ -330,10 +336,13 @@ class BidirectionalLinearBranch(nn.Module):
         return out
 
     def _readout(self, xv, f, s, bounds, qkv_raw, text_x, text_qkv_raw, heads, beta, gate,
-                 frame_mean, text_beta):
+                 frame_mean, text_beta, frame_size=None):
         h = self.num_heads if heads is None else heads.stop - heads.start
         d = self.head_dim
         q, k, v = qkv_raw
+        if self.short_conv is not None:  # video rows only; the prompt has no grid
+            q, k, v = (self.short_conv.apply(name, t, f, frame_size, heads=heads)
+                       for name, t in zip(("q", "k", "v"), (q, k, v)))
         if beta is None:
             beta = torch.sigmoid(self.beta_proj(xv))
         beta = beta.to(torch.bfloat16).reshape(f * s, h)
