@@ -156,3 +156,112 @@ def test_routing_on_gloo_ranks(world):
                     p.terminate()
                 if p.pid is not None:
                     p.join()
+
+
+# ----------------------------------------------------------- branch-parallel layout
+def test_branch_parallel_layout():
+    """Rank roles and head ranges of the branch-parallel layout (ulysses_runtime.py:176-251):
+    the shipped B200 5 + 3 split of 40 heads, and the argument checks."""
+    roles = []
+    for rank in range(8):
+        rt = _runtime(rank, 8)
+        rt.enable_branch_parallel(5)
+        rt.configure(32760, 40)
+        roles.append((rt.branch_kind, rt.branch_first_head, rt.branch_heads, rt.heads_per_rank))
+        assert rt.branch_head_splits == (8, 8, 8, 8, 8, 14, 13, 13)
+        assert rt.splits == (4095,) * 8
+    assert roles == [("softmax", 8 * r, 8, 8) for r in range(5)] + \
+        [("linear", 0, 14, 14), ("linear", 14, 13, 13), ("linear", 27, 13, 13)]
+    rt = _runtime(0, 3)
+    rt.enable_branch_parallel(2)
+    rt.configure(9, 5)                                # heads need not divide the ranks
+    assert rt.branch_head_splits == (3, 2, 5)
+    for bad in (0, 3, -1, True, 1.0):
+        with pytest.raises(ValueError):
+            _runtime(0, 3).enable_branch_parallel(bad)
+    with pytest.raises(RuntimeError):
+        rt.enable_branch_parallel(1)                  # after the first configure
+    plain = _runtime(0, 3)
+    for attr in ("branch_kind", "branch_head_splits"):
+        with pytest.raises(RuntimeError):
+            getattr(plain, attr)
+    with pytest.raises(RuntimeError):
+        plain.branches_to_sequence(torch.zeros(1, 1, 1))
+    with pytest.raises(RuntimeError):                 # no dispatch communicators
+        rt.dispatch_fields_to_branches_overlapped(*([torch.zeros(3, 5, 4)] * 3), torch.zeros(3, 5),
+                                                  *([torch.zeros(3, 5, 4)] * 2), torch.zeros(3, 5),
+                                                  torch.zeros(3, 2))
+
+
+def _branch_worker(rank, world, rendezvous):
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=rendezvous, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=30))
+    try:
+        d, r = 4, 3
+        for softmax_ranks in range(1, world):
+            for rows, heads in ((7, world + 2), (10, 2 * world - 1)):
+                rt = _runtime(rank, world)
+                rt.enable_branch_parallel(softmax_ranks)
+                rt.configure(rows, heads)
+                lo, hi = rt.local_start, rt.local_end
+                g = torch.Generator().manual_seed(rows * 100 + heads)
+                for dtype in (torch.bfloat16, torch.float32):
+                    fields = [torch.randn(rows, heads, d, generator=g).to(dtype) for _ in range(5)]
+                    sq, sk, v, lq, lk = fields
+                    sgate, beta = (torch.rand(rows, heads, generator=g).to(dtype) for _ in range(2))
+                    shared = torch.randn(rows, r, generator=g).to(dtype)
+                    local = [t[lo:hi] for t in (sq, sk, v, sgate, lq, lk, beta, shared)]
+                    before = [t.clone() for t in local]
+                    packed, got_shared, pending = rt.dispatch_fields_to_branches_overlapped(*local)
+                    pending[0].wait()
+                    for t, b in zip(local, before):
+                        assert torch.equal(t, b)
+                    h0, hb = rt.branch_first_head, rt.branch_heads
+                    hs = slice(h0, h0 + hb)
+                    assert packed.shape == (rows, hb, 3 * d + 1)
+                    if rt.branch_kind == "softmax":
+                        want = torch.cat([sq[:, hs], sk[:, hs], v[:, hs], sgate[:, hs, None]], -1)
+                        assert got_shared is None
+                    else:
+                        want = torch.cat([lq[:, hs], lk[:, hs], v[:, hs], beta[:, hs, None]], -1)
+                        assert torch.equal(got_shared, shared)
+                    assert torch.equal(packed, want), (rank, softmax_ranks, rows, heads, dtype)
+                    # Reverse exchange: every owner gets all heads of both branches.
+                    soft_full = torch.randn(rows, heads, d, generator=g).to(dtype)
+                    lin_full = torch.randn(rows, heads, d, generator=g).to(dtype)
+                    mine = (soft_full if rt.branch_kind == "softmax" else lin_full)[:, hs]
+                    soft_local, lin_local = rt.branches_to_sequence(mine)
+                    assert torch.equal(soft_local, soft_full[lo:hi])
+                    assert torch.equal(lin_local, lin_full[lo:hi])
+                with pytest.raises(ValueError):
+                    rt.branches_to_sequence(torch.zeros(rows, rt.branch_heads + 1, d))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [3, 4])
+def test_branch_parallel_routing_on_gloo_ranks(world):
+    with tempfile.TemporaryDirectory() as directory:
+        ctx = multiprocessing.get_context("spawn")
+        procs = [ctx.Process(target=_branch_worker, args=(r, world, "file://" + directory + "/pg"))
+                 for r in range(world)]
+        old = os.environ.copy()
+        os.environ["CUDA_VISIBLE_DEVICES"] = ""
+        try:
+            for p in procs:
+                p.start()
+        finally:
+            os.environ.clear()
+            os.environ.update(old)
+        try:
+            deadline = time.monotonic() + 180
+            for p in procs:
+                p.join(max(0, deadline - time.monotonic()))
+            assert [p.exitcode for p in procs] == [0] * world
+        finally:
+            for p in procs:
+                if p.is_alive():
+                    p.terminate()
+                if p.pid is not None:
+                    p.join()

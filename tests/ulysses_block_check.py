@@ -5,7 +5,8 @@ rows on its own GPU (no exchange), once sequence-sharded through the Ulysses
 runtime (NCCL all-to-all around head-sharded attention, frame-sum all-reduce).
 The rank's shard of the two outputs must agree: the GEMMs and producers are
 row-independent and attention is head-independent, so the only difference is
-the summation order of the frame mean that feeds alpha.
+the summation order of the frame mean that feeds alpha.  The same holds for
+every branch-parallel layout (n softmax ranks + P - n VDA ranks, n = 1..P-1).
 """
 import os
 import sys
@@ -16,13 +17,19 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from vdn_b200.block import BlockConfig, HybridBlock  # noqa: E402
-from vdn_b200.ulysses import init_ulysses  # noqa: E402
+from vdn_b200.ulysses import UlyssesRuntime, init_ulysses  # noqa: E402
 
 
 def main():
     rt = init_ulysses("nccl", timeout_seconds=60)
     dev = rt.device
     failures = []
+    branch_runtimes = {}
+    for n_soft in range(1, rt.world_size):
+        brt = UlyssesRuntime(rank=rt.rank, world_size=rt.world_size, local_rank=rt.local_rank,
+                             device=dev, backend="nccl", timeout_seconds=60)
+        brt.enable_branch_parallel(n_soft)
+        branch_runtimes[n_soft] = brt
     for frames, tokens in ((4, 64), (3, 100)):
         cfg = BlockConfig(hidden=512, heads=4, head_dim=128, ffn=1024, radius=1, lora_rank=8)
         block = HybridBlock(cfg, seed=3, device=dev)
@@ -66,6 +73,19 @@ def main():
         del graph
         for ex in rt._exchanges.values():
             ex.check()                              # no device fence timed out
+        # Branch-parallel layouts: n softmax ranks + P - n VDA ranks.
+        for n_soft, brt in branch_runtimes.items():
+            brt.sequence_length = 0
+            brt.configure(T, cfg.heads)
+            shard = block(x[brt.local_start:brt.local_end].contiguous(), temb, frames, tokens, brt)
+            torch.cuda.synchronize()
+            want = full[brt.local_start:brt.local_end].double()
+            err = float((shard.double() - want).norm() / want.norm())
+            ok = bool(torch.isfinite(shard).all()) and err < 2e-3
+            print(f"rank {brt.rank} branch{n_soft}+{brt.world_size - n_soft} ({brt.branch_kind}) "
+                  f"frames={frames} tokens={tokens} rows={shard.shape[0]} rel_l2={err:.3e}", flush=True)
+            if not ok:
+                failures.append((f"branch{n_soft}", frames, tokens, err))
         # The two exchanges move the same bytes: identical block outputs.
         if not torch.equal(shards["alltoall"], shards["peer"]):
             d = (shards["alltoall"].float() - shards["peer"].float()).abs().max().item()

@@ -193,7 +193,12 @@ class HybridBlock(nn.Module):
         idx = torch.zeros(rows, dtype=torch.int64, device=dev)
         y1, q1, s1, _ = launch_prenorm_quantize(x, self.norm1, cfg.eps, scale_msa.view(1, hd),
                                                 shift_msa.view(1, hd), idx, write_bf16=True)
-        if runtime is not None and runtime.world_size > 1 and runtime.exchange_mode == "peer":
+        if runtime is not None and runtime.world_size > 1 and runtime.branch_parallel:
+            qkv = torch.empty(rows, 3 * hd, device=dev, dtype=torch.bfloat16)
+            self._gemm(q1, s1, self.qkv, rows, qkv, bias=self.qkv.bias)
+            first, second = self._attention_branch_parallel(qkv, self._gate_projections(y1), y1, frames,
+                                                            tokens, runtime)
+        elif runtime is not None and runtime.world_size > 1 and runtime.exchange_mode == "peer":
             first, second = self._attention_peer(y1, q1, s1, frames, tokens, runtime)
         else:
             qkv = torch.empty(rows, 3 * hd, device=dev, dtype=torch.bfloat16)
@@ -287,6 +292,55 @@ class HybridBlock(nn.Module):
         lq = self._quantize_grouped(flat, d, rows)
         return att, lq
 
+    def _attention_branch_parallel(self, qkv, g3, y1, frames, tokens, rt):
+        """Branch-parallel attention (src/inference/utils/ulysses.py:421-598): the softmax
+        ranks run the gated window softmax and the linear ranks the VDA branch, each
+        for its own contiguous share of ALL heads.
+
+        QKV is projected once by every sequence owner; one uneven all-to-all per
+        branch (two communicators) sends q | k | v | softmax gate to the softmax
+        ranks and q | k | v | beta plus the output gate's low-rank hidden to the
+        linear ranks, which apply the gate's `up` half to their own heads only.  One
+        reverse all-to-all returns both branches' heads to the sequence owner, where
+        each is quantised on its own (its own block scales) into the dual-K output
+        GEMM.
+        """
+        from .linear_attention import vda_forward
+        cfg = self.cfg
+        hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+        T = frames * tokens
+        rows = qkv.shape[0]
+        sums, work = rt.video_frame_mean_async(y1, frames, tokens)
+        q = qkv[:, :hd].view(rows, H, d)
+        k = qkv[:, hd:2 * hd].view(rows, H, d)
+        v = qkv[:, 2 * hd:].view(rows, H, d)
+        packed, shared, pending = rt.dispatch_fields_to_branches_overlapped(
+            q, k, v, g3[:, :H], q, k, g3[:, H:2 * H], g3[:, 2 * H:])
+        work.wait()
+        frame_mean = sums / tokens
+        hb, h0 = rt.branch_heads, rt.branch_first_head
+        # The wire rows are 3d + 1 wide; the kernels want 16-byte aligned operands.
+        fields = packed[:, :, :3 * d].contiguous()                        # [T, hb, 3d]
+        scalar = packed[:, :, 3 * d].contiguous()                         # [T, hb]
+        qh, kh, vh = fields[:, :, :d], fields[:, :, d:2 * d], fields[:, :, 2 * d:]
+        if rt.branch_kind == "softmax":
+            out = torch.empty(T, hb, d, device=qkv.device, dtype=torch.bfloat16)
+            window_softmax(qh, kh, vh, scalar, frames, tokens, cfg.radius, out=out)
+        else:
+            og = self.output_gate
+            cols = slice(h0 * d, (h0 + hb) * d)
+            lgate = torch.sigmoid(F.linear(shared.contiguous(), og.up.weight[cols], og.up.bias[cols]))
+            alpha = self.alpha.forward_native(frame_mean, heads=slice(h0, h0 + hb))
+            out = vda_forward(qh, kh, vh, scalar, lgate.view(T, hb, d), alpha,
+                              window_bounds(frames, cfg.radius), frames, tokens,
+                              self.vda_norm).view(T, hb, d)
+        pending[0].wait()
+        del pending
+        softmax_local, linear_local = rt.branches_to_sequence(out)        # [rows, H, d] each
+        att = quantize_activation(softmax_local.view(rows, hd), check_finite=False)
+        lq = quantize_activation(linear_local.view(rows, hd), check_finite=False)
+        return att, lq
+
     def _attention_peer(self, y1, q1, s1, frames, tokens, rt):
         """Head-sharded attention with the exchange done by the producers (peer memory).
 
@@ -364,8 +418,9 @@ class BlockGraph:
     """
 
     def __init__(self, block: HybridBlock, x, temb, frames, tokens, runtime=None, warmup=2):
-        if runtime is not None and runtime.world_size > 1 and runtime.exchange_mode != "peer":
-            raise ValueError("CUDA-graph capture needs the peer exchange at world_size > 1")
+        if runtime is not None and runtime.world_size > 1 and (runtime.exchange_mode != "peer"
+                                                               or runtime.branch_parallel):
+            raise ValueError("CUDA-graph capture needs the standard peer exchange at world_size > 1")
         self.block, self.x, self.temb = block, x, temb
         self.frames, self.tokens, self.runtime = frames, tokens, runtime
         dev = x.device
