@@ -442,8 +442,12 @@ def bench_block(args, torch, dist, rank, world):
     lo, hi = 0, T
     if world > 1:
         runtime = init_ulysses("nccl")
+        if args.softmax_ranks:
+            runtime.enable_branch_parallel(args.softmax_ranks)
         runtime.configure(T, BLOCK_CFG["heads"])
         lo, hi = runtime.local_start, runtime.local_end
+    if args.softmax_ranks and (world < 2 or not args.eager):
+        raise SystemExit("--softmax-ranks needs --gpus >= 2 and --eager (NCCL all-to-alls are not captured)")
     g = torch.Generator(device=dev).manual_seed(1234)
     x_full = torch.randn(T, BLOCK_CFG["hidden"], device=dev, generator=g).bfloat16()
     temb = torch.randn(BLOCK_CFG["hidden"], device=dev, generator=g)
@@ -533,7 +537,7 @@ def bench_block(args, torch, dist, rank, world):
                 "h2d_bytes_per_step": x_host[0].numel() * 2, "d2h_bytes_per_step": out_host[0].numel() * 2,
                 "steps": e2e_steps, "copies": "per step; overlapped with neighbouring steps"
                 if not args.eager and world == 1 else "per step; serial"},
-        "gpu_launches": block.launches_per_forward(world) * args.steps,
+        "gpu_launches": block.launches_per_forward(world, runtime) * args.steps,
         "launch": "eager" if args.eager else "cuda_graph",
         "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (QKV, %d x 15360 x 5120)" % rows,
                      "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
@@ -548,6 +552,10 @@ def bench_block(args, torch, dist, rank, world):
     }
     if runtime is not None:
         rec["config"]["exchange"] = runtime.exchange_mode
+        if runtime.branch_parallel:
+            rec["config"]["exchange"] = "nccl all-to-all (two dispatch communicators)"
+            rec["config"]["parallelism"] = (f"ulysses branch-parallel {runtime.softmax_ranks} softmax + "
+                                            f"{world - runtime.softmax_ranks} VDA ranks")
         runtime.close()
     return rec
 
@@ -597,6 +605,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="block: launch eagerly instead of a CUDA graph")
+    ap.add_argument("--softmax-ranks", type=int, default=0,
+                    help="block, N > 1: branch-parallel layout with this many softmax ranks (needs --eager)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -172,12 +172,20 @@ class HybridBlock(nn.Module):
             return out
         return join
 
-    def launches_per_forward(self, world_size=1):
+    def launches_per_forward(self, world_size=1, runtime=None):
         """Kernels of this library launched per block forward (for bench accounting)."""
-        # prenorm, QKV GEMM, window merge, VDA (5), quantise VDA out, O GEMM, prenorm,
-        # FFN up (+GELU quantise), FFN down; the peer exchange adds a second scatter
-        # quantiser, two side-input broadcasts and two fences
-        return 13 if world_size == 1 else 17
+        # Every layout: prenorm, QKV GEMM, output GEMM, prenorm, FFN up (+GELU
+        # quantise), FFN down.  Window softmax: the merge (the attention legs are
+        # cuDNN).  VDA: alpha (2), statistics, factors, scans, gather, readout.
+        common, softmax, vda = 6, 1, 7
+        if world_size == 1:
+            return common + softmax + vda + 1                  # + quantise the VDA output
+        if runtime is not None and runtime.branch_parallel:    # one branch per rank, 2 quantisers
+            return common + (softmax if runtime.branch_kind == "softmax" else vda) + 2
+        if runtime is not None and runtime.exchange_mode != "peer":
+            return common + softmax + vda + 2                  # NCCL all-to-alls, 2 quantisers
+        # peer exchange: two scatter quantisers, two side-input broadcasts, two fences
+        return common + softmax + vda + 6
 
     # ---------------------------------------------------------------- forward
     @torch.no_grad()
