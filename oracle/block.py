@@ -57,28 +57,59 @@ def window_attention(q, k, v, frames, tokens, radius, scale):
     return out
 
 
-def block_reference(x, temb, w, frames, tokens, cfg, alpha_fn):
-    """x [T, hidden] bf16 values; w: dict of dequantised fp32 weights / biases."""
+def block_reference(x, temb, w, frames, tokens, cfg, alpha_fn, text_rows=0):
+    """x [text_rows + T, hidden] bf16 values; w: dict of dequantised fp32 weights / biases.
+
+    The attention layout follows cfg.radius / cfg.chunk / cfg.anchor_frames /
+    cfg.text_state (defaults: +-radius frames, no anchors, no text seed) with the
+    text rows (global, dense) first: window.py:56-111 for the softmax,
+    branch.py:256-402 for the linear branch (anchor frames dropped under "both",
+    half the prompt state seeding both scans), hybrid_attention.py:200-255 for
+    the merge (to_out on every row, to_out_linear on the video rows only, and not
+    at all when every window spans the clip).  w["o_b"] is to_out's plus
+    to_out_linear's bias; w["o_b_softmax"] (to_out's alone) is needed for text rows
+    or a clip-spanning window.
+    """
+    from . import window as owin
     hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+    chunk = getattr(cfg, "chunk", 0)
+    anchors = getattr(cfg, "anchor_frames", "none")
+    L = text_rows
     T = frames * tokens
+    n = L + T
     x = x.float()
     ada = _bf16(F.silu(_bf16(temb.float())) @ w["adaln_w"].T + w["adaln_b"]).view(6, hd)
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = ada
     y1 = prenorm(x, w["norm1"], scale_msa, shift_msa, cfg.eps)
     qkv = _linear(_qdq(y1), w["qkv"], w["qkv_b"])
-    q, k, v = (qkv[:, i * hd:(i + 1) * hd].reshape(T, H, d) for i in range(3))
+    q, k, v = (qkv[:, i * hd:(i + 1) * hd].reshape(n, H, d) for i in range(3))
     sgate = _bf16(torch.sigmoid(_bf16(y1 @ w["sg_w"].T + w["sg_b"])))
     beta = _bf16(torch.sigmoid(_bf16(y1 @ w["beta_w"].T)))
     lg = _bf16(torch.sigmoid(_bf16(_bf16(y1 @ w["og_down"].T) @ w["og_up"].T + w["og_b"])))
-    att = window_attention(q, k, v, frames, tokens, cfg.radius, d ** -0.5)
+    bounds = owin.window_bounds(frames, cfg.radius, chunk)
+    if L or chunk or anchors != "none":
+        att = owin.window_attention(q, k, v, frames, tokens, bounds, d ** -0.5, text_rows=L,
+                                    anchor_frames=anchors)
+    else:
+        att = window_attention(q, k, v, frames, tokens, cfg.radius, d ** -0.5)
     att = _bf16(_bf16(att) * sgate[..., None])
-    frame_mean = y1.view(frames, tokens, hd).mean(1)
-    alpha = alpha_fn(frame_mean).numpy()
-    lin = ovda.readout(q.numpy(), k.numpy(), v.numpy(), beta.numpy(), lg.view(T, H, d).numpy(),
-                       alpha, ovda.window_bounds(frames, cfg.radius), frames, tokens)
-    lin = torch.from_numpy(lin)
-    o = _bf16(_qdq(att.reshape(T, hd)) @ w["o"].T + _qdq(lin) @ w["ol"].T)
-    o = _bf16(o + w["o_b"].float())
+    o = torch.empty(n, hd)
+    if L:
+        o[:L] = _bf16(_bf16(_qdq(att[:L].reshape(L, hd)) @ w["o"].T) + w["o_b_softmax"].float())
+    av = _qdq(att[L:].reshape(T, hd)) @ w["o"].T
+    if owin.full_cover(bounds, frames):
+        o[L:] = _bf16(_bf16(av) + w["o_b_softmax"].float())
+    else:
+        frame_mean = y1[L:].view(frames, tokens, hd).mean(1)
+        alpha = alpha_fn(frame_mean).numpy()
+        seed = None
+        if getattr(cfg, "text_state", False) and L:
+            seed = ovda.text_seed(k[:L].numpy(), v[:L].numpy(), beta[:L].numpy())
+        lin = ovda.branch_forward(q[L:].numpy(), k[L:].numpy(), v[L:].numpy(), beta[L:].numpy(),
+                                  lg[L:].view(T, H, d).numpy(), alpha, bounds, frames, tokens,
+                                  skip_ends=anchors == "both", seed=seed)
+        lin = torch.from_numpy(lin)
+        o[L:] = _bf16(_bf16(av + _qdq(lin) @ w["ol"].T) + w["o_b"].float())
     x1 = _bf16(x + _bf16(gate_msa * o))
     y2 = prenorm(x1, w["norm2"], scale_mlp, shift_mlp, cfg.eps)
     up = _linear(_qdq(y2), w["up"], w["up_b"])

@@ -16,7 +16,10 @@ It imports the reference (ec-jt/vdn) and records, on seeded synthetic inputs:
     gather_linear_state (scan.py, delta_rule.py) on one d=128 case;
   * the separable short conv LinearAttentionSepConv (features.py:133-209): its
     spatial 5x5 half, the eager temporal 5-tap shift and the activated k / v
-    features, on two grids (--sepconv-only regenerates just these).
+    features, on two grids (--sepconv-only regenerates just these);
+  * window_softmax_reference (src/models/softmax_attention/window.py:56-111) with
+    global text rows, frame and chunk-aligned windows and every anchor mode
+    (--window-only regenerates just these).
 
 Nothing at test time reads the reference; the tests read only these .npz files.
 """
@@ -158,14 +161,58 @@ def sepconv_fixtures(features_mod):
     np.savez_compressed(HERE / "sepconv_golden.npz", **out)
 
 
-def main(ref_root: str, sepconv_only: bool = False):
+WINDOW_CASES = {
+    # name: text rows, frames, tokens per frame, heads, head dim, radius, chunk, anchors
+    "frame_text_both": (5, 6, 8, 2, 16, 1, 0, "both"),
+    "chunk_text_columns": (3, 7, 6, 2, 16, 1, 2, "columns"),
+    "frame_rows": (0, 5, 8, 3, 16, 0, 0, "rows"),
+    "frame_text_none": (4, 4, 8, 2, 16, 1, 0, "none"),
+    "chunk_both_short_last": (2, 5, 4, 2, 32, 0, 2, "both"),
+}
+
+
+def window_fixtures(ref_root: str):
+    """window_softmax_reference (src/models/softmax_attention/window.py:56-111) on CPU,
+    fp32, with global text rows first, frame and chunk-aligned windows and every
+    anchor mode.  The module is loaded from its file: the package __init__ imports
+    diffusers."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "ref_window", str(Path(ref_root) / "src/models/softmax_attention/window.py"))
+    win = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(win)
+    from src.models.sequence_layout import SequenceLayout
+    out = {}
+    for i, (name, (L, f, s, h, d, radius, chunk, anchors)) in enumerate(WINDOW_CASES.items()):
+        g = torch.Generator().manual_seed(300 + i)
+        n = L + f * s
+        q, k, v = (torch.randn(n, h, d, generator=g) for _ in range(3))
+        layout = SequenceLayout(seq_len=n, video_start=L, num_frames=f, tokens_per_frame=s,
+                                text_start=0, text_len=L)
+        bounds = win.window_bounds(f, radius, chunk)
+        with torch.no_grad():
+            o = win.window_softmax_reference(q, k, v, layout, bounds, d ** -0.5, anchor_frames=anchors)
+        out[f"{name}_q"], out[f"{name}_k"], out[f"{name}_v"] = q.numpy(), k.numpy(), v.numpy()
+        out[f"{name}_out"] = o.numpy()
+        out[f"{name}_geom"] = np.array([L, f, s, h, d, radius, chunk], np.int64)
+        out[f"{name}_bounds"] = np.array(bounds, np.int64)
+        out[f"{name}_anchors"] = np.array(anchors)
+    np.savez_compressed(HERE / "window_golden.npz", **out)
+
+
+def main(ref_root: str, sepconv_only: bool = False, window_only: bool = False):
     sys.path.insert(0, ref_root)
     torch.set_num_threads(8)
+    if window_only:
+        window_fixtures(ref_root)
+        print("wrote window_golden.npz")
+        return
     from src.models.linear_attention import features as features_mod
     sepconv_fixtures(features_mod)
     if sepconv_only:
         print("wrote sepconv_golden.npz")
         return
+    window_fixtures(ref_root)
     from src.models.ops.mxfp8_quant import quantize_cpu
     from src.models.linear_attention import scan, delta_rule
     from src.models.linear_attention.branch import BidirectionalLinearBranch
@@ -191,5 +238,6 @@ def main(ref_root: str, sepconv_only: bool = False):
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     if len(args) != 1:
-        raise SystemExit("usage: make_golden.py <path to the ec-jt/vdn checkout> [--sepconv-only]")
-    main(args[0], sepconv_only="--sepconv-only" in sys.argv)
+        raise SystemExit("usage: make_golden.py <path to the ec-jt/vdn checkout> "
+                         "[--sepconv-only | --window-only]")
+    main(args[0], sepconv_only="--sepconv-only" in sys.argv, window_only="--window-only" in sys.argv)

@@ -41,10 +41,26 @@ __all__ = ["HybridBlock", "BlockConfig", "BlockGraph", "BlockPipeline"]
 
 
 class BlockConfig:
+    """Block geometry and the attention layout knobs of HybridAttention
+    (src/models/hybrid_attention.py:45-80): `radius` / `chunk` (frame window, or
+    K-frame chunk-aligned window when chunk > 0), `anchor_frames` ("none",
+    "columns", "rows", "both"; "both" also drops frames 0 and F-1 from the linear
+    branch) and `text_state` (seed both VDA scans with half the prompt state)."""
+
     def __init__(self, hidden=5120, heads=40, head_dim=128, ffn=13824, radius=1, lora_rank=32,
-                 eps=1e-6, gelu="tanh"):
+                 eps=1e-6, gelu="tanh", chunk=0, anchor_frames="none", text_state=False):
         self.hidden, self.heads, self.head_dim, self.ffn = hidden, heads, head_dim, ffn
         self.radius, self.lora_rank, self.eps, self.gelu = radius, lora_rank, eps, gelu
+        if anchor_frames not in ("none", "columns", "rows", "both"):
+            raise ValueError(f"anchor_frames={anchor_frames!r}")
+        if chunk < 0 or radius < 0:
+            raise ValueError("radius and chunk must be >= 0")
+        self.chunk, self.anchor_frames, self.text_state = chunk, anchor_frames, bool(text_state)
+
+    @property
+    def plain_window(self) -> bool:
+        """The BASELINE config-3 layout: a +-radius frame window, no anchors."""
+        return self.chunk == 0 and self.anchor_frames == "none"
 
 
 class _Packed:
@@ -189,15 +205,26 @@ class HybridBlock(nn.Module):
 
     # ---------------------------------------------------------------- forward
     @torch.no_grad()
-    def forward(self, x, temb, frames, tokens, runtime=None):
-        """x: this rank's rows [T_local, hidden] bf16 (all T rows when runtime is None)."""
+    def forward(self, x, temb, frames, tokens, runtime=None, text_rows=0):
+        """x: this rank's rows [T_local, hidden] bf16 (all T rows when runtime is None).
+
+        text_rows > 0 (one GPU): x is the packed sequence [text_rows + frames * tokens,
+        hidden], prompt rows first as global rows: dense softmax in both directions,
+        no linear-branch output, and (cfg.text_state) the prompt seeds both VDA scans.
+        """
         cfg = self.cfg
         hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
         T = frames * tokens
         rows = x.shape[0]
         dev = x.device
-        ada = self.adaln(F.silu(temb.to(torch.bfloat16)).view(1, hd)).view(6, hd)
-        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = ada
+        general = text_rows > 0 or not cfg.plain_window
+        if general:
+            if runtime is not None and runtime.world_size > 1:
+                raise ValueError("text rows, anchor frames and chunk windows run on one GPU")
+            if rows != text_rows + T:
+                raise ValueError("x must hold text_rows + frames * tokens rows")
+            return self._forward_general(x, temb, frames, tokens, text_rows)
+        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self._adaln(temb)
         idx = torch.zeros(rows, dtype=torch.int64, device=dev)
         y1, q1, s1, _ = launch_prenorm_quantize(x, self.norm1, cfg.eps, scale_msa.view(1, hd),
                                                 shift_msa.view(1, hd), idx, write_bf16=True)
@@ -225,23 +252,99 @@ class HybridBlock(nn.Module):
         x1 = torch.empty_like(x)
         self._gemm(first[0], first[1], self.o, rows, x1, second=(second, self.ol),
                    bias=self.o_bias, resid=x, gate=gate_msa.contiguous())
+        return self._ffn(x1, shift_mlp, scale_mlp, gate_mlp, idx)
+
+    def _adaln(self, temb):
+        hd = self.cfg.hidden
+        return self.adaln(F.silu(temb.to(torch.bfloat16)).view(1, hd)).view(6, hd)
+
+    def _ffn(self, x1, shift_mlp, scale_mlp, gate_mlp, idx):
+        """x2 = x1 + gate_mlp * FFN(prenorm(x1)) (GELU-tanh and its MXFP8 quantise fused into
+        the FFN-up epilogue)."""
+        cfg = self.cfg
+        hd, rows, dev = cfg.hidden, x1.shape[0], x1.device
         _, q2, s2, _ = launch_prenorm_quantize(x1, self.norm2, cfg.eps, scale_mlp.view(1, hd),
                                                shift_mlp.view(1, hd), idx, write_bf16=False)
-        # FFN up with GELU and the MXFP8 quantisation of the down projection's
-        # input fused into the GEMM epilogue (bit-identical to GEMM -> bf16 ->
-        # launch_gelu_quantize).
         w = self.up
         q3 = torch.empty(q2.shape[0], w.n, device=dev, dtype=torch.uint8)
         s3 = torch.empty(q2.shape[0] * w.n // 32, device=dev, dtype=torch.uint8)
         if cfg.gelu != "tanh":
             raise ValueError("the fused FFN epilogue implements GELU (tanh)")
-        act = _lib.ACT_GELU_TANH
         _lib.call("vdn_mxfp8_gemm_act_quantize", _lib.ptr(q2), _lib.ptr(s2), _lib.ptr(w.q), _lib.ptr(w.s),
-                  w.k_pad, _lib.ptr(w.bias), q2.shape[0], w.n, w.n_pad, rows, act, _lib.ptr(q3),
-                  _lib.ptr(s3), _lib.ptr(self._status), _lib.stream_of(dev))
-        x2 = torch.empty_like(x)
+                  w.k_pad, _lib.ptr(w.bias), q2.shape[0], w.n, w.n_pad, rows, _lib.ACT_GELU_TANH,
+                  _lib.ptr(q3), _lib.ptr(s3), _lib.ptr(self._status), _lib.stream_of(dev))
+        x2 = torch.empty_like(x1)
         self._gemm(q3, s3, self.down, rows, x2, bias=self.down.bias, resid=x1, gate=gate_mlp.contiguous())
         return x2
+
+    def _forward_general(self, x, temb, frames, tokens, L):
+        """One-GPU block with text rows, anchor frames and / or chunk-aligned windows
+        (hybrid_attention.py:178-255 with branch.py:256-402).
+
+        The softmax covers every row (text rows dense, video rows their window plus
+        the anchors); the VDA branch covers the video rows it owns (all of them, or
+        frames 1..F-2 under anchor_frames == "both") and is skipped when every window
+        spans the clip.  The output projection runs as two GEMMs: the text rows take
+        to_out alone, the video rows to_out + to_out_linear in one dual-K accumulator.
+        """
+        from .linear_attention import vda_forward, vda_text_seed
+        cfg = self.cfg
+        hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+        T = frames * tokens
+        n = x.shape[0]
+        dev = x.device
+        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self._adaln(temb)
+        idx = torch.zeros(n, dtype=torch.int64, device=dev)
+        y1, q1, s1, _ = launch_prenorm_quantize(x, self.norm1, cfg.eps, scale_msa.view(1, hd),
+                                                shift_msa.view(1, hd), idx, write_bf16=True)
+        qkv = torch.empty(n, 3 * hd, device=dev, dtype=torch.bfloat16)
+        self._gemm(q1, s1, self.qkv, n, qkv, bias=self.qkv.bias)
+        g3 = self._gate_projections(y1)
+        q = qkv[:, :hd].view(n, H, d)
+        k = qkv[:, hd:2 * hd].view(n, H, d)
+        v = qkv[:, 2 * hd:].view(n, H, d)
+        sgate, beta = g3[:, :H], g3[:, H:2 * H]
+        bounds = window_bounds(frames, cfg.radius, cfg.chunk)
+        linear_active = not all(lo <= 0 and hi >= frames - 1 for lo, hi in bounds)
+
+        def branch():  # VDA over the video rows, on the side stream
+            og = self.output_gate
+            lgate = torch.sigmoid(F.linear(g3[L:, 2 * H:], og.up.weight, og.up.bias)).view(T, H, d)
+            frame_mean = y1[L:].view(frames, tokens, hd).mean(1, dtype=torch.float32)
+            alpha = self.alpha.forward_native(frame_mean)
+            seed = vda_text_seed(k[:L], v[:L], beta[:L], 0.5) if cfg.text_state and L else None
+            qv, kv, vv, bv = q[L:], k[L:], v[L:], beta[L:]
+            if cfg.anchor_frames != "both":
+                lin = vda_forward(qv, kv, vv, bv, lgate, alpha, bounds, frames, tokens, self.vda_norm,
+                                  seed=seed)
+            else:  # frames 0 and F-1 are exact softmax: dropped from the branch, rows zero
+                lin = torch.zeros(T, hd, device=dev, dtype=torch.bfloat16)
+                if frames > 2:
+                    inner = slice(tokens, (frames - 1) * tokens)
+                    lin[inner] = vda_forward(qv[inner], kv[inner], vv[inner], bv[inner], lgate[inner],
+                                             alpha[1:-1].contiguous(),
+                                             [(lo - 1, hi - 1) for lo, hi in bounds[1:frames - 1]],
+                                             frames - 2, tokens, self.vda_norm, seed=seed)
+            return quantize_activation(lin, check_finite=False)
+
+        join = self._vda_side(branch, dev) if linear_active else None
+        att = torch.empty(n, H, d, device=dev, dtype=torch.bfloat16)
+        window_softmax(q, k, v, sgate, frames, tokens, cfg.radius, out=att, bounds=bounds, text_rows=L,
+                       anchor_frames=cfg.anchor_frames)
+        att = att.view(n, hd)
+        lin = join() if join is not None else None
+        x1 = torch.empty_like(x)
+        gm = gate_msa.contiguous()
+        if L:
+            aq, as_ = quantize_activation(att[:L], check_finite=False)
+            self._gemm(aq, as_, self.o, L, x1[:L], bias=self.o.bias, resid=x[:L], gate=gm)
+        aq, as_ = quantize_activation(att[L:], check_finite=False)
+        if lin is None:
+            self._gemm(aq, as_, self.o, T, x1[L:], bias=self.o.bias, resid=x[L:], gate=gm)
+        else:
+            self._gemm(aq, as_, self.o, T, x1[L:], second=(lin, self.ol), bias=self.o_bias, resid=x[L:],
+                       gate=gm)
+        return self._ffn(x1, shift_mlp, scale_mlp, gate_mlp, idx)
 
     def _attention(self, qkv, sgate, beta, lgate, frame_mean, frames, tokens, heads):
         """Single-GPU attention: returns ((codes, scales) softmax, (codes, scales) VDA)."""
