@@ -27,6 +27,10 @@ Workloads:
         (15360, 5120), (5120, 5120), (13824, 5120), (5120, 13824); each step
         quantises the bf16 activation and runs the four GEMMs; metric = TFLOP/s.
         --rows M shrinks M (small profiling case).  N > 1: replicas.
+  stack BASELINE config 4 on one GPU: one denoise step = a 40-block stack of the
+        config-3 block over 512 text rows (packed first, dense softmax) + 60 x 1560
+        video rows, then the Euler update; --steps 8 is the 8-step loop; metric =
+        video tokens/s.  --depth / --frames shrink it (small case).
 """
 from __future__ import annotations
 
@@ -590,7 +594,136 @@ def cpu_baseline_block(threads):
             "3 frames x 1560 tokens (per-token work is constant in the frame count)"}
 
 
-CPU_BASELINES = {"block": cpu_baseline_block, "vda": cpu_baseline_vda, "gemm": cpu_baseline_gemm}
+# ---------------------------------------------------------------------- stack
+STACK_CFG = dict(F=60, S=1560, text_rows=512, depth=40, denoise_steps=8)
+
+# Kernels of this library each entry point launches (default 1; setup calls launch none).
+KERNELS_PER_CALL = {"vdn_vda_forward": 5, "vdn_frame_alpha": 2, "vdn_sepconv": 2,
+                    "vdn_peer_alloc": 0, "vdn_peer_free": 0, "vdn_ipc_handle": 0, "vdn_ipc_open": 0,
+                    "vdn_ipc_close": 0, "vdn_copy_async": 0, "vdn_mxfp8_quantize_host": 0,
+                    "vdn_last_error": 0, "vdn_mxfp8_padded_shape": 0, "vdn_vda_workspace_size": 0}
+
+
+def count_launches(fn):
+    """Run fn() once and count the kernels of this library it launches (by entry point)."""
+    from vdn_b200 import _lib
+    real = _lib.call
+    count = [0]
+
+    def counting(name, *a, **k):
+        count[0] += KERNELS_PER_CALL.get(name, 1)
+        return real(name, *a, **k)
+
+    _lib.call = counting
+    try:
+        fn()
+    finally:
+        _lib.call = real
+    return count[0]
+
+
+def bench_stack(args, torch, dist, rank, world):
+    """BASELINE config 4 on one GPU: the 8-step denoise loop of a 40-block stack over
+    512 text rows + 60 x 1560 video rows (text packed first as global rows)."""
+    from vdn_b200.block import BlockConfig
+    from vdn_b200.mxfp8_quant import quantize_activation
+    from vdn_b200.stack import HybridStack, denoise
+    if world > 1:
+        raise SystemExit("the stack workload runs on one GPU: the Ulysses paths do not shard text rows")
+    F = args.frames or STACK_CFG["F"]
+    S, L = STACK_CFG["S"], STACK_CFG["text_rows"]
+    depth = args.depth or STACK_CFG["depth"]
+    cfg = BlockConfig()
+    hd = cfg.hidden
+    T = F * S
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    stack = HybridStack(cfg, depth, seed=0, device=dev, init="device")
+    g = torch.Generator(device=dev).manual_seed(4321)
+    video = torch.randn(T, hd, device=dev, generator=g).bfloat16()
+    text = torch.randn(L, hd, device=dev, generator=g).bfloat16()
+    nsteps = STACK_CFG["denoise_steps"]
+    tembs = torch.randn(nsteps, hd, device=dev, generator=g)
+    packed = torch.empty(L + T, hd, device=dev, dtype=torch.bfloat16)
+    i = [0]
+
+    def step():  # one denoise step: the whole stack over [text | video], then the Euler update
+        j = i[0] % nsteps
+        denoise(stack, video, text, tembs[j:j + 1], F, S, packed=packed, dt=-1.0 / nsteps)
+        i[0] += 1
+
+    launches = count_launches(step)
+    with ClockSampler(dev.index) as clk:
+        ms = time_steps(torch, step, args.steps, args.warmup, dist, stream)
+    finite = bool(torch.isfinite(video).all())
+    per_step_ms = ms / args.steps
+    value = T / (per_step_ms * 1e-3)
+
+    # e2e: each step copies its inputs (latent + text context) in from pinned host memory
+    # and reads the updated latent back.
+    v_host = video.cpu().pin_memory()
+    t_host = text.cpu().pin_memory()
+    out_host = torch.empty_like(v_host).pin_memory()
+
+    def e2e_step():
+        video.copy_(v_host, non_blocking=True)
+        text.copy_(t_host, non_blocking=True)
+        step()
+        out_host.copy_(video, non_blocking=True)
+
+    e2e_steps = 2
+    e2e_ms = time_steps(torch, e2e_step, e2e_steps, 1, dist, stream) / e2e_steps
+
+    blk = stack.blocks[0]
+    n = L + T
+    y1 = torch.randn(n, hd, device=dev).bfloat16()
+    q1, s1 = quantize_activation(y1)
+    out = torch.empty(n, 3 * hd, device=dev, dtype=torch.bfloat16)
+    kt = kernel_times(torch, [("mxfp8_gemm_qkv", lambda: blk._gemm(q1, s1, blk.qkv, n, out,
+                                                                  bias=blk.qkv.bias))], 5, stream)
+    gemm_flops = 2 * n * 3 * hd * hd
+    achieved = gemm_flops / (kt["mxfp8_gemm_qkv"] * 1e-3) / 1e12
+    pk, src = peaks()
+    fp8_peak = 2 * pk["bf16_tflops"]
+    return {
+        "metric": "denoise-loop tokens/s (BASELINE config 4: 40-block stack, 60 x 1560 video + 512 text rows)",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_step_ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "mxfp8 GEMMs (fp32 accumulate), bf16 activations",
+        "data": "synthetic (seeded N(0,1) latent, text context and timestep embeddings; random-init "
+                "weights drawn on the device)",
+        "config": {"workload": "denoise_stack_config4", "frames": F, "tokens_per_frame": S, "text_rows": L,
+                   "depth": depth, "denoise_steps": nsteps, "step": "one denoise step (whole stack + Euler update)",
+                   "hidden": hd, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": cfg.ffn,
+                   "window": "+-1 frame, text rows dense", "parallelism": "single GPU",
+                   "l2": "per-step working set (weights 23 GB, activations > 1 GB) larger than L2",
+                   "latent_finite_after_timing": finite},
+        "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": v_host.numel() * 2 + t_host.numel() * 2,
+                "d2h_bytes_per_step": out_host.numel() * 2, "steps": e2e_steps, "copies": "per step; serial"},
+        "gpu_launches": launches * args.steps,
+        "launch": "eager",
+        "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (QKV, %d x 15360 x 5120)" % n,
+                     "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / fp8_peak, 4), "traffic": None,
+                     "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']}): the FP8 rate",
+                     "algorithmic_flops_per_launch": gemm_flops},
+        "kernels_ms": {k_: round(v_, 4) for k_, v_ in kt.items()},
+        "clocks": clk.summary(),
+    }
+
+
+def cpu_baseline_stack(threads):
+    """The block CPU baseline divided over the stack's depth (per-token work of one step)."""
+    base = cpu_baseline_block(threads)
+    base["value"] = round(base["value"] / STACK_CFG["depth"], 3)
+    base["sample"] = ("reference block composition, 3 frames x 1560 tokens, divided by the 40 blocks "
+                      "of one denoise step (text rows not included)")
+    return base
+
+
+CPU_BASELINES = {"block": cpu_baseline_block, "vda": cpu_baseline_vda, "gemm": cpu_baseline_gemm,
+                 "stack": cpu_baseline_stack}
 
 
 # ---------------------------------------------------------------------- main
@@ -599,9 +732,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="block", choices=["block", "vda", "gemm"])
+    ap.add_argument("--workload", default="block", choices=["block", "vda", "gemm", "stack"])
     ap.add_argument("--rows", type=int, default=0, help="gemm: M override (small profiling case)")
-    ap.add_argument("--frames", type=int, default=0, help="vda: frame-count override (small case)")
+    ap.add_argument("--frames", type=int, default=0, help="vda / stack: frame-count override (small case)")
+    ap.add_argument("--depth", type=int, default=0, help="stack: block-count override (small case)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="block: launch eagerly instead of a CUDA graph")
@@ -629,6 +763,10 @@ def main():
             meta = dict(metric="hybrid-block tokens/s (BASELINE config 3, 32760 tokens)",
                         unit="tokens/s", scaling="strong",
                         config={"workload": "hybrid_block_config3", **BLOCK_CFG})
+        elif args.workload == "stack":
+            meta = dict(metric="denoise-loop tokens/s (BASELINE config 4: 40-block stack, 60 x 1560 video + "
+                               "512 text rows)", unit="tokens/s", scaling="strong",
+                        config={"workload": "denoise_stack_config4", **STACK_CFG})
         elif args.workload == "gemm":
             meta = dict(metric="MXFP8 GEMM TFLOP/s, BASELINE config 1 sweep (activation quantised each step)",
                         unit="TFLOP/s", scaling="weak",
@@ -660,6 +798,8 @@ def main():
         torch.cuda.set_device(0)
     if args.workload == "block":
         rec = bench_block(args, torch, dist, rank, world)
+    elif args.workload == "stack":
+        rec = bench_stack(args, torch, dist, rank, world)
     elif args.workload == "gemm":
         rec = bench_gemm(args, torch, dist, rank, world)
     else:
