@@ -89,7 +89,12 @@ def test_block_layouts_refuse_ulysses(cuda):
     cfg = BlockConfig(hidden=256, heads=2, head_dim=128, ffn=512, lora_rank=8, anchor_frames="both")
     block = HybridBlock(cfg, seed=1, device=cuda)
     x = torch.zeros(4 * 64, 256, dtype=torch.bfloat16, device=cuda)
-    with pytest.raises(ValueError):
-        block(x, torch.zeros(256, device=cuda), 4, 64, SimpleNamespace(world_size=2))
+    peer = SimpleNamespace(world_size=2, exchange_mode="peer", branch_parallel=False)
+    with pytest.raises(ValueError):                       # layouts shard through the all-to-all only
+        block(x, torch.zeros(256, device=cuda), 4, 64, peer)
+    a2a = SimpleNamespace(world_size=2, exchange_mode="alltoall", branch_parallel=False,
+                          sequence_length=4 * 64 + 8, local_start=0, local_end=132)
+    with pytest.raises(ValueError):                       # runtime configured for another geometry
+        block(x, torch.zeros(256, device=cuda), 4, 64, a2a)
     with pytest.raises(ValueError):
         block(x, torch.zeros(256, device=cuda), 4, 64, text_rows=3)

@@ -32,4 +32,4 @@ def test_ulysses_block_matches_unsharded():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=os.path.dirname(here))
     res = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
-    assert res.stdout.count("rel_l2") == 2 * (3 + n - 1) * n
+    assert res.stdout.count("rel_l2") == 2 * (4 + n - 1) * n

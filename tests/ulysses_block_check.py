@@ -6,7 +6,8 @@ runtime (NCCL all-to-all around head-sharded attention, frame-sum all-reduce).
 The rank's shard of the two outputs must agree: the GEMMs and producers are
 row-independent and attention is head-independent, so the only difference is
 the summation order of the frame mean that feeds alpha.  The same holds for
-every branch-parallel layout (n softmax ranks + P - n VDA ranks, n = 1..P-1).
+every branch-parallel layout (n softmax ranks + P - n VDA ranks, n = 1..P-1) and
+for a packed sequence with text rows first and anchor frames (all-to-all exchange).
 """
 import os
 import sys
@@ -30,6 +31,8 @@ def main():
                              device=dev, backend="nccl", timeout_seconds=60)
         brt.enable_branch_parallel(n_soft)
         branch_runtimes[n_soft] = brt
+    text_rt = UlyssesRuntime(rank=rt.rank, world_size=rt.world_size, local_rank=rt.local_rank,
+                             device=dev, backend="nccl", timeout_seconds=60, exchange_mode="alltoall")
     for frames, tokens in ((4, 64), (3, 100)):
         cfg = BlockConfig(hidden=512, heads=4, head_dim=128, ffn=1024, radius=1, lora_rank=8)
         block = HybridBlock(cfg, seed=3, device=dev)
@@ -86,6 +89,28 @@ def main():
                   f"frames={frames} tokens={tokens} rows={shard.shape[0]} rel_l2={err:.3e}", flush=True)
             if not ok:
                 failures.append((f"branch{n_soft}", frames, tokens, err))
+        # Text rows packed first, anchor frames and the text seed through the all-to-all.
+        L = 16
+        tcfg = BlockConfig(hidden=512, heads=4, head_dim=128, ffn=1024, radius=1, lora_rank=8,
+                           anchor_frames="both", text_state=True)
+        tblock = HybridBlock(tcfg, seed=4, device=dev)
+        with torch.random.fork_rng(devices=[]):
+            torch.manual_seed(12)
+            torch.nn.init.normal_(tblock.softmax_gate.weight, std=0.05)
+        xt = torch.randn(L + T, tcfg.hidden, generator=g).bfloat16().to(dev)
+        tfull = tblock(xt, temb, frames, tokens, text_rows=L)
+        text_rt.sequence_length = 0
+        text_rt.configure(L + T, tcfg.heads)
+        lo, hi = text_rt.local_start, text_rt.local_end
+        shard = tblock(xt[lo:hi].contiguous(), temb, frames, tokens, text_rt, text_rows=L)
+        torch.cuda.synchronize()
+        want = tfull[lo:hi].double()
+        err = float((shard.double() - want).norm() / want.norm())
+        ok = bool(torch.isfinite(shard).all()) and err < 2e-3
+        print(f"rank {rt.rank} text{L}+anchors frames={frames} tokens={tokens} rows={shard.shape[0]} "
+              f"rel_l2={err:.3e}", flush=True)
+        if not ok:
+            failures.append(("text rows", frames, tokens, err))
         # The two exchanges move the same bytes: identical block outputs.
         if not torch.equal(shards["alltoall"], shards["peer"]):
             d = (shards["alltoall"].float() - shards["peer"].float()).abs().max().item()

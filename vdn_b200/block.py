@@ -224,9 +224,11 @@ class HybridBlock(nn.Module):
     def forward(self, x, temb, frames, tokens, runtime=None, text_rows=0):
         """x: this rank's rows [T_local, hidden] bf16 (all T rows when runtime is None).
 
-        text_rows > 0 (one GPU): x is the packed sequence [text_rows + frames * tokens,
-        hidden], prompt rows first as global rows: dense softmax in both directions,
-        no linear-branch output, and (cfg.text_state) the prompt seeds both VDA scans.
+        text_rows > 0: x is the packed sequence [text_rows + frames * tokens, hidden] (or
+        this rank's rows of it), prompt rows first as global rows: dense softmax in both
+        directions, no linear-branch output, and (cfg.text_state) the prompt seeds both
+        VDA scans.  With such a layout (or anchors / chunk windows) a runtime must use
+        exchange_mode "alltoall".
         """
         cfg = self.cfg
         hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
@@ -236,7 +238,12 @@ class HybridBlock(nn.Module):
         general = text_rows > 0 or not cfg.plain_window
         if general:
             if runtime is not None and runtime.world_size > 1:
-                raise ValueError("text rows, anchor frames and chunk windows run on one GPU")
+                if runtime.exchange_mode != "alltoall" or runtime.branch_parallel:
+                    raise ValueError("text rows, anchor frames and chunk windows shard through the "
+                                     "standard all-to-all exchange (exchange_mode='alltoall')")
+                if runtime.sequence_length != text_rows + T or rows != runtime.local_end - runtime.local_start:
+                    raise ValueError("configure the runtime for text_rows + frames * tokens rows")
+                return self._forward_general(x, temb, frames, tokens, text_rows, runtime)
             if rows != text_rows + T:
                 raise ValueError("x must hold text_rows + frames * tokens rows")
             return self._forward_general(x, temb, frames, tokens, text_rows)
@@ -293,8 +300,8 @@ class HybridBlock(nn.Module):
         self._gemm(q3, s3, self.down, rows, x2, bias=self.down.bias, resid=x1, gate=gate_mlp.contiguous())
         return x2
 
-    def _forward_general(self, x, temb, frames, tokens, L):
-        """One-GPU block with text rows, anchor frames and / or chunk-aligned windows
+    def _forward_general(self, x, temb, frames, tokens, L, runtime=None):
+        """Block with text rows, anchor frames and / or chunk-aligned windows
         (hybrid_attention.py:178-255 with branch.py:256-402).
 
         The softmax covers every row (text rows dense, video rows their window plus
@@ -302,8 +309,10 @@ class HybridBlock(nn.Module):
         frames 1..F-2 under anchor_frames == "both") and is skipped when every window
         spans the clip.  The output projection runs as two GEMMs: the text rows take
         to_out alone, the video rows to_out + to_out_linear in one dual-K accumulator.
+        With a runtime (world_size > 1, the all-to-all exchange) x holds this rank's
+        rows of the packed sequence [text | video] and attention runs on H / P heads
+        of all rows between the two exchanges (ulysses.py:271-419).
         """
-        from .linear_attention import vda_forward, vda_text_seed
         cfg = self.cfg
         hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
         T = frames * tokens
@@ -316,51 +325,112 @@ class HybridBlock(nn.Module):
         qkv = torch.empty(n, 3 * hd, device=dev, dtype=torch.bfloat16)
         self._gemm(q1, s1, self.qkv, n, qkv, bias=self.qkv.bias)
         g3 = self._gate_projections(y1)
-        q = qkv[:, :hd].view(n, H, d)
-        k = qkv[:, hd:2 * hd].view(n, H, d)
-        v = qkv[:, 2 * hd:].view(n, H, d)
-        sgate, beta = g3[:, :H], g3[:, H:2 * H]
+        og = self.output_gate
+        if runtime is None:
+            q = qkv[:, :hd].view(n, H, d)
+            k = qkv[:, hd:2 * hd].view(n, H, d)
+            v = qkv[:, 2 * hd:].view(n, H, d)
+            lgate = torch.sigmoid(F.linear(g3[L:, 2 * H:], og.up.weight, og.up.bias)).view(T, H, d)
+            frame_mean = y1[L:].view(frames, tokens, hd).mean(1, dtype=torch.float32)
+            att = torch.empty(n, H, d, device=dev, dtype=torch.bfloat16)
+            lin_q = self._layout_branches(q, k, v, g3[:, :H], g3[:, H:2 * H], lgate, frame_mean, frames,
+                                          tokens, L, slice(0, H), att, quantize_lin=True)
+            att = att.view(n, hd)
+            local_text = L
+
+            def quant_att(a, b):
+                return quantize_activation(att[a:b], check_finite=False)
+        else:
+            rt = runtime
+            hl = H // rt.world_size
+            N = L + T
+            sums, work = rt.video_frame_mean_async(y1, frames, tokens, video_start=L)
+            lgate = torch.sigmoid(F.linear(g3[:, 2 * H:], og.up.weight, og.up.bias))
+            # Per head: q | k | v | linear gate | softmax gate | beta | pad (W = 4d + 8).
+            W = 4 * d + 8
+            pack = torch.empty(n, H, W, device=dev, dtype=torch.bfloat16)
+            pack[:, :, 0:3 * d] = qkv.view(n, 3, H, d).permute(0, 2, 1, 3).reshape(n, H, 3 * d)
+            pack[:, :, 3 * d:4 * d] = lgate.view(n, H, d)
+            pack[:, :, 4 * d] = g3[:, :H]
+            pack[:, :, 4 * d + 1] = g3[:, H:2 * H]
+            recv = rt.sequence_to_heads(pack)                             # [N, H/P, W]
+            work.wait()
+            frame_mean = sums / tokens
+            h0 = rt.rank * hl
+            ret = torch.empty(N, hl, 2 * d, device=dev, dtype=torch.bfloat16)
+            lin = self._layout_branches(recv[:, :, 0:d], recv[:, :, d:2 * d], recv[:, :, 2 * d:3 * d],
+                                        recv[:, :, 4 * d], recv[:, :, 4 * d + 1], recv[L:, :, 3 * d:4 * d],
+                                        frame_mean, frames, tokens, L, slice(h0, h0 + hl), ret[:, :, :d],
+                                        quantize_lin=False)
+            ret[:L, :, d:].zero_()
+            if lin is None:
+                ret[L:, :, d:].zero_()
+            else:
+                ret[L:, :, d:] = lin.view(T, hl, d)
+            flat = rt.heads_to_sequence(ret).view(n, H * 2 * d)           # [rows, H * 2d]
+            local_text = max(0, min(L - rt.local_start, n))
+            lin_q = None
+            if lin is not None and n > local_text:
+                lin_q = self._quantize_grouped(flat[local_text:], d, n - local_text)
+
+            def quant_att(a, b):
+                return self._quantize_grouped(flat[a:b], 0, b - a)
+        x1 = self._project_out(x, quant_att, lin_q, local_text, gate_msa.contiguous())
+        return self._ffn(x1, shift_mlp, scale_mlp, gate_mlp, idx)
+
+    def _layout_branches(self, q, k, v, sgate, beta, lgate, frame_mean, frames, tokens, L, heads, att_out,
+                         *, quantize_lin):
+        """Window softmax over all [L + F*S, h, d] rows into att_out; the VDA branch over the
+        video rows (lgate [F*S, h, d]) on the side stream.  Returns the VDA output (bf16
+        [F*S, h*d], or its MXFP8 when quantize_lin), or None when every window spans the clip."""
+        from .linear_attention import vda_forward, vda_text_seed
+        cfg = self.cfg
+        h, d = q.shape[1], q.shape[2]
+        T = frames * tokens
+        dev = q.device
         bounds = window_bounds(frames, cfg.radius, cfg.chunk)
         linear_active = not all(lo <= 0 and hi >= frames - 1 for lo, hi in bounds)
 
         def branch():  # VDA over the video rows, on the side stream
-            og = self.output_gate
-            lgate = torch.sigmoid(F.linear(g3[L:, 2 * H:], og.up.weight, og.up.bias)).view(T, H, d)
-            frame_mean = y1[L:].view(frames, tokens, hd).mean(1, dtype=torch.float32)
-            alpha = self.alpha.forward_native(frame_mean)
+            alpha = self.alpha.forward_native(frame_mean, heads=heads)
             seed = vda_text_seed(k[:L], v[:L], beta[:L], 0.5) if cfg.text_state and L else None
             qv, kv, vv, bv = q[L:], k[L:], v[L:], beta[L:]
             if cfg.anchor_frames != "both":
                 lin = vda_forward(qv, kv, vv, bv, lgate, alpha, bounds, frames, tokens, self.vda_norm,
                                   seed=seed)
             else:  # frames 0 and F-1 are exact softmax: dropped from the branch, rows zero
-                lin = torch.zeros(T, hd, device=dev, dtype=torch.bfloat16)
+                lin = torch.zeros(T, h * d, device=dev, dtype=torch.bfloat16)
                 if frames > 2:
                     inner = slice(tokens, (frames - 1) * tokens)
                     lin[inner] = vda_forward(qv[inner], kv[inner], vv[inner], bv[inner], lgate[inner],
                                              alpha[1:-1].contiguous(),
                                              [(lo - 1, hi - 1) for lo, hi in bounds[1:frames - 1]],
                                              frames - 2, tokens, self.vda_norm, seed=seed)
-            return quantize_activation(lin, check_finite=False)
+            return quantize_activation(lin, check_finite=False) if quantize_lin else lin
 
         join = self._vda_side(branch, dev) if linear_active else None
-        att = torch.empty(n, H, d, device=dev, dtype=torch.bfloat16)
-        window_softmax(q, k, v, sgate, frames, tokens, cfg.radius, out=att, bounds=bounds, text_rows=L,
-                       anchor_frames=cfg.anchor_frames)
-        att = att.view(n, hd)
-        lin = join() if join is not None else None
+        window_softmax(q, k, v, sgate, frames, tokens, cfg.radius, out=att_out,
+                       bounds=bounds, text_rows=L, anchor_frames=cfg.anchor_frames)
+        return join() if join is not None else None
+
+    def _project_out(self, x, quant_att, lin_q, text_rows, gate_msa):
+        """x1 = x + gate_msa * (to_out(softmax) [+ to_out_linear(VDA) on the video rows]):
+        rows [0, text_rows) take to_out alone (hybrid_attention.py:250-255)."""
+        n = x.shape[0]
         x1 = torch.empty_like(x)
-        gm = gate_msa.contiguous()
-        if L:
-            aq, as_ = quantize_activation(att[:L], check_finite=False)
-            self._gemm(aq, as_, self.o, L, x1[:L], bias=self.o.bias, resid=x[:L], gate=gm)
-        aq, as_ = quantize_activation(att[L:], check_finite=False)
-        if lin is None:
-            self._gemm(aq, as_, self.o, T, x1[L:], bias=self.o.bias, resid=x[L:], gate=gm)
-        else:
-            self._gemm(aq, as_, self.o, T, x1[L:], second=(lin, self.ol), bias=self.o_bias, resid=x[L:],
-                       gate=gm)
-        return self._ffn(x1, shift_mlp, scale_mlp, gate_mlp, idx)
+        if text_rows:
+            aq, as_ = quant_att(0, text_rows)
+            self._gemm(aq, as_, self.o, text_rows, x1[:text_rows], bias=self.o.bias, resid=x[:text_rows],
+                       gate=gate_msa)
+        if n > text_rows:
+            aq, as_ = quant_att(text_rows, n)
+            if lin_q is None:
+                self._gemm(aq, as_, self.o, n - text_rows, x1[text_rows:], bias=self.o.bias,
+                           resid=x[text_rows:], gate=gate_msa)
+            else:
+                self._gemm(aq, as_, self.o, n - text_rows, x1[text_rows:], second=(lin_q, self.ol),
+                           bias=self.o_bias, resid=x[text_rows:], gate=gate_msa)
+        return x1
 
     def _attention(self, qkv, sgate, beta, lgate, frame_mean, frames, tokens, heads):
         """Single-GPU attention: returns ((codes, scales) softmax, (codes, scales) VDA)."""
