@@ -17,11 +17,15 @@ The pieces follow the reference: the pre-norm producer and gated residual of
 src/models/ops/fused_block.py:43-51 / mxfp8_kernels.py:86-139, the hybrid
 attention merge of src/models/hybrid_attention.py:178-255 (to_out + to_out_linear
 on the video rows), the standard Ulysses forward of
-src/inference/utils/ulysses.py:271-419 and the branch of
-src/models/linear_attention/branch.py.  The BASELINE block has no RoPE / QK-norm
-and no text rows; the FFN is GELU (tanh form) rather than H3's SwiGLU.  Weights
-are random (seeded), with a rank-32 LoRA merged into Q, K, V and O on the host
-before MXFP8 quantisation, as the reference merges before conversion.
+src/inference/utils/ulysses.py:271-419, its branch-parallel forward (:421-598)
+and the branch of src/models/linear_attention/branch.py.  The BASELINE block has
+no RoPE / QK-norm and no text rows; the FFN is GELU (tanh form) rather than H3's
+SwiGLU.  Weights are random (seeded), with a rank-32 LoRA merged into Q, K, V and
+O before MXFP8 quantisation, as the reference merges before conversion.
+
+Layouts beyond the BASELINE window (text rows packed first, anchor frames,
+chunk-aligned windows, the text-seeded scans) take `_forward_general`: one GPU,
+or Ulysses through the all-to-all exchange.
 """
 from __future__ import annotations
 
