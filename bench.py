@@ -27,10 +27,11 @@ Workloads:
         (15360, 5120), (5120, 5120), (13824, 5120), (5120, 13824); each step
         quantises the bf16 activation and runs the four GEMMs; metric = TFLOP/s.
         --rows M shrinks M (small profiling case).  N > 1: replicas.
-  stack BASELINE config 4 on one GPU: one denoise step = a 40-block stack of the
-        config-3 block over 512 text rows (packed first, dense softmax) + 60 x 1560
-        video rows, then the Euler update; --steps 8 is the 8-step loop; metric =
-        video tokens/s.  --depth / --frames shrink it (small case).
+  stack BASELINE config 4: one denoise step = a 40-block stack of the config-3
+        block over 512 text rows (packed first, dense softmax) + 60 x 1560 video
+        rows, then the Euler update; --steps 8 is the 8-step loop; metric = video
+        tokens/s.  N > 1: Ulysses over the packed rows (all-to-all exchange).
+        --depth / --frames shrink it (small case).
 """
 from __future__ import annotations
 
@@ -623,13 +624,13 @@ def count_launches(fn):
 
 
 def bench_stack(args, torch, dist, rank, world):
-    """BASELINE config 4 on one GPU: the 8-step denoise loop of a 40-block stack over
-    512 text rows + 60 x 1560 video rows (text packed first as global rows)."""
+    """the 8-step denoise loop of a 40-block stack over 512 text rows +
+    60 x 1560 video rows (text packed first as global rows); N > 1 shards the packed rows
+    with Ulysses (all-to-all exchange)."""
     from vdn_b200.block import BlockConfig
     from vdn_b200.mxfp8_quant import quantize_activation
-    from vdn_b200.stack import HybridStack, denoise
-    if world > 1:
-        raise SystemExit("the stack workload runs on one GPU: the Ulysses paths do not shard text rows")
+    from vdn_b200.stack import HybridStack, denoise, local_rows
+    from vdn_b200.ulysses import init_ulysses
     F = args.frames or STACK_CFG["F"]
     S, L = STACK_CFG["S"], STACK_CFG["text_rows"]
     depth = args.depth or STACK_CFG["depth"]
@@ -638,18 +639,25 @@ def bench_stack(args, torch, dist, rank, world):
     T = F * S
     dev = torch.device("cuda", torch.cuda.current_device())
     stream = torch.cuda.current_stream(dev)
+    runtime = None
+    if world > 1:  # Ulysses over the packed [text | video] rows, all-to-all exchange
+        runtime = init_ulysses("nccl")
+        runtime.exchange_mode = "alltoall"
+        runtime.configure(L + T, cfg.heads)
+    (ta, tb), (va, vb) = local_rows(L, runtime, L + T)
     stack = HybridStack(cfg, depth, seed=0, device=dev, init="device")
     g = torch.Generator(device=dev).manual_seed(4321)
-    video = torch.randn(T, hd, device=dev, generator=g).bfloat16()
+    video = torch.randn(T, hd, device=dev, generator=g).bfloat16()[va:vb].contiguous()
     text = torch.randn(L, hd, device=dev, generator=g).bfloat16()
     nsteps = STACK_CFG["denoise_steps"]
     tembs = torch.randn(nsteps, hd, device=dev, generator=g)
-    packed = torch.empty(L + T, hd, device=dev, dtype=torch.bfloat16)
+    rows = (tb - ta) + (vb - va)
+    packed = torch.empty(rows, hd, device=dev, dtype=torch.bfloat16)
     i = [0]
 
     def step():  # one denoise step: the whole stack over [text | video], then the Euler update
         j = i[0] % nsteps
-        denoise(stack, video, text, tembs[j:j + 1], F, S, packed=packed, dt=-1.0 / nsteps)
+        denoise(stack, video, text, tembs[j:j + 1], F, S, packed=packed, dt=-1.0 / nsteps, runtime=runtime)
         i[0] += 1
 
     launches = count_launches(step)
@@ -675,7 +683,7 @@ def bench_stack(args, torch, dist, rank, world):
     e2e_ms = time_steps(torch, e2e_step, e2e_steps, 1, dist, stream) / e2e_steps
 
     blk = stack.blocks[0]
-    n = L + T
+    n = rows
     y1 = torch.randn(n, hd, device=dev).bfloat16()
     q1, s1 = quantize_activation(y1)
     out = torch.empty(n, 3 * hd, device=dev, dtype=torch.bfloat16)
@@ -685,7 +693,7 @@ def bench_stack(args, torch, dist, rank, world):
     achieved = gemm_flops / (kt["mxfp8_gemm_qkv"] * 1e-3) / 1e12
     pk, src = peaks()
     fp8_peak = 2 * pk["bf16_tflops"]
-    return {
+    rec = {
         "metric": "denoise-loop tokens/s (BASELINE config 4: 40-block stack, 60 x 1560 video + 512 text rows)",
         "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(per_step_ms, 3), "higher_is_better": True,
@@ -695,7 +703,8 @@ def bench_stack(args, torch, dist, rank, world):
         "config": {"workload": "denoise_stack_config4", "frames": F, "tokens_per_frame": S, "text_rows": L,
                    "depth": depth, "denoise_steps": nsteps, "step": "one denoise step (whole stack + Euler update)",
                    "hidden": hd, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": cfg.ffn,
-                   "window": "+-1 frame, text rows dense", "parallelism": "single GPU",
+                   "window": "+-1 frame, text rows dense",
+                   "parallelism": f"ulysses sp{world} (all-to-all exchange)" if world > 1 else "single GPU",
                    "l2": "per-step working set (weights 23 GB, activations > 1 GB) larger than L2",
                    "latent_finite_after_timing": finite},
         "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
@@ -711,6 +720,9 @@ def bench_stack(args, torch, dist, rank, world):
         "kernels_ms": {k_: round(v_, 4) for k_, v_ in kt.items()},
         "clocks": clk.summary(),
     }
+    if runtime is not None:
+        runtime.close()
+    return rec
 
 
 def cpu_baseline_stack(threads):

@@ -16,7 +16,7 @@ from torch import nn
 
 from .block import BlockConfig, HybridBlock
 
-__all__ = ["HybridStack", "denoise"]
+__all__ = ["HybridStack", "denoise", "local_rows"]
 
 
 class HybridStack(nn.Module):
@@ -35,22 +35,42 @@ class HybridStack(nn.Module):
         return x
 
 
+def local_rows(text_rows, runtime=None, total=None):
+    """(text, video) row ranges of this rank's shard of the packed sequence [text | video]:
+    text rows [a, b) of the context and video rows [c, e) of the clip."""
+    if runtime is None or runtime.world_size == 1:
+        return (0, text_rows), (0, total - text_rows)
+    lo, hi = runtime.local_start, runtime.local_end
+    t = (min(lo, text_rows), min(hi, text_rows))
+    v = (max(lo, text_rows) - text_rows, max(hi, text_rows) - text_rows)
+    return t, v
+
+
 @torch.no_grad()
-def denoise(stack: HybridStack, video, text, tembs, frames, tokens, *, packed=None, dt=None):
+def denoise(stack: HybridStack, video, text, tembs, frames, tokens, *, packed=None, dt=None,
+            runtime=None):
     """Euler loop: for each step i, packed = [text_i | video]; video += dt * stack(packed)[video rows]
-    with dt = -1 / steps unless given.  video [F*S, hidden] bf16 (updated in place and
-    returned); text [steps, L, hidden] or [L, hidden] (the same context every step) or
-    None; tembs [steps, hidden]."""
+    with dt = -1 / steps unless given.  text [steps, L, hidden] or [L, hidden] (the same
+    context every step) or None; tembs [steps, hidden].  video is updated in place and
+    returned: all F*S rows, or with a Ulysses runtime (configured for L + F*S rows) this
+    rank's video rows of the sharded packed sequence."""
     steps = tembs.shape[0]
     L = 0 if text is None else text.shape[-2]
-    n = L + video.shape[0]
+    if runtime is not None and runtime.world_size > 1:
+        (ta, tb), (va, vb) = local_rows(L, runtime)
+        if runtime.sequence_length != L + frames * tokens or video.shape[0] != vb - va:
+            raise ValueError("video must hold this rank's video rows of the configured sequence")
+    else:
+        (ta, tb), (va, vb) = local_rows(L, None, L + video.shape[0])
+    nt = tb - ta
+    n = nt + video.shape[0]
     if packed is None:
         packed = torch.empty(n, video.shape[1], device=video.device, dtype=video.dtype)
     dt = -1.0 / steps if dt is None else dt
     for i in range(steps):
-        if L:
-            packed[:L].copy_(text[i] if text.dim() == 3 else text)
-        packed[L:].copy_(video)
-        out = stack(packed, tembs[i], frames, tokens, text_rows=L)
-        video.add_(out[L:], alpha=dt)
+        if nt:
+            packed[:nt].copy_((text[i] if text.dim() == 3 else text)[ta:tb])
+        packed[nt:].copy_(video)
+        out = stack(packed, tembs[i], frames, tokens, runtime, text_rows=L)
+        video.add_(out[nt:], alpha=dt)
     return video
