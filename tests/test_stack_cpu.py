@@ -62,3 +62,14 @@ def test_denoise_sharded_matches_whole():
     bad = SimpleNamespace(world_size=3, local_start=0, local_end=6, sequence_length=L + T + 1)
     with pytest.raises(ValueError):
         denoise(_Echo(), video[:0].clone(), text, tembs, F, S, runtime=bad)
+
+
+def test_block_config_layout_arguments():
+    from vdn_b200.block import BlockConfig
+    assert BlockConfig().plain_window
+    assert not BlockConfig(anchor_frames="both").plain_window
+    assert not BlockConfig(chunk=5).plain_window
+    assert BlockConfig(text_state=1).text_state is True
+    for bad in (dict(anchor_frames="corners"), dict(chunk=-1), dict(radius=-1)):
+        with pytest.raises(ValueError):
+            BlockConfig(**bad)
