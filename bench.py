@@ -16,9 +16,15 @@ Workloads:
   block (default)  BASELINE config 3: one hybrid DiT block (hidden 5120, 40 x 128
         heads, GELU FFN 13824, MXFP8 projections, VDA + window softmax +-1 frame)
         over 21 frames x 1560 tokens = 32760 tokens; metric = tokens/s of the
-        whole job.  N > 1: Ulysses sequence parallelism over NCCL (sequence
-        shards, all-to-all to heads around attention): strong scaling, the same
-        32760-token block split over N GPUs.
+        whole job.  N > 1: Ulysses sequence parallelism (sequence shards, heads
+        around attention) with the exchange done by the producers over NVLink
+        peer memory (the QKV GEMM's scatter epilogue and the scatter quantiser,
+        device fences; NCCL carries only setup and the timing reductions):
+        strong scaling, the same 32760-token block split over N GPUs.  Each rank
+        then recomputes the unsharded block outside the timed region and the line
+        carries `parity` (max over ranks of the relative L2 of its rows).  N = 1:
+        the line also carries `vda` (config 2), `gemm_sweep` (config 1) and
+        `quantiser` sub-records, each timed on its own after the block.
   vda   BASELINE config 2: the VDA branch, H=40, d=128, 21 frames x 1560 tokens,
         metric = algorithmic HBM GB/s (q, k, v, gate, beta, alpha in; out).
         N > 1: independent replicas (heads are independent; no collective).
@@ -113,8 +119,9 @@ class ClockSampler:
 
 
 # DRAM bytes (read + write) per launch of the dominant kernels at the full
-# BASELINE shapes, from one single-pass ncu capture of the block bench (see the
-# block launch-list summary under profiles/); reported as roofline "traffic".
+# BASELINE shapes, from a separate ncu capture (not measured in this run; the
+# capture is summarised under profiles/); reported as roofline "traffic" with
+# "traffic_source" saying so.
 NCU_TRAFFIC_BYTES = {
     "mxfp8_gemm_qkv": 1471.4e6 + 981.8e6,
     "statistics": 674.4e6 + 89.9e6,
@@ -123,6 +130,8 @@ NCU_TRAFFIC_BYTES = {
     "gather": 100.1e6 + 8.3e6,
     "readout": 698.8e6 + 297.0e6,
 }
+
+TRAFFIC_SOURCE = "from a separate ncu capture of this kernel (profiles/), not measured in this run"
 
 
 # ------------------------------------------------------------------ timing
@@ -162,6 +171,19 @@ def kernel_times(torch, launches, reps, stream):
         torch.cuda.synchronize()
         out[name] = a.elapsed_time(b) / reps
     return out
+
+
+def cublas_fp8_ms(torch, m, n, k, dev, stream, reps=10):
+    """Device ms of the same-box cuBLAS per-tensor E4M3 GEMM [m, k] x [n, k]^T -> bf16:
+    the reference's B200 FP8 path, Fp8Linear.forward_quantized (src/models/ops/
+    fp8_linear.py:269-273: torch._scaled_mm, scalar scales, use_fast_accum=True)."""
+    g = torch.Generator(device=dev).manual_seed(99)
+    a = torch.randn(m, k, device=dev, generator=g).to(torch.float8_e4m3fn)
+    b = torch.randn(n, k, device=dev, generator=g).to(torch.float8_e4m3fn)
+    one = torch.ones((), device=dev)
+    fn = lambda: torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16,
+                                  use_fast_accum=True)
+    return kernel_times(torch, [("cublas", fn)], reps, stream)["cublas"]
 
 
 # ------------------------------------------------------------------ VDA
@@ -281,7 +303,8 @@ def bench_vda(args, torch, dist, rank, world):
         "roofline": {"bound": "hbm", "kernel": top, "achieved": round(achieved, 1),
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                      "traffic": NCU_TRAFFIC_BYTES.get(top) if F == VDA_CFG["F"] else None,
-                     "traffic_unit": "bytes per launch (ncu dram read + write)", "peak_source": src,
+                     "traffic_unit": "bytes per launch (ncu dram read + write)",
+                     "traffic_source": TRAFFIC_SOURCE, "peak_source": src,
                      "algorithmic_bytes_per_launch": algo[top]},
         "kernels_ms": {k_: round(v_, 4) for k_, v_ in kt.items()},
         "clocks": clk.summary(),
@@ -364,9 +387,15 @@ def bench_gemm(args, torch, dist, rank, world):
     per_shape = {}
     for c in cases:
         tf = c["flops"] / (kt[c["name"]] * 1e-3) / 1e12
+        try:
+            cub = c["flops"] / (cublas_fp8_ms(torch, M, c["n"], c["k"], dev, stream) * 1e-3) / 1e12
+        except Exception:  # comparator only
+            cub = None
         qbytes = M * c["k"] * 2 + (M + 127) // 128 * 128 * c["k"] * 33 // 32
         per_shape[c["name"]] = {"m": M, "n": c["n"], "k": c["k"], "gemm_ms": round(kt[c["name"]], 4),
                                 "tflops": round(tf, 1), "frac_fp8_peak": round(tf / fp8_peak, 4),
+                                "cublas_fp8_per_tensor_tflops": None if cub is None else round(cub, 1),
+                                "frac_of_cublas": None if cub is None else round(tf / cub, 4),
                                 "quantize_ms": round(kt[c["name"] + "_quantize"], 4),
                                 "quantize_gbs": round(qbytes / (kt[c["name"] + "_quantize"] * 1e-3) / 1e9, 1)}
     top = cases[0]
@@ -404,6 +433,7 @@ def bench_gemm(args, torch, dist, rank, world):
                      "frac": round(achieved / fp8_peak, 4),
                      "traffic": NCU_TRAFFIC_BYTES["mxfp8_gemm_qkv"] if M == GEMM_ROWS else None,
                      "traffic_unit": "bytes per launch (ncu dram read + write)",
+                     "traffic_source": TRAFFIC_SOURCE,
                      "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']}): the FP8 rate",
                      "algorithmic_flops_per_launch": top["flops"]},
         "shapes": per_shape,
@@ -457,7 +487,8 @@ def bench_block(args, torch, dist, rank, world):
     x_full = torch.randn(T, BLOCK_CFG["hidden"], device=dev, generator=g).bfloat16()
     temb = torch.randn(BLOCK_CFG["hidden"], device=dev, generator=g)
     x = x_full[lo:hi].contiguous()
-    del x_full
+    if world == 1:
+        del x_full  # N > 1 keeps it for the parity check against the unsharded block
     rows = hi - lo
 
     if args.eager:
@@ -489,12 +520,11 @@ def bench_block(args, torch, dist, rank, world):
     fp8_peak = 2 * pk["bf16_tflops"]
     comp = {}
     try:
-        x8 = y1.to(torch.float8_e4m3fn)
-        w8 = torch.randn(3 * BLOCK_CFG["hidden"], BLOCK_CFG["hidden"], device=dev).to(torch.float8_e4m3fn)
-        one = torch.ones((), device=dev)
-        ct = kernel_times(torch, [("cublas_fp8_per_tensor", lambda: torch._scaled_mm(
-            x8, w8.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16))], 10, stream)
-        comp["cublas_fp8_per_tensor_tflops"] = round(gemm_flops / (ct["cublas_fp8_per_tensor"] * 1e-3) / 1e12, 1)
+        cub = gemm_flops / (cublas_fp8_ms(torch, rows, 3 * BLOCK_CFG["hidden"], BLOCK_CFG["hidden"], dev,
+                                          stream) * 1e-3) / 1e12
+        comp["cublas_fp8_per_tensor_tflops"] = round(cub, 1)
+        comp["cublas_call"] = "torch._scaled_mm, scalar scales, use_fast_accum=True (Fp8Linear)"
+        comp["frac_of_cublas"] = round(achieved / cub, 4)
     except Exception as e:  # comparator only
         comp["cublas_fp8_per_tensor_error"] = repr(e)[:120]
 
@@ -549,12 +579,18 @@ def bench_block(args, torch, dist, rank, world):
                      "frac": round(achieved / fp8_peak, 4),
                      "traffic": NCU_TRAFFIC_BYTES["mxfp8_gemm_qkv"] if world == 1 else None,
                      "traffic_unit": "bytes per launch (ncu dram read + write)",
+                     "traffic_source": TRAFFIC_SOURCE,
                      "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']}): the FP8 rate",
                      "algorithmic_flops_per_launch": gemm_flops},
         "comparators": comp,
         "kernels_ms": {k_: round(v_, 4) for k_, v_ in kt.items()},
         "clocks": clk.summary(),
     }
+    if world > 1:
+        rec["parity"] = block_parity(torch, dist, block, step, x_full, temb, F, S, lo, hi)
+        del x_full
+    elif not args.no_sub:
+        rec.update(sub_records(args, torch))
     if runtime is not None:
         rec["config"]["exchange"] = runtime.exchange_mode
         if runtime.branch_parallel:
@@ -563,6 +599,52 @@ def bench_block(args, torch, dist, rank, world):
                                             f"{world - runtime.softmax_ranks} VDA ranks")
         runtime.close()
     return rec
+
+
+def block_parity(torch, dist, block, step, x_full, temb, F, S, lo, hi, tol=2e-3):
+    """This rank's rows of the sharded forward against the unsharded block computed on
+    the same rank (same weights, same inputs), outside the timed region; the relative
+    L2 and max-abs differences are reduced by MAX over ranks.  The bar (2e-3) is the
+    multi-GPU block test's: alpha sees the frame sums added in another order."""
+    y = step().clone()                       # every rank replays its shard (peer fences)
+    torch.cuda.synchronize()
+    ref = block(x_full, temb, F, S, None)[lo:hi]
+    torch.cuda.synchronize()
+    rel = float((y.double() - ref.double()).norm() / ref.double().norm())
+    mx = float((y.float() - ref.float()).abs().max())
+    t = torch.tensor([rel, mx], device=y.device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    rel, mx = float(t[0]), float(t[1])
+    return {"rel_l2_max": rel, "max_abs": mx, "tol_rel_l2": tol, "ok": bool(rel < tol),
+            "reference": "unsharded block on each rank (same seeded weights and input)"}
+
+
+def sub_records(args, torch):
+    """BASELINE configs 2 and 1 timed on their own after the block (N = 1): the VDA
+    branch (8 calls), the four-GEMM sweep and the activation quantiser.  Each keeps
+    its metric, roofline, kernel times, e2e and clocks."""
+    sub = argparse.Namespace(**vars(args))
+    sub.steps, sub.warmup, sub.frames, sub.rows = 8, 3, 0, 0
+    keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "e2e", "roofline",
+            "kernels_ms", "clocks", "config", "gpu_launches")
+    torch.cuda.empty_cache()
+    v = bench_vda(sub, torch, None, 0, 1)
+    torch.cuda.empty_cache()
+    g = bench_gemm(sub, torch, None, 0, 1)
+    torch.cuda.empty_cache()
+    pk, src = peaks()
+    qkv = g["shapes"]["qkv"]
+    qbytes = GEMM_ROWS * 5120 * 2 + (GEMM_ROWS + 127) // 128 * 128 * 5120 * 33 // 32
+    quant = {"metric": "MXFP8 activation quantiser GB/s (32760 x 5120 bf16 -> E4M3 codes + E8M0 scales)",
+             "value": qkv["quantize_gbs"], "unit": "GB/s", "ms": qkv["quantize_ms"],
+             "algorithmic_bytes": qbytes,
+             "roofline": {"bound": "hbm", "achieved": qkv["quantize_gbs"], "peak": pk["hbm_gbs"],
+                          "unit": "GB/s", "frac": round(qkv["quantize_gbs"] / pk["hbm_gbs"], 4),
+                          "peak_source": src},
+             "clocks": g["clocks"]}
+    return {"vda": {k: v[k] for k in keep if k in v},
+            "gemm_sweep": {**{k: g[k] for k in keep if k in g}, "shapes": g["shapes"]},
+            "quantiser": quant}
 
 
 def cpu_baseline_block(threads):
@@ -750,6 +832,8 @@ def main():
     ap.add_argument("--depth", type=int, default=0, help="stack: block-count override (small case)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="block, N = 1: skip the config-2 / config-1 sub-records")
     ap.add_argument("--eager", action="store_true", help="block: launch eagerly instead of a CUDA graph")
     ap.add_argument("--softmax-ranks", type=int, default=0,
                     help="block, N > 1: branch-parallel layout with this many softmax ranks (needs --eager)")

@@ -323,13 +323,17 @@ int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss,
  * this library device memory or let it call cudaMalloc (a host engine that owns
  * all device memory through its own pool, or a latency-critical loop that cannot
  * take cudaMalloc's device synchronisation).  Same kernels and results as
- * vdn_vda_forward; the scratch is a 64 MiB array built into the library, held
- * by every GPU that loads it until the process exits.  Geometries needing more
- * than 64 MiB (18 * F * H * d^2 bytes plus alignment) return VDN_ERR_VALUE.
- * The first call on a device looks the array's address up (make it before any
- * stream capture); all calls share the array, so calls that overlap on the GPU
- * race.  It allocates nothing.  This entry point has no counterpart in the
- * reference (ec-jt/vdn): its branch body always allocates through PyTorch. */
+ * vdn_vda_forward; the scratch is a 64 MiB array built into the library.
+ * Geometries whose vdn_vda_workspace_size exceeds 64 MiB return VDN_ERR_VALUE
+ * (at d = 128: 22 frames x 10 heads fit, 23 x 10 do not).  The first call on a
+ * device looks the array's address up; under CUDA's lazy module loading that is
+ * also when the device reserves the 64 MiB (kept until the process exits) and
+ * it may synchronise the device, so make one warm-up call outside latency-
+ * critical code and before any stream capture.  The address is looked up again
+ * if the device's context was recreated.  All calls share the array, so calls
+ * that overlap on the GPU race.  It allocates nothing.  This entry point has no
+ * counterpart in the reference (ec-jt/vdn): its branch body always allocates
+ * through PyTorch. */
 int vdn_vda_forward_noalloc(const void* q, const void* k, const void* v, int64_t qkv_ss,
                             int64_t qkv_sh, const void* beta, int64_t b_ss, int64_t b_sh,
                             const void* gate, int64_t g_ss, int64_t g_sh,

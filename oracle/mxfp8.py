@@ -68,7 +68,11 @@ def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
 
 
 def round_bf16(x: np.ndarray) -> np.ndarray:
-    return bf16_to_f32(f32_to_bf16_bits(np.asarray(x, dtype=np.float32)))
+    """float32 values rounded to bf16 (round to nearest even), as float32.  Uses torch's
+    conversion (multithreaded), which equals f32_to_bf16_bits on every finite input."""
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    return t.to(torch.bfloat16).float().numpy()
 
 
 def _rne_shift(value: np.ndarray, shift: np.ndarray) -> np.ndarray:
@@ -153,6 +157,32 @@ def dequantize(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
     natural = unswizzle(scales, rp, kp).astype(np.float64)
     vals = e4m3_bits_to_f32(codes).astype(np.float64).reshape(rp, kp // 32, 32)
     return (vals * np.exp2(natural - 127)[..., None]).reshape(rp, kp)
+
+
+def qdq_torch(x):
+    """MXFP8 quantise-then-dequantise of a [rows, K] CPU tensor: the fp32 values the GEMM
+    multiplies (cropped to [rows, K]).  The same rule as quantize() (quantize_cpu,
+    src/models/ops/mxfp8_quant.py:40-74) in multithreaded torch CPU ops, with torch's
+    float8_e4m3fn conversion (round to nearest even) in place of the bit-pattern
+    restatement; pinned bit-exact against dequantize(quantize(x)) by the CPU tests.
+    For the full-size checks, where the numpy path takes minutes."""
+    import torch
+    r, k = x.shape
+    kp = (k + 127) // 128 * 128
+    v = torch.zeros(r, kp, dtype=torch.float32)
+    v[:, :k] = x.float()
+    if not bool(torch.isfinite(v).all()):
+        raise ValueError("nonfinite MXFP8 input")
+    blocks = v.view(r, kp // 32, 32)
+    amax = blocks.abs().amax(-1)
+    bits = amax.view(torch.int32)
+    e0 = ((bits >> 23) & 255) - 135
+    thr = (((e0 + 135) << 23) | 0x600000).view(torch.float32)
+    e = (e0 + (amax > thr).to(torch.int32)).clamp_min(-127)
+    inv = ((127 - e) << 23).view(torch.float32)
+    codes = (blocks * inv[..., None]).to(torch.float8_e4m3fn)
+    out = codes.to(torch.float64) * torch.pow(2.0, e.to(torch.float64))[..., None]
+    return out.view(r, kp)[:, :k].to(torch.float32)
 
 
 def mxfp8_gemm(xq, xs, wq, ws, rows, n, bias=None) -> np.ndarray:

@@ -42,13 +42,18 @@ def silu(x, acc=np.float32):
 
 
 def features(raw, l2norm: bool):
-    """[N, H, d] bf16 values (as fp32) -> bf16 features (eager rounding points)."""
-    x = round_bf16(silu(raw, np.float32))
-    if not l2norm:
-        return x
-    norm = np.sqrt((x.astype(np.float64) ** 2).sum(-1, keepdims=True))
-    norm = round_bf16(np.maximum(round_bf16(norm.astype(np.float32)), np.float32(1e-6)))
-    return round_bf16(x / norm)
+    """[N, H, d] bf16 values (as fp32) -> bf16 features (as fp32).
+
+    The eager body's SiLU then L2 normalisation over d (eps 1e-6), evaluated as the
+    reference evaluates it (_activate_body, features.py:47-60): torch CPU silu and
+    normalize on the bf16 tensor, so every rounding point (bf16 silu, bf16 norm,
+    bf16 quotient) is torch's own; multithreaded, which keeps full-size checks fast."""
+    import torch
+    import torch.nn.functional as Fn
+    x = Fn.silu(torch.from_numpy(np.ascontiguousarray(raw, np.float32)).to(torch.bfloat16))
+    if l2norm:
+        x = Fn.normalize(x, dim=-1, eps=1e-6).to(x.dtype)
+    return x.float().numpy()
 
 
 def frame_statistics(k, v, beta, acc=np.float64):
@@ -125,15 +130,20 @@ def text_seed(tk_raw, tv_raw, t_beta, scale=0.5):
 
 
 def readout(q_raw, k_raw, v_raw, beta, gate, alpha, bounds, num_frames, tokens_per_frame,
-            norm_weight=None, eps=1e-6, seed=None, bridge=True, return_parts=False):
+            norm_weight=None, eps=1e-6, seed=None, bridge=True, return_parts=False, out_frames=None):
     """The branch body over the frames it owns. Returns [F*S, H*d] (fp32 of bf16).
 
     q_raw/k_raw/v_raw [F*S, H, d] and gate [F*S, H, d] hold bf16 values, beta
     [F*S, H] bf16 values, alpha [F, H, d] fp32, seed [H, d, d] or None.
+    out_frames: read out only those frames (their rows; the other rows are zero);
+    the statistics, factors and scans still cover every frame.
     """
     f, s = num_frames, tokens_per_frame
     n, h, d = q_raw.shape
     assert n == f * s
+    if out_frames is not None:
+        return _readout_frames(q_raw, k_raw, v_raw, beta, gate, alpha, bounds, f, s, norm_weight,
+                               eps, seed, bridge, out_frames)
     q = features(q_raw, True).reshape(f, s, h, d)
     k = features(k_raw, True).reshape(f, s, h, d).transpose(0, 2, 1, 3)
     v = features(v_raw, False).reshape(f, s, h, d).transpose(0, 2, 1, 3)
@@ -151,6 +161,29 @@ def readout(q_raw, k_raw, v_raw, beta, gate, alpha, bounds, num_frames, tokens_p
     if return_parts:
         return out, dict(a=a_stat, b=b_stat, t=t, j=j, prefix=prefix, suffix=suffix,
                          state=state, readout=r)
+    return out
+
+
+def _readout_frames(q_raw, k_raw, v_raw, beta, gate, alpha, bounds, f, s, norm_weight, eps, seed,
+                    bridge, out_frames):
+    n, h, d = q_raw.shape
+    k = features(k_raw, True).reshape(f, s, h, d).transpose(0, 2, 1, 3)
+    v = features(v_raw, False).reshape(f, s, h, d).transpose(0, 2, 1, 3)
+    b = np.asarray(beta, np.float32).reshape(f, s, h).transpose(0, 2, 1)
+    a_stat, b_stat = frame_statistics(k, v, b)
+    t, j = delta_factors(a_stat, b_stat, alpha)
+    prefix, suffix = run_scans(t, j, seed)
+    state = round_bf16(gather(prefix, suffix, alpha, bounds, seed, bridge).astype(np.float32))
+    w = np.ones(d, np.float32) if norm_weight is None else norm_weight
+    out = np.zeros((n, h * d), np.float32)
+    for fr in out_frames:
+        rows = slice(fr * s, (fr + 1) * s)
+        q = features(q_raw[rows], True)                                  # [S, H, d]
+        r = np.matmul(q.astype(np.float64).transpose(1, 0, 2),
+                      np.swapaxes(state[fr].astype(np.float64), -1, -2))  # [H, S, d]
+        r = round_bf16(r.transpose(1, 0, 2).astype(np.float32))
+        g = np.asarray(gate[rows], np.float32)
+        out[rows] = rms_gate_epilogue(r, w, g, eps).reshape(s, h * d)
     return out
 
 

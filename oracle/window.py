@@ -53,15 +53,18 @@ def _sdpa(q, k, v, scale):
 
 
 def window_attention(q, k, v, num_frames, tokens_per_frame, bounds, scale, text_rows=0,
-                     anchor_frames="none"):
-    """q/k/v [text_rows + F*S, H, d] (fp32 values) -> [same] fp32."""
+                     anchor_frames="none", only_frames=None):
+    """q/k/v [text_rows + F*S, H, d] (fp32 values) -> [same] fp32.  only_frames: compute
+    those video query frames only (text rows and other frames are left zero)."""
     q, k, v = q.float(), k.float(), v.float()
     L, S = text_rows, tokens_per_frame
-    out = torch.empty_like(q)
-    if L:
+    out = torch.zeros_like(q)
+    if L and only_frames is None:
         out[:L] = _sdpa(q[:L], k, v, scale)
     gk, gv = k[:L], v[:L]
     for f, (lo, hi, extra) in enumerate(frame_keys(bounds, num_frames, anchor_frames)):
+        if only_frames is not None and f not in only_frames:
+            continue
         keys = [gk, k[L + lo * S:L + (hi + 1) * S]] + [k[L + a * S:L + (a + 1) * S] for a in extra]
         vals = [gv, v[L + lo * S:L + (hi + 1) * S]] + [v[L + a * S:L + (a + 1) * S] for a in extra]
         r0 = L + f * S

@@ -35,6 +35,11 @@ def vda_stages_golden():
 
 
 @pytest.fixture(scope="session")
+def alpha_golden():
+    return np.load(GOLDEN / "alpha_golden.npz")
+
+
+@pytest.fixture(scope="session")
 def cuda():
     import torch
     if not torch.cuda.is_available():

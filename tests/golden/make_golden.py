@@ -19,7 +19,10 @@ It imports the reference (ec-jt/vdn) and records, on seeded synthetic inputs:
     features, on two grids (--sepconv-only regenerates just these);
   * window_softmax_reference (src/models/softmax_attention/window.py:56-111) with
     global text rows, frame and chunk-aligned windows and every anchor mode
-    (--window-only regenerates just these).
+    (--window-only regenerates just these);
+  * FrameKDAAlpha.forward (src/models/linear_attention/layers.py:36-69): its seeded
+    weights, frame means and alpha, for all heads and for a head range
+    (--alpha-only regenerates just these).
 
 Nothing at test time reads the reference; the tests read only these .npz files.
 """
@@ -200,9 +203,40 @@ def window_fixtures(ref_root: str):
     np.savez_compressed(HERE / "window_golden.npz", **out)
 
 
-def main(ref_root: str, sepconv_only: bool = False, window_only: bool = False):
+def alpha_fixtures(layers_mod):
+    """FrameKDAAlpha at its own init (torch default Linear init, fla A_log / dt_bias),
+    on frame means of two magnitudes (block-like means and large ones that reach the
+    softplus tail), for every head and for the head range [1, 3)."""
+    out = {}
+    cases = {"small": dict(hidden=256, heads=4, d=64, frames=5, scale=0.05, seed=31),
+             "d128": dict(hidden=512, heads=4, d=128, frames=7, scale=3.0, seed=32)}
+    for name, c in cases.items():
+        torch.manual_seed(c["seed"])
+        mod = layers_mod.FrameKDAAlpha(c["hidden"], c["heads"], c["d"])
+        g = torch.Generator().manual_seed(c["seed"] + 100)
+        fm = torch.randn(c["frames"], c["hidden"], generator=g) * c["scale"]
+        with torch.no_grad():
+            full = mod(fm)
+            part = mod(fm, heads=slice(1, 3))
+        out.update({f"{name}_down": mod.down.weight.detach().numpy(),
+                    f"{name}_up": mod.up.weight.detach().numpy(),
+                    f"{name}_a_log": mod.A_log.detach().numpy(),
+                    f"{name}_dt_bias": mod.dt_bias.detach().numpy(),
+                    f"{name}_frame_mean": fm.numpy(), f"{name}_alpha": full.numpy(),
+                    f"{name}_alpha_heads13": part.numpy(),
+                    f"{name}_geometry": np.array([c["hidden"], c["heads"], c["d"]])})
+    np.savez_compressed(HERE / "alpha_golden.npz", **out)
+
+
+def main(ref_root: str, sepconv_only: bool = False, window_only: bool = False,
+         alpha_only: bool = False):
     sys.path.insert(0, ref_root)
     torch.set_num_threads(8)
+    from src.models.linear_attention import layers as layers_mod
+    alpha_fixtures(layers_mod)
+    if alpha_only:
+        print("wrote alpha_golden.npz")
+        return
     if window_only:
         window_fixtures(ref_root)
         print("wrote window_golden.npz")
@@ -239,5 +273,6 @@ if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     if len(args) != 1:
         raise SystemExit("usage: make_golden.py <path to the ec-jt/vdn checkout> "
-                         "[--sepconv-only | --window-only]")
-    main(args[0], sepconv_only="--sepconv-only" in sys.argv, window_only="--window-only" in sys.argv)
+                         "[--sepconv-only | --window-only | --alpha-only]")
+    main(args[0], sepconv_only="--sepconv-only" in sys.argv, window_only="--window-only" in sys.argv,
+         alpha_only="--alpha-only" in sys.argv)

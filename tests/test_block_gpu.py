@@ -62,8 +62,7 @@ def test_block_matches_reference_composition(cuda, frames, tokens):
     torch.cuda.synchronize()
     assert out.shape == (T, cfg.hidden) and out.dtype == torch.bfloat16
     assert bool(torch.isfinite(out).all())
-    ref = oblock.block_reference(x, temb, _weights(block), frames, tokens, cfg,
-                                 lambda fm: block.alpha(fm.to(cuda)).float().cpu())
+    ref = oblock.block_reference(x, temb, _weights(block), frames, tokens, cfg, _reference_alpha(block))
     err = _rel(out.float(), ref)
     assert err < 1e-2, err
 
@@ -134,6 +133,37 @@ def test_block_graph_replay_matches_eager(cuda):
         out = graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(out, w)
+
+
+def _reference_alpha(block):
+    """Alpha from the block's own FrameKDAAlpha weights through the oracle's restatement
+    (pinned to the reference's FrameKDAAlpha by tests/golden/alpha_golden.npz), so the
+    block test does not take alpha from the module under test."""
+    a = block.alpha
+    w = [t.detach().float().cpu().numpy() for t in (a.down.weight, a.up.weight, a.dt_bias, a.A_log)]
+    return oblock.alpha_fn(*w, a.num_heads, a.head_dim)
+
+
+@pytest.mark.parametrize("case", ["small", "d128"])
+@pytest.mark.parametrize("heads", [None, (1, 3)])
+@torch.no_grad()
+def test_frame_alpha_native_matches_reference_fixture(cuda, alpha_golden, case, heads):
+    """vdn_frame_alpha (FrameKDAAlpha.forward_native) against the alpha the reference's
+    FrameKDAAlpha produced from the same weights and frame means (layers.py:36-69)."""
+    from vdn_b200.linear_attention import FrameKDAAlpha
+    g = alpha_golden
+    hidden, nh, d = (int(x) for x in g[case + "_geometry"])
+    mod = FrameKDAAlpha(hidden, nh, d)
+    mod.down.weight.copy_(torch.from_numpy(g[case + "_down"]))
+    mod.up.weight.copy_(torch.from_numpy(g[case + "_up"]))
+    mod.A_log.copy_(torch.from_numpy(g[case + "_a_log"]))
+    mod.dt_bias.copy_(torch.from_numpy(g[case + "_dt_bias"]))
+    mod = mod.to(cuda)
+    fm = torch.from_numpy(g[case + "_frame_mean"]).to(cuda)
+    sl = None if heads is None else slice(*heads)
+    want = torch.from_numpy(g[case + ("_alpha" if heads is None else "_alpha_heads13")])
+    got = mod.forward_native(fm, heads=sl).cpu()
+    torch.testing.assert_close(got, want, rtol=2e-5, atol=1e-6)
 
 
 @pytest.mark.parametrize("heads", [None, (2, 5)])

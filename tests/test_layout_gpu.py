@@ -9,7 +9,7 @@ import torch
 from oracle import block as oblock
 from oracle import window as ow
 
-from test_block_gpu import _rel, _weights
+from test_block_gpu import _reference_alpha, _rel, _weights
 
 pytestmark = pytest.mark.gpu
 
@@ -76,7 +76,7 @@ def test_block_layouts_match_reference_composition(cuda, L, frames, tokens, radi
     w = _weights(block)
     w["o_b_softmax"] = block.o.bias.float().cpu()
     ref = oblock.block_reference(x, temb, w, frames, tokens, cfg,
-                                 lambda fm: block.alpha(fm.to(cuda)).float().cpu(), text_rows=L)
+                                 _reference_alpha(block), text_rows=L)
     assert _rel(out.float(), ref) < 1e-2
     if L:
         assert _rel(out[:L].float(), ref[:L]) < 1e-2

@@ -112,3 +112,90 @@ def test_window_bounds_chunk_mode():
     assert vda.window_bounds(4, 1) == [(-1, 1), (0, 2), (1, 3), (2, 4)]
     b = vda.window_bounds(12, 1, 5)
     assert b[5] == b[9] == (0, 14) and b[10] == (5, 19)
+
+
+@pytest.mark.parametrize("case", ["small", "d128"])
+def test_frame_alpha_oracle_vs_reference(alpha_golden, case):
+    """oracle.vda.frame_alpha against FrameKDAAlpha.forward run by the reference
+    (layers.py:36-69), for every head and for the head range [1, 3)."""
+    g = alpha_golden
+    hidden, heads, d = (int(x) for x in g[case + "_geometry"])
+    up, dt = g[case + "_up"], g[case + "_dt_bias"]
+    got = vda.frame_alpha(g[case + "_frame_mean"], g[case + "_down"], up, dt, g[case + "_a_log"], heads, d)
+    want = g[case + "_alpha"]
+    assert got.shape == want.shape
+    np.testing.assert_allclose(got, want, rtol=2e-6, atol=1e-7)
+    rows = slice(1 * d, 3 * d)
+    part = vda.frame_alpha(g[case + "_frame_mean"], g[case + "_down"], up[rows], dt[rows],
+                           g[case + "_a_log"][1:3], 2, d)
+    np.testing.assert_allclose(part, g[case + "_alpha_heads13"], rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("case", MX_CASES)
+def test_qdq_torch_matches_numpy_oracle(mxfp8_golden, case):
+    """The torch CPU restatement used by the full-size checks gives exactly the values of
+    dequantize(quantize(x)) on every fixture."""
+    import torch
+    x = _x(mxfp8_golden, case + "_x")
+    r, k = x.shape
+    want = mx.dequantize(*mx.quantize(x))[:r, :k].astype(np.float32)
+    got = mx.qdq_torch(torch.from_numpy(np.ascontiguousarray(x, np.float32))).numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_qdq_torch_random_and_subnormal_blocks():
+    import torch
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(300, 640, generator=g) * torch.exp2(torch.randint(-140, 100, (300, 1), generator=g).float())
+    x[5, :32] = 0.0
+    x[6, :32] = -0.0
+    x = x.bfloat16().float()
+    want = mx.dequantize(*mx.quantize(x.numpy()))[:300, :640].astype(np.float32)
+    got = mx.qdq_torch(x).numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("text_rows,chunk", [(0, 0), (24, 0), (0, 2)])
+def test_block_oracle_sampled_frames_equal_full(text_rows, chunk):
+    """block_reference(out_frames=...) returns exactly the full evaluation's rows of those
+    frames (the full-size GPU checks rely on it)."""
+    import types
+    import torch
+    from oracle import block as oblock
+    cfg = types.SimpleNamespace(hidden=256, heads=2, head_dim=128, ffn=512, radius=1, eps=1e-6,
+                                gelu="tanh", chunk=chunk, anchor_frames="none", text_state=bool(text_rows))
+    g = torch.Generator().manual_seed(3)
+    hd, H, d, ffn = 256, 2, 128, 512
+    r = lambda *s, std=0.05: torch.randn(*s, generator=g) * std
+    w = dict(adaln_w=r(6 * hd, hd), adaln_b=r(6 * hd), norm1=torch.ones(hd), norm2=torch.ones(hd),
+             qkv=r(3 * hd, hd), qkv_b=r(3 * hd), o=r(hd, hd), ol=r(hd, hd), o_b=r(hd), o_b_softmax=r(hd),
+             up=r(ffn, hd), up_b=r(ffn), down=r(hd, ffn), down_b=r(hd), sg_w=r(H, hd), sg_b=r(H),
+             beta_w=r(H, hd), og_down=r(d, hd), og_up=r(hd, d), og_b=r(hd))
+    frames, tokens = 5, 16
+    x = torch.randn(text_rows + frames * tokens, hd, generator=g).bfloat16()
+    temb = torch.randn(hd, generator=g)
+    alpha = lambda fm: torch.full((frames, H, d), 0.9)
+    full = oblock.block_reference(x, temb, w, frames, tokens, cfg, alpha, text_rows=text_rows)
+    pick = [4, 0, 2]
+    part = oblock.block_reference(x, temb, w, frames, tokens, cfg, alpha, text_rows=text_rows,
+                                  out_frames=pick)
+    want = torch.cat([full[text_rows + f * tokens:text_rows + (f + 1) * tokens] for f in pick])
+    assert torch.equal(part, want)
+
+
+@pytest.mark.parametrize("case", ["d128", "d128_wide", "d128_text"])
+def test_vda_oracle_out_frames_equal_full(vda_golden, case):
+    """readout(out_frames=...) gives exactly the full readout's rows of those frames."""
+    kw, _ = _vda_inputs(vda_golden, case)
+    full = vda.branch_forward(**kw)
+    f, s = kw["num_frames"], kw["tokens_per_frame"]
+    part = vda.branch_forward(**kw, out_frames=[f - 1, 0])
+    for fr in (f - 1, 0):
+        assert np.array_equal(part[fr * s:(fr + 1) * s], full[fr * s:(fr + 1) * s])
+
+
+def test_round_bf16_matches_bit_formula():
+    g = np.random.default_rng(5)
+    x = (g.standard_normal(200_000) * np.exp2(g.integers(-130, 120, 200_000))).astype(np.float32)
+    x[:4] = [0.0, -0.0, 1.0 + 2.0 ** -8, 1.0 + 3 * 2.0 ** -8]   # ties round to even
+    assert np.array_equal(mx.round_bf16(x).view(np.uint32), mx.bf16_to_f32(mx.f32_to_bf16_bits(x)).view(np.uint32))

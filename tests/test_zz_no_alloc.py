@@ -6,10 +6,13 @@ memory through its own pool, or a latency-critical loop that cannot take
 cudaMalloc's implicit device synchronisation.  For them the library carries a
 fixed 64 MiB scratch array and this entry point uses it instead of a caller
 workspace.  This test calls it through the C ABI and checks that two calls in a
-row (with different inputs, so stale scratch contents would show) match the
-regular workspace entry point, vdn_vda_forward, within the branch tolerance used
-elsewhere in the suite (relative L2 < 4e-3), and that a geometry larger than the
-scratch is rejected with a clear error.
+row (with different inputs, so stale scratch contents would show) give exactly
+the output of the regular workspace entry point, vdn_vda_forward (the two run
+the same deterministic kernels, so the results are bit-identical), that the
+second call leaves the device's free memory unchanged (it allocates nothing),
+and that the size limit sits exactly where the 64 MiB scratch runs out: 22
+frames x 10 heads at d = 128 are accepted, 23 x 10 are rejected with a clear
+error.
 
 The file is named so that pytest collects it last.
 """
@@ -60,16 +63,45 @@ def test_noalloc_matches_workspace_entry_point_twice():
     f, s, h, d = 7, 96, 3, 128
     bounds = [(t - 1, t + 1) for t in range(f)]
     ws = torch.empty(_lib.load().vdn_vda_workspace_size(f, s, h, d), dtype=torch.uint8, device=dev)
-    for seed in (1, 2):                       # two calls in a row, different inputs
+    for call, seed in enumerate((1, 2)):      # two calls in a row, different inputs
         x = _inputs(f, s, h, d, seed, dev)
         want = torch.empty(f * s, h * d, device=dev, dtype=torch.bfloat16)
         got = torch.full_like(want, float("nan"))
         assert _call("vdn_vda_forward", _lib, x, f, s, h, d, want, bounds, ws) == 0
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info(dev)[0]
         rc = _call("vdn_vda_forward_noalloc", _lib, x, f, s, h, d, got, bounds)
         assert rc == 0, _lib.load().vdn_last_error()
         torch.cuda.synchronize()
+        if call == 1:                         # the first call may load the scratch's module
+            assert torch.cuda.mem_get_info(dev)[0] == free_before
         assert bool(torch.isfinite(got).all())
-        assert _rel_l2(got, want) < 4e-3
+        assert torch.equal(got, want), _rel_l2(got, want)
+
+
+@torch.no_grad()
+@pytest.mark.parametrize("frames,accepted", [(22, True), (23, False)])
+def test_noalloc_size_limit(frames, accepted):
+    from vdn_b200 import _lib
+    dev = torch.device("cuda", 0)
+    f, s, h, d = frames, 8, 10, 128
+    need = _lib.load().vdn_vda_workspace_size(f, s, h, d)
+    assert (need <= 64 << 20) == accepted
+    x = _inputs(f, s, h, d, 3, dev)
+    out = torch.empty(f * s, h * d, device=dev, dtype=torch.bfloat16)
+    bounds = [(max(t - 1, 0), min(t + 1, f - 1)) for t in range(f)]
+    rc = _call("vdn_vda_forward_noalloc", _lib, x, f, s, h, d, out, bounds)
+    torch.cuda.synchronize()
+    if accepted:
+        assert rc == 0, _lib.load().vdn_last_error()
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        want = torch.empty_like(out)
+        assert _call("vdn_vda_forward", _lib, x, f, s, h, d, want, bounds, ws) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+    else:
+        assert rc == _lib.VDN_ERR_VALUE
+        assert "scratch" in _lib.load().vdn_last_error().decode()
 
 
 @torch.no_grad()

@@ -49,36 +49,8 @@ __device__ __forceinline__ bool bar_and(uint32_t id, uint32_t count, bool pred) 
   return out != 0;
 }
 
-// x * sigmoid(x).  VDN_SILU selects the formulation (timed variants):
-//   0: __expf + __fdividef (two MUFU ops)
-//   1: ex2.approx + rcp.approx (two MUFU ops, no range handling)
-//   2: ex2.approx + magic-constant reciprocal and Newton steps (one MUFU op)
-#ifndef VDN_SILU
-#define VDN_SILU 0
-#endif
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float rcp_approx(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float silu_fast(float x) {
-#if VDN_SILU == 0
-  return __fdividef(x, 1.0f + __expf(-x));
-#elif VDN_SILU == 1
-  return x * rcp_approx(1.0f + ex2_approx(fminf(-x, 80.0f) * 1.4426950408889634f));
-#else
-  const float y = 1.0f + ex2_approx(fminf(-x, 80.0f) * 1.4426950408889634f);
-  float r = __int_as_float(0x7EF311C3 - __float_as_int(y));
-#pragma unroll
-  for (int it = 0; it < 3; ++it) r = fmaf(r, fmaf(-y, r, 1.0f), r);
-  return x * r;
-#endif
-}
+// x * sigmoid(x) with the fast exponential and divide (two MUFU operations).
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // ------------------------------------------------------------------ statistics
 // Persistent, warp-specialised: grid = min(F*H, SMs), one CTA per SM walking
