@@ -186,6 +186,19 @@ def cublas_fp8_ms(torch, m, n, k, dev, stream, reps=10):
     return kernel_times(torch, [("cublas", fn)], reps, stream)["cublas"]
 
 
+def torch_mxfp8_ms(torch, xq, xs, wq, ws, stream, reps=10):
+    """Device ms of torch's block-scaled MXFP8 GEMM on the same codes and swizzled scales:
+    the call the reference's MXFP8Linear makes (src/models/ops/mxfp8_linear.py:89-94,
+    F.scaled_mm with BlockWise1x32 / SWIZZLE_32_4_4; gated to SM120 there).  Raises if
+    this torch / cuBLAS build does not run it on this GPU."""
+    import torch.nn.functional as Fn
+    e4, e8 = torch.float8_e4m3fn, torch.float8_e8m0fnu
+    fn = lambda: Fn.scaled_mm(xq.view(e4), wq.view(e4).T, xs.view(e8), Fn.ScalingType.BlockWise1x32,
+                              ws.view(e8), Fn.ScalingType.BlockWise1x32, Fn.SwizzleType.SWIZZLE_32_4_4,
+                              Fn.SwizzleType.SWIZZLE_32_4_4, output_dtype=torch.bfloat16)
+    return kernel_times(torch, [("mx", fn)], reps, stream)["mx"]
+
+
 # ------------------------------------------------------------------ VDA
 VDA_CFG = dict(F=21, S=1560, H=40, d=128)
 
@@ -391,11 +404,16 @@ def bench_gemm(args, torch, dist, rank, world):
             cub = c["flops"] / (cublas_fp8_ms(torch, M, c["n"], c["k"], dev, stream) * 1e-3) / 1e12
         except Exception:  # comparator only
             cub = None
+        try:
+            tmx = c["flops"] / (torch_mxfp8_ms(torch, c["xq"], c["xs"], c["wq"], c["ws"], stream) * 1e-3) / 1e12
+        except Exception as e:  # comparator only
+            tmx = repr(e)[:100]
         qbytes = M * c["k"] * 2 + (M + 127) // 128 * 128 * c["k"] * 33 // 32
         per_shape[c["name"]] = {"m": M, "n": c["n"], "k": c["k"], "gemm_ms": round(kt[c["name"]], 4),
                                 "tflops": round(tf, 1), "frac_fp8_peak": round(tf / fp8_peak, 4),
                                 "cublas_fp8_per_tensor_tflops": None if cub is None else round(cub, 1),
                                 "frac_of_cublas": None if cub is None else round(tf / cub, 4),
+                                "torch_mxfp8_tflops": round(tmx, 1) if isinstance(tmx, float) else tmx,
                                 "quantize_ms": round(kt[c["name"] + "_quantize"], 4),
                                 "quantize_gbs": round(qbytes / (kt[c["name"] + "_quantize"] * 1e-3) / 1e9, 1)}
     top = cases[0]

@@ -4,6 +4,8 @@ Composition of the reference pieces (ec-jt/vdn), evaluated in fp32 on the CPU
 with the MXFP8 quantisation points of the B200 path reproduced bit-exactly by
 oracle.mxfp8 (so the GEMM inputs match) and the VDA branch by oracle.vda:
 
+  AdaLN modulation ........ bf16 SiLU of the timestep embedding, then the bf16 projection
+                            (block.adaln_proj(temb), src/models/ops/fused_block.py:118)
   pre-norm + AdaLN ........ src/models/ops/fused_block.py:43-46 (_pre_ref)
   MXFP8 linears ........... src/models/ops/mxfp8_linear.py:60-102 (dequantised GEMM)
   window softmax .......... src/models/softmax_attention/window.py:56-111
@@ -98,7 +100,10 @@ def block_reference(x, temb, w, frames, tokens, cfg, alpha_fn, text_rows=0, out_
     T = frames * tokens
     n = L + T
     x = x.float()
-    ada = _bf16(F.silu(_bf16(temb.float())) @ w["adaln_w"].T + w["adaln_b"]).view(6, hd)
+    # The eager bf16 AdaLN: SiLU of the bf16 embedding is itself a bf16 tensor before the
+    # projection (at full size the peaked window softmax turns the 2^-9 difference of
+    # skipping that rounding into a few percent of the block output).
+    ada = _bf16(_bf16(F.silu(_bf16(temb.float()))) @ w["adaln_w"].T + w["adaln_b"]).view(6, hd)
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = ada
     y1 = prenorm(x, w["norm1"], scale_msa, shift_msa, cfg.eps)
     qkv = _linear(_qdq(y1), w["qkv"], w["qkv_b"])

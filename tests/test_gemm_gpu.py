@@ -202,3 +202,35 @@ def test_gemm_act_quantize_matches_unfused(cuda, act, rows):
         rq, rs = quantize_activation(y)
     torch.cuda.synchronize()
     assert torch.equal(q, rq) and torch.equal(s, rs)
+
+
+@pytest.mark.parametrize("m,n,k", [(4096, 15360, 5120), (32768, 5120, 13824)])
+@torch.no_grad()
+def test_gemm_matches_torch_blockscaled_mxfp8(cuda, m, n, k):
+    """The same codes and swizzled scales through torch's block-scaled MXFP8 GEMM
+    (F.scaled_mm, BlockWise1x32 / SWIZZLE_32_4_4: the reference MXFP8Linear's own call,
+    src/models/ops/mxfp8_linear.py:89-94): the two fp32-accumulated results agree to a
+    few bf16 ulps (different accumulation order only).  Skipped where this torch build
+    does not run that GEMM on sm_100."""
+    import torch.nn.functional as Fn
+    from vdn_b200.mxfp8_linear import mxfp8_gemm
+    from vdn_b200.mxfp8_quant import quantize_activation
+    g = torch.Generator(device=cuda).manual_seed(m + n)
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=cuda, generator=g) * 0.02).bfloat16()
+    xq, xs = quantize_activation(x)
+    wq, ws = quantize_activation(w)
+    e4, e8 = torch.float8_e4m3fn, torch.float8_e8m0fnu
+    try:
+        want = Fn.scaled_mm(xq.view(e4), wq.view(e4).T, xs.view(e8), Fn.ScalingType.BlockWise1x32,
+                            ws.view(e8), Fn.ScalingType.BlockWise1x32, Fn.SwizzleType.SWIZZLE_32_4_4,
+                            Fn.SwizzleType.SWIZZLE_32_4_4, output_dtype=torch.bfloat16)
+    except Exception as e:
+        pytest.skip(f"torch block-scaled MXFP8 GEMM unavailable on this device: {e!r}"[:200])
+    got = mxfp8_gemm(xq, xs, wq, ws, n, rows=m)
+    torch.cuda.synchronize()
+    want = want[:m, :n].float()
+    diff = (got.float() - want).abs()
+    # at most one bf16 ulp apart (<= 2^-7 of the value): fp32 sums rounded to bf16
+    assert bool((diff <= 2 ** -7 * want.abs() + 1e-4).all()), float(diff.max())
+    assert float(diff.norm() / want.norm()) < 1e-3

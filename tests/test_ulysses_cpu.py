@@ -265,3 +265,45 @@ def test_branch_parallel_routing_on_gloo_ranks(world):
                     p.terminate()
                 if p.pid is not None:
                     p.join()
+
+
+# ------------------------------------------------------------------- install_ulysses
+def _small_stack(heads=2, depth=2):
+    from vdn_b200.block import BlockConfig
+    from vdn_b200.stack import HybridStack
+    cfg = BlockConfig(hidden=128 * heads, heads=heads, head_dim=128, ffn=256, lora_rank=4)
+    return HybridStack(cfg, depth=depth, seed=1, device="cpu")
+
+
+def test_install_ulysses_refusals():
+    """The reference's checks (src/inference/utils/ulysses.py:717-764)."""
+    from vdn_b200.ulysses import install_ulysses
+    with pytest.raises(ValueError, match="requires a HybridAttention checkpoint"):
+        install_ulysses(torch.nn.Linear(2, 2), _runtime(0, 2))
+    with pytest.raises(ValueError, match="attention heads are not divisible by 3 ranks"):
+        install_ulysses(_small_stack(heads=2), _runtime(0, 3))
+    mixed = _small_stack(heads=2)
+    mixed.blocks[1].cfg = type(mixed.cfg)(hidden=512, heads=4, head_dim=128, ffn=256)
+    with pytest.raises(ValueError, match="same attention head count"):
+        install_ulysses(mixed, _runtime(0, 2))
+    with pytest.raises(ValueError, match="softmax_ranks must lie in"):
+        install_ulysses(_small_stack(heads=2), _runtime(0, 2), softmax_ranks=2)
+
+
+def test_install_ulysses_binds_runtime_and_forwards():
+    from vdn_b200.ulysses import install_ulysses
+    stack = _small_stack(heads=2)
+    rt = _runtime(1, 2)
+    install_ulysses(stack, rt)
+    assert stack._ulysses_runtime is rt
+    assert all(b._ulysses_runtime is rt for b in stack.transformer_blocks)
+    assert stack.forward.__func__.__name__ == "_ulysses_transformer_forward"
+    assert stack.blocks[0].forward.__func__.__name__ == "_ulysses_block_forward"
+    x = torch.zeros(4 * 8, 256, dtype=torch.bfloat16)
+    with torch.enable_grad(), pytest.raises(RuntimeError, match="inference-only"):
+        stack(x, torch.zeros(256), 4, 8)
+    with torch.no_grad(), pytest.raises(ValueError, match="text_rows \\+ frames \\* tokens"):
+        stack(x, torch.zeros(256), 5, 8)
+    brt = _runtime(0, 2)
+    install_ulysses(_small_stack(heads=2), brt, softmax_ranks=1)
+    assert brt.branch_parallel and brt.softmax_ranks == 1

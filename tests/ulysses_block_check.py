@@ -44,8 +44,7 @@ def main():
         x = torch.randn(T, cfg.hidden, generator=g).bfloat16().to(dev)
         temb = torch.randn(cfg.hidden, generator=g).to(dev)
         full = block(x, temb, frames, tokens)
-        rt.close()
-        rt.sequence_length = 0
+        rt.reset()
         rt.configure(T, cfg.heads)
         shards = {}
         for mode in ("alltoall", "peer", "peer"):     # the peer path twice: buffer reuse
@@ -78,7 +77,7 @@ def main():
             ex.check()                              # no device fence timed out
         # Branch-parallel layouts: n softmax ranks + P - n VDA ranks.
         for n_soft, brt in branch_runtimes.items():
-            brt.sequence_length = 0
+            brt.reset()
             brt.configure(T, cfg.heads)
             shard = block(x[brt.local_start:brt.local_end].contiguous(), temb, frames, tokens, brt)
             torch.cuda.synchronize()
@@ -99,7 +98,7 @@ def main():
             torch.nn.init.normal_(tblock.softmax_gate.weight, std=0.05)
         xt = torch.randn(L + T, tcfg.hidden, generator=g).bfloat16().to(dev)
         tfull = tblock(xt, temb, frames, tokens, text_rows=L)
-        text_rt.sequence_length = 0
+        text_rt.reset()
         text_rt.configure(L + T, tcfg.heads)
         lo, hi = text_rt.local_start, text_rt.local_end
         shard = tblock(xt[lo:hi].contiguous(), temb, frames, tokens, text_rt, text_rows=L)
@@ -115,6 +114,26 @@ def main():
         if not torch.equal(shards["alltoall"], shards["peer"]):
             d = (shards["alltoall"].float() - shards["peer"].float()).abs().max().item()
             print(f"rank {rt.rank} alltoall vs peer max abs diff {d:.3e}", flush=True)
+    # install_ulysses: the installed sharded model forward equals the unsharded stack.
+    from vdn_b200.stack import HybridStack
+    from vdn_b200.ulysses import install_ulysses
+    scfg = BlockConfig(hidden=512, heads=4, head_dim=128, ffn=1024, radius=1, lora_rank=8)
+    stack = HybridStack(scfg, depth=2, seed=5, device=dev)
+    frames, tokens = 5, 48
+    gs = torch.Generator().manual_seed(77)
+    xs = torch.randn(frames * tokens, scfg.hidden, generator=gs).bfloat16().to(dev)
+    ts = torch.randn(scfg.hidden, generator=gs).to(dev)
+    want = stack(xs, ts, frames, tokens)
+    irt = UlyssesRuntime(rank=rt.rank, world_size=rt.world_size, local_rank=rt.local_rank, device=dev,
+                         backend="nccl", timeout_seconds=60)
+    install_ulysses(stack, irt)
+    got = stack(xs, ts, frames, tokens)
+    torch.cuda.synchronize()
+    err = float((got.double() - want.double()).norm() / want.double().norm())
+    print(f"rank {rt.rank} install_ulysses depth=2 rows={got.shape[0]} rel_l2={err:.3e}", flush=True)
+    if not (got.shape == want.shape and bool(torch.isfinite(got).all()) and err < 4e-3):
+        failures.append(("install_ulysses", err))
+    irt.close()
     rt.close()
     flag = torch.tensor([len(failures)], device=dev)
     dist.all_reduce(flag)

@@ -28,6 +28,11 @@ class HybridStack(nn.Module):
         self.blocks = nn.ModuleList(HybridBlock(self.cfg, seed=seed + 7919 * i, device=device, init=init)
                                     for i in range(depth))
 
+    @property
+    def transformer_blocks(self) -> nn.ModuleList:
+        """The reference model's name for its block list (install_ulysses walks it)."""
+        return self.blocks
+
     @torch.no_grad()
     def forward(self, x, temb, frames, tokens, runtime=None, text_rows=0):
         for block in self.blocks:
