@@ -125,8 +125,8 @@ class ClockSampler:
 NCU_TRAFFIC_BYTES = {
     "mxfp8_gemm_qkv": 1471.4e6 + 981.8e6,
     "statistics": 674.4e6 + 89.9e6,
-    "factors": 110.6e6 + 52.4e6,
-    "scan": 190.7e6 + 76.6e6,
+    "factors": None,
+    "scan": None,
     "gather": 100.1e6 + 8.3e6,
     "readout": 698.8e6 + 297.0e6,
 }
@@ -250,25 +250,27 @@ def bench_vda(args, torch, dist, rank, world):
     nbytes = vda_bytes(F, S, H, d)
     value = world * nbytes / (per_step_ms * 1e-3) / 1e9
 
-    # Per-kernel device times of the five stage launches (same stream).
+    # Per-kernel device times of the five stage launches (same stream), on the regions of
+    # the forward's own workspace (d = 128: A then the forward bank over it, B, the split
+    # inverses, the reverse bank, the gathered state).
     plane = F * H * d * d
     up = lambda b: (b + 255) // 256 * 256
     A = ws[: plane * 4].view(torch.float32)
     B = ws[up(plane * 4): up(plane * 4) + plane * 4].view(torch.float32)
-    pre = ws[2 * up(plane * 4): 2 * up(plane * 4) + plane * 4].view(torch.float32)
-    suf = ws[3 * up(plane * 4): 3 * up(plane * 4) + plane * 4].view(torch.float32)
-    state = ws[4 * up(plane * 4): 4 * up(plane * 4) + plane * 2]
+    planes = ws[2 * up(plane * 4): 2 * up(plane * 4) + plane * 6]
+    pre = A
+    suf = ws[2 * up(plane * 4) + up(plane * 6): 2 * up(plane * 4) + up(plane * 6) + plane * 4].view(torch.float32)
+    state = ws[3 * up(plane * 4) + up(plane * 6): 3 * up(plane * 4) + up(plane * 6) + plane * 2]
     sf = S * q.stride(0)
     launches = [
         ("statistics", lambda: _lib.call("vdn_vda_statistics", _lib.ptr(k), sf, q.stride(0), q.stride(1),
                                          _lib.ptr(v), sf, q.stride(0), q.stride(1), _lib.ptr(beta),
                                          S * beta.stride(0), beta.stride(0), beta.stride(1), 0, F, S, H,
                                          d, _lib.ptr(A), _lib.ptr(B), st)),
-        ("factors", lambda: _lib.call("vdn_delta_factors", _lib.ptr(A), _lib.ptr(B), _lib.ptr(alpha),
-                                      F * H, d, _lib.ptr(pre), _lib.ptr(suf), st)),
-        ("scan", lambda: _lib.call("vdn_vda_scan", _lib.ptr(pre), _lib.ptr(suf), None, F, H, d,
-                                   _lib.ptr(A), _lib.ptr(B), st)),
-        ("gather", lambda: _lib.call("vdn_vda_gather", _lib.ptr(A), _lib.ptr(B), _lib.ptr(alpha), buf,
+        ("factors", lambda: _lib.call("vdn_vda_factor_inverse", _lib.ptr(A), F * H, _lib.ptr(planes), st)),
+        ("scan", lambda: _lib.call("vdn_vda_scan_tc", _lib.ptr(planes), _lib.ptr(B), _lib.ptr(alpha), None, F, H,
+                                   _lib.ptr(pre), _lib.ptr(suf), None, st)),
+        ("gather", lambda: _lib.call("vdn_vda_gather", _lib.ptr(pre), _lib.ptr(suf), _lib.ptr(alpha), buf,
                                      None, 1, F, H, d, _lib.ptr(state), _lib.DTYPE_BF16, st)),
         ("readout", lambda: _lib.call("vdn_vda_readout", _lib.ptr(q), sf, q.stride(0), q.stride(1),
                                       _lib.ptr(state), _lib.ptr(gate), S * gate.stride(0), gate.stride(0),
@@ -278,8 +280,8 @@ def bench_vda(args, torch, dist, rank, world):
     n_tok_h_d = n * H * d
     algo = {  # algorithmic bytes per launch
         "statistics": 2 * n_tok_h_d * 2 + n * H * 2 + 2 * F * H * d * d * 4,
-        "factors": 2 * F * H * d * d * 4 + F * H * d * 4 + 2 * F * H * d * d * 4,
-        "scan": 2 * F * H * d * d * 4 + 2 * F * H * d * d * 4,
+        "factors": F * H * d * d * 4 + F * H * d * d * 6,
+        "scan": F * H * d * d * 6 * 2 + F * H * d * d * 4 * 2 + 2 * F * H * d * d * 4,
         "gather": 2 * F * H * d * d * 4 + F * H * d * d * 2,
         "readout": 2 * n_tok_h_d * 2 + F * H * d * d * 2 + n_tok_h_d * 2,
     }

@@ -300,6 +300,22 @@ int vdn_vda_readout(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh,
                     const float* norm_weight, float eps, int F, int S, int H, int d,
                     void* out, cudaStream_t stream);
 
+/* The two tensor-core stages vdn_vda_forward runs for d = 128 in place of
+ * vdn_delta_factors + vdn_vda_scan (no separate counterpart in the reference: together
+ * they compute delta_rule.py:45-60 and scan.py:176-261 with the injection J = B inv
+ * folded into each scan step).
+ * vdn_vda_factor_inverse: inv = (I + A)^-1 for n fp32 [128, 128] matrices A, written
+ * as three bf16 planes whose sum is the fp32 inverse, each plane in the 128B-swizzled
+ * K-major tcgen05 operand layout: 98304 bytes per matrix at `planes` (16-byte aligned).
+ * vdn_vda_scan_tc: P_f = (P_{f-1} diag(alpha_f) + B_f) inv_f over the F frames in both
+ * directions (forward into prefix, reverse into suffix, [F, H, 128, 128] fp32), from
+ * the planes of [F, H] inverses, B [F, H, 128, 128] fp32, alpha [F, H, 128] fp32 and an
+ * optional seed [H, 128, 128]; status (optional int32) receives VDN_ERR_TIMEOUT if a
+ * bounded wait gave up. */
+int vdn_vda_factor_inverse(const float* A, int64_t n, void* planes, cudaStream_t stream);
+int vdn_vda_scan_tc(const void* planes, const float* B, const float* alpha, const float* seed, int F, int H,
+                    float* prefix, float* suffix, int* status, cudaStream_t stream);
+
 /* Workspace bytes vdn_vda_forward needs for this geometry. */
 size_t vdn_vda_workspace_size(int F, int S, int H, int d);
 

@@ -1,53 +1,159 @@
 """GPU: the hybrid block at the BASELINE sizes against the CPU composition of the
-reference pieces, on sampled frames.
+reference pieces.
 
-Config 3: one block at hidden 5120, 40 x 128 heads, FFN 13824, 21 frames x 1560
-tokens (32760 rows), the geometry bench.py times.  Config 4's shape: two stacked
-blocks over 512 text rows packed in front of 60 x 1560 video rows (94112 rows);
-the second block takes the first block's GPU output as its input, so each block is
-checked on its own at full size.
+Config 3 (hidden 5120, 40 x 128 heads, FFN 13824, 21 frames x 1560 tokens, the
+geometry bench.py times), checked two ways:
 
-The oracle (oracle/block.py, out_frames=...) evaluates only the sampled frames'
-rows of the window softmax, output projection and FFN, but every row of what those
-rows depend on: the pre-norm, QKV and gates of the whole sequence (the softmax
-keys, the VDA statistics and scans over every frame, alpha's frame means).  Alpha
-comes from the block's FrameKDAAlpha weights through the oracle's restatement
+* stage by stage: the test replays the block's own stages (the same library calls
+  the block makes, asserted to give exactly the block's output), and checks every
+  stage against the oracle's stage evaluated on the GPU's inputs to that stage, at
+  full size on sampled frames / heads, with the bars of the small-shape tests;
+* end to end against oracle/block.py on sampled frames (out_frames: everything the
+  sampled rows depend on is still computed for every row).  The end-to-end bar is
+  5e-2, not the small block's 1e-2: with these seeded weights the full-size block
+  amplifies any 1e-3-level difference about tenfold.  MXFP8 keeps 3 mantissa bits,
+  so a 2e-3 perturbation flips ~2 % of the E4M3 codes by a whole 12.5 % step at each
+  of the block's four quantisation points, and the window softmax (q . k scores of
+  standard deviation ~5 over 4680 keys) is peaked.  Measured on the CPU oracle
+  alone: 2e-3 noise on the attention output (the size of cuDNN's bf16-softmax
+  error, a library kernel outside the parity contract) moves the block output by
+  2.1 %; one-ulp flips in 1 % of the AdaLN outputs move it by 2.6 %.
+
+Config 4's shape: two stacked blocks over 512 text rows packed in front of 60 x 1560
+video rows (94112 rows); the second block takes the first block's GPU output, and
+each block is checked end to end on sampled frames at the same bar.
+
+Alpha comes from the block's FrameKDAAlpha weights through the oracle's restatement
 (pinned to the reference's FrameKDAAlpha), not from the module under test.
-Tolerance: relative L2 < 1e-2 on the sampled rows, the small-shape block bar
-(bf16 rounding points and the rare one-code MXFP8 flips they cause).
 """
+import numpy as np
 import pytest
 import torch
+import torch.nn.functional as F
 
 from oracle import block as oblock
+from oracle import vda as ovda
 from test_block_gpu import _reference_alpha, _rel, _weights
 
 pytestmark = pytest.mark.gpu
+
+END_TO_END = 5e-2
 
 
 def _rows(out, frames, tokens, text_rows=0):
     return torch.cat([out[text_rows + f * tokens:text_rows + (f + 1) * tokens] for f in frames])
 
 
-@torch.no_grad()
-def test_block_config3_full_size_sampled_frames(cuda):
+@pytest.fixture(scope="module")
+def config3(cuda):
     from vdn_b200.block import HybridBlock
+    torch.set_grad_enabled(False)
     block = HybridBlock(seed=0, device=cuda)                  # BlockConfig() = BASELINE config 3
     cfg = block.cfg
     assert (cfg.hidden, cfg.heads, cfg.head_dim, cfg.ffn) == (5120, 40, 128, 13824)
-    frames, tokens = 21, 1560
     g = torch.Generator().manual_seed(2024)
-    x = torch.randn(frames * tokens, cfg.hidden, generator=g).bfloat16()
+    x = torch.randn(21 * 1560, cfg.hidden, generator=g).bfloat16()
     temb = torch.randn(cfg.hidden, generator=g)
-    out = block(x.to(cuda), temb.to(cuda), frames, tokens)
+    out = block(x.to(cuda), temb.to(cuda), 21, 1560)
     torch.cuda.synchronize()
-    assert bool(torch.isfinite(out).all())
+    yield block, x, temb, out
+    torch.set_grad_enabled(True)
+
+
+@torch.no_grad()
+def test_block_config3_stages_full_size(cuda, config3):
+    from vdn_b200.linear_attention import vda_forward, window_bounds
+    from vdn_b200.mxfp8_kernels import launch_prenorm_quantize
+    from vdn_b200.mxfp8_quant import quantize_activation
+    from vdn_b200.window import window_softmax
+    block, x, temb, out = config3
+    cfg = block.cfg
+    hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+    frames, tokens = 21, 1560
+    T = frames * tokens
+    w = _weights(block)
+    xd = x.to(cuda)
+    # The block's stages, replayed (same calls as HybridBlock.forward's one-GPU path).
+    ada = block._adaln(temb.to(cuda))
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = ada
+    idx = torch.zeros(T, dtype=torch.int64, device=cuda)
+    y1, q1, s1, _ = launch_prenorm_quantize(xd, block.norm1, cfg.eps, scale_msa.view(1, hd),
+                                            shift_msa.view(1, hd), idx, write_bf16=True)
+    qkv = torch.empty(T, 3 * hd, device=cuda, dtype=torch.bfloat16)
+    block._gemm(q1, s1, block.qkv, T, qkv, bias=block.qkv.bias)
+    g3 = block._gate_projections(y1)
+    og = block.output_gate
+    lgate = torch.sigmoid(F.linear(g3[:, 2 * H:], og.up.weight, og.up.bias))
+    q, k, v = (qkv[:, i * hd:(i + 1) * hd].view(T, H, d) for i in range(3))
+    att = torch.empty(T, H, d, device=cuda, dtype=torch.bfloat16)
+    window_softmax(q, k, v, g3[:, :H], frames, tokens, cfg.radius, out=att)
+    frame_mean = y1.view(frames, tokens, hd).mean(1, dtype=torch.float32)
+    alpha = block.alpha.forward_native(frame_mean)
+    bounds = window_bounds(frames, cfg.radius)
+    lin = vda_forward(q, k, v, g3[:, H:2 * H], lgate.view(T, H, d), alpha, bounds, frames, tokens, block.vda_norm)
+    attq = quantize_activation(att.view(T, hd), check_finite=False)
+    linq = quantize_activation(lin, check_finite=False)
+    x1 = torch.empty_like(xd)
+    block._gemm(attq[0], attq[1], block.o, T, x1, second=(linq, block.ol), bias=block.o_bias, resid=xd,
+                gate=gate_msa.contiguous())
+    x2 = block._ffn(x1, shift_mlp, scale_mlp, gate_mlp, idx)
+    torch.cuda.synchronize()
+    assert torch.equal(x2, out)                               # the replay is the block
+
+    # Each stage against the oracle on the GPU's inputs to that stage.
+    cpu = lambda t: t.float().cpu()
+    ada_o = oblock._bf16(oblock._bf16(F.silu(oblock._bf16(temb.float()))) @ w["adaln_w"].T + w["adaln_b"])
+    assert _rel(cpu(ada).view(-1), ada_o) < 2e-3             # bf16 GEMM, accumulation order
+    ada_g = cpu(ada)
+    sample = [0, 10, 20]
+    rows = torch.cat([torch.arange(f * tokens, (f + 1) * tokens) for f in sample])
+    y1_o = oblock.prenorm(x[rows].float(), w["norm1"], ada_g[1], ada_g[0], cfg.eps)
+    assert _rel(cpu(y1)[rows], y1_o) < 2e-3
+    y1c = cpu(y1)
+    qkv_o = oblock._linear(oblock._qdq(y1c[rows]), w["qkv"], w["qkv_b"])
+    assert _rel(cpu(qkv)[rows], qkv_o) < 1e-3
+    sg_o = oblock._bf16(torch.sigmoid(oblock._bf16(y1c[rows] @ w["sg_w"].T + w["sg_b"])))
+    be_o = oblock._bf16(torch.sigmoid(oblock._bf16(y1c[rows] @ w["beta_w"].T)))
+    lg_o = oblock._bf16(torch.sigmoid(oblock._bf16(oblock._bf16(y1c[rows] @ w["og_down"].T) @ w["og_up"].T
+                                                   + w["og_b"])))
+    assert _rel(cpu(g3[:, :H])[rows], sg_o) < 2e-3 and _rel(cpu(g3[:, H:2 * H])[rows], be_o) < 2e-3
+    assert _rel(cpu(lgate)[rows], lg_o) < 2e-3
+    qc, kc, vc = cpu(q), cpu(k), cpu(v)
+    att_o = oblock.window_attention(qc, kc, vc, frames, tokens, cfg.radius, d ** -0.5, only_frames=sample)
+    att_o = oblock._bf16(oblock._bf16(att_o[rows]) * cpu(g3[:, :H])[rows][..., None])
+    assert _rel(cpu(att)[rows], att_o) < 5e-3                 # cuDNN (bf16 softmax) vs exact
+    al_o = _reference_alpha(block)(cpu(frame_mean))
+    assert _rel(cpu(alpha), al_o) < 1e-6
+    for hh in (0, 21, 39):                                    # the VDA branch, whole heads
+        sl = slice(hh, hh + 1)
+        ref = ovda.readout(qc[:, sl].numpy(), kc[:, sl].numpy(), vc[:, sl].numpy(),
+                           cpu(g3[:, H + hh:H + hh + 1]).numpy(), cpu(lgate).view(T, H, d)[:, sl].numpy(),
+                           cpu(alpha)[:, sl].numpy(), bounds, frames, tokens, out_frames=sample)
+        got = cpu(lin).view(T, H, d)[:, hh][rows].numpy()
+        assert float(np.linalg.norm(got - ref[rows.numpy()]) / np.linalg.norm(ref[rows.numpy()])) < 4e-3
+    o = oblock._bf16(oblock._bf16(oblock._qdq(cpu(att)[rows].reshape(-1, hd)) @ w["o"].T
+                                  + oblock._qdq(cpu(lin)[rows]) @ w["ol"].T) + w["o_b"])
+    x1_o = oblock._bf16(x[rows].float() + oblock._bf16(ada_g[2] * o))
+    assert _rel(cpu(x1)[rows], x1_o) < 1e-3
+    x1c = cpu(x1)[rows]
+    y2, _, _, _ = launch_prenorm_quantize(x1, block.norm2, cfg.eps, scale_mlp.view(1, hd),
+                                          shift_mlp.view(1, hd), idx, write_bf16=True)
+    y2_o = oblock.prenorm(x1c, w["norm2"], ada_g[4], ada_g[3], cfg.eps)
+    assert _rel(cpu(y2)[rows], y2_o) < 2e-3
+    up = oblock._linear(oblock._qdq(cpu(y2)[rows]), w["up"], w["up_b"])
+    down = oblock._linear(oblock._qdq(oblock._bf16(F.gelu(up, approximate=cfg.gelu))), w["down"], w["down_b"])
+    x2_o = oblock._bf16(x1c + oblock._bf16(ada_g[5] * down))
+    assert _rel(cpu(x2)[rows], x2_o) < 2e-3
+
+
+@torch.no_grad()
+def test_block_config3_end_to_end_sampled_frames(cuda, config3):
+    block, x, temb, out = config3
     sample = [0, 10, 20]                                      # both edges and the middle
-    ref = oblock.block_reference(x, temb, _weights(block), frames, tokens, cfg, _reference_alpha(block),
+    ref = oblock.block_reference(x, temb, _weights(block), 21, 1560, block.cfg, _reference_alpha(block),
                                  out_frames=sample)
-    got = _rows(out.cpu(), sample, tokens)
-    err = _rel(got.float(), ref)
-    assert err < 1e-2, err
+    err = _rel(_rows(out.cpu(), sample, 1560).float(), ref)
+    assert err < END_TO_END, err
 
 
 @torch.no_grad()
@@ -72,5 +178,5 @@ def test_stack_config4_shape_two_blocks_sampled_frames(cuda):
                                      text_rows=L, out_frames=sample)
         got = _rows(out.cpu(), sample, tokens, L)
         err = _rel(got.float(), ref)
-        assert err < 1e-2, (i, err)
+        assert err < END_TO_END, (i, err)
         x = out.cpu()                                         # block 2 takes block 1's output

@@ -274,3 +274,68 @@ def test_full_size_config2_properties(cuda):
                        bounds, f, s)
     got = out.view(n, h, d)[:, 7].float().cpu().numpy()
     assert rel_l2(got, ref.reshape(n, d)) < 4e-3
+
+
+# ------------------------------------------------------- tensor-core factor + scan
+@pytest.mark.parametrize("frames,heads,tokens,beta_scale", [(3, 2, 40, 1.0), (5, 3, 1008, 50.0)])
+def test_factor_inverse_planes_equal_factor_kernel(cuda, frames, heads, tokens, beta_scale):
+    """The split planes of vdn_vda_factor_inverse sum exactly to the fp32 inverse the
+    T / J factor kernel computes (the same Gauss-Jordan arithmetic), and that inverse
+    matches fp64."""
+    from vdn_b200.linear_attention import split_inverse_values, vda_factor_inverse
+    from vdn_b200.paper_factor import paper_delta_factors
+    A, B, _ = _stats_inputs(frames, heads, tokens, beta_scale, d=128)
+    planes = vda_factor_inverse(A.to(cuda))
+    inv = split_inverse_values(planes)
+    t, _ = paper_delta_factors(A.to(cuda), B.to(cuda), None)
+    assert torch.equal(inv, t)
+    ref, _ = _fp64_factors(A, B)
+    assert rel_l2(inv.double().cpu().numpy(), ref.numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("frames", [1, 2, 11, 31])
+@pytest.mark.parametrize("text", [False, True])
+@pytest.mark.parametrize("decay", [1.0, 0.7, 0.001])
+def test_scan_tc_vs_fp64(cuda, frames, text, decay):
+    """The tensor-core scan (three-way bf16 split products, fp32 accumulation) against
+    the fp64 recurrence on the same inverse: T = diag(alpha) inv^T, J = B inv^T (the MMA
+    reads the inverse's rows as the B operand), the reference's scan limits."""
+    from vdn_b200.linear_attention import split_inverse_values, vda_factor_inverse, vda_scan_tc
+    torch.manual_seed(frames)
+    h, d = 2, 128
+    k = F.normalize(torch.randn(frames, h, 9, d), dim=-1)
+    a = (k.transpose(-1, -2) @ k).contiguous()
+    b = torch.randn_like(a) * 0.1
+    alpha = (torch.rand(frames, h, d) * 0.1 + 0.9) * decay
+    planes = vda_factor_inverse(a.to(cuda))
+    inv = split_inverse_values(planes).double().cpu()
+    t = alpha.double()[..., :, None] * inv.transpose(-1, -2)
+    j = b.double() @ inv.transpose(-1, -2)
+    seed = torch.randn(h, d, d) * .3 if text else None
+    prefix, suffix = vda_scan_tc(planes, b.to(cuda), alpha.to(cuda), None if seed is None else seed.to(cuda))
+    op, osf = ovda.run_scans(t.numpy(), j.numpy(), None if seed is None else seed.double().numpy())
+    torch.testing.assert_close(prefix.double().cpu(), torch.from_numpy(op), atol=3e-6, rtol=3e-5)
+    torch.testing.assert_close(suffix.double().cpu(), torch.from_numpy(osf), atol=3e-6, rtol=3e-5)
+
+
+@pytest.mark.parametrize("heads", [1, 5, 40, 80])
+def test_scan_tc_head_counts_and_long_recurrence(cuda, heads):
+    """Every head count (one CTA per head and direction: 2 to 160 CTAs) and a long
+    recurrence near identity (102 frames at one head, reference test_paper_stack_vda_ops.py:300-323)."""
+    from vdn_b200.linear_attention import split_inverse_values, vda_factor_inverse, vda_scan_tc
+    frames = 102 if heads == 1 else 5
+    g = torch.Generator().manual_seed(heads)
+    k = torch.randn(frames, heads, 7, 128, generator=g) * (.025 if heads == 1 else .3)
+    a = (k.transpose(-1, -2) @ k).contiguous()
+    b = torch.randn(a.shape, generator=g) * (.01 if heads == 1 else .1)
+    alpha = torch.rand(frames, heads, 128, generator=g) * .01 + .99
+    seed = torch.randn(heads, 128, 128, generator=g) * .3
+    planes = vda_factor_inverse(a.to(cuda))
+    inv = split_inverse_values(planes).double().cpu()
+    t = alpha.double()[..., :, None] * inv.transpose(-1, -2)
+    j = b.double() @ inv.transpose(-1, -2)
+    prefix, suffix = vda_scan_tc(planes, b.to(cuda), alpha.to(cuda), seed.to(cuda))
+    op, osf = ovda.run_scans(t.numpy(), j.numpy(), seed.double().numpy())
+    tol = dict(atol=4e-6, rtol=1e-4) if heads == 1 else dict(atol=3e-6, rtol=3e-5)
+    torch.testing.assert_close(prefix.double().cpu(), torch.from_numpy(op), **tol)
+    torch.testing.assert_close(suffix.double().cpu(), torch.from_numpy(osf), **tol)

@@ -94,4 +94,23 @@ __device__ __forceinline__ uint4 pack_exact8(const float* v) {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
+// Exact three-way bf16 split of eight fp32 values: x = x1 + x2 + x3 with each part
+// the round-to-nearest bf16 of what the earlier parts leave (every subtraction is
+// exact in fp32, and the three 8-bit significands cover fp32's 24).  w[p] holds
+// part p of the eight values as packed bf16 pairs (element 2i in the low half).
+__device__ __forceinline__ void split3_bf16x8(const float* x, uint32_t (&w)[3][4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float a = x[2 * i], b = x[2 * i + 1];
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+      float ra = a, rb = b;
+      round_bf16_pair(ra, rb);
+      w[p][i] = pack_exact2(ra, rb);
+      a -= ra;
+      b -= rb;
+    }
+  }
+}
+
 }  // namespace vdn

@@ -158,7 +158,11 @@ __global__ void __launch_bounds__(256) stats_kernel(
 // applies the rank-1 update with one FMA per element, and the owners of row /
 // column p then overwrite those entries.  J = B inv reads B rows from global
 // (L2) and inv from shared memory.
-template <int D>
+// SPLIT (d = 128 only): instead of T and J, store inv = (I + A)^-1 as three bf16
+// planes whose sum is the fp32 value (x = x1 + x2 + x3 exactly), each plane in the
+// 128B-swizzled K-major operand layout of the tensor-core scan (two 64-column
+// halves of 128 rows x 128 B per plane, 96 KB per matrix at `Tout` bytes).
+template <int D, bool SPLIT = false>
 __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const float* B,
                                                         const float* __restrict__ alpha,
                                                         float* Tout, float* Jout) {
@@ -218,6 +222,28 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
         if (ty == o) m[jj][jj] = ip;
       }
     }
+  }
+  if constexpr (SPLIT) {
+    static_assert(D == 128, "split planes are laid out for d = 128");
+#pragma unroll
+    for (int i = 0; i < T; ++i)
+#pragma unroll
+      for (int j = 0; j < T; ++j) inv_s[(ty + 16 * i) * D + tx + 16 * j] = m[i][j];
+    __syncthreads();
+    uint8_t* planes = reinterpret_cast<uint8_t*>(Tout) + mat * (3 * 2 * D * D);
+    for (int q = threadIdx.x; q < D * (D / 8); q += blockDim.x) {
+      const int r = q / (D / 8), cc = q % (D / 8), kh = cc >> 3, c = cc & 7;
+      const float4 v0 = *reinterpret_cast<const float4*>(inv_s + r * D + cc * 8);
+      const float4 v1 = *reinterpret_cast<const float4*>(inv_s + r * D + cc * 8 + 4);
+      const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      uint32_t w[3][4];
+      split3_bf16x8(x, w);
+      const uint32_t off = kh * 16384 + r * 128 + ((c ^ (r & 7)) << 4);
+#pragma unroll
+      for (int p = 0; p < 3; ++p)
+        *reinterpret_cast<uint4*>(planes + p * 32768 + off) = make_uint4(w[p][0], w[p][1], w[p][2], w[p][3]);
+    }
+    return;
   }
   const float* al = alpha ? alpha + mat * D : nullptr;
   float* t_out = Tout + mat * D * D;
@@ -598,6 +624,23 @@ int launch_factors(const float* A, const float* B, const float* alpha, int64_t n
   return VDN_OK;
 }
 
+// Factor stage of the tensor-core scan: inv = (I + A)^-1 as three bf16 operand
+// planes (96 KB per matrix) for each of the n matrices of A (d = 128).
+int launch_factor_split(const float* A, int64_t n, void* planes, cudaStream_t stream) {
+  VDN_CHECK_ARG(n >= 0 && n < (1ll << 31), "bad matrix count");
+  if (n == 0) return VDN_OK;
+  VDN_CHECK_ARG(A && planes && aligned16(A) && aligned16(planes), "A and planes must be 16-byte aligned");
+  const size_t smem = (4 * 128 + 128 * 128) * sizeof(float);
+  if (int rc = set_smem(factor_kernel<128, true>, smem)) return rc;
+  factor_kernel<128, true><<<(unsigned)n, 256, smem, stream>>>(A, nullptr, nullptr, static_cast<float*>(planes),
+                                                              nullptr);
+  VDN_LAUNCH_CHECK("delta factors (split inverse)");
+  return VDN_OK;
+}
+
+int launch_scan_tc(const void* inv_planes, const float* B, const float* alpha, const float* seed, int F,
+                   int H, float* prefix, float* suffix, int* status, cudaStream_t stream);
+
 int launch_scan(const float* T, const float* J, const float* seed, int F, int H, int d,
                 float* prefix, float* suffix, cudaStream_t stream) {
   if (int rc = check_d(d)) return rc;
@@ -723,13 +766,61 @@ int vdn_vda_readout(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, con
                         S, H, d, out, stream);
 }
 
+// Workspace regions of vdn_vda_forward, each 256-byte aligned.  d = 128 (tensor-core
+// scan): A, then the forward bank over it (A is dead once the factors have read it),
+// B, the split inverses (three bf16 planes), the reverse bank, the gathered state
+// (bf16): 20 bytes per state element.  d = 64: A/T and B/J (the factors overwrite the
+// statistics), prefix, suffix, state: 18 bytes per state element.
+struct VdaWorkspace {
+  float* A;
+  float* B;
+  void* planes;
+  float* prefix;
+  float* suffix;
+  void* state;
+  size_t bytes;
+};
+
+static VdaWorkspace vda_workspace(void* base, int F, int H, int d) {
+  const size_t plane = (size_t)F * H * d * d;
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  char* ws = static_cast<char*>(base);
+  VdaWorkspace w{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = ws ? ws + off : nullptr;
+    off += up(bytes);
+    return p;
+  };
+  if (d == 128) {
+    w.A = reinterpret_cast<float*>(take(plane * 4));
+    w.prefix = w.A;
+    w.B = reinterpret_cast<float*>(take(plane * 4));
+    w.planes = take(plane * 6);
+    w.suffix = reinterpret_cast<float*>(take(plane * 4));
+  } else {
+    w.A = reinterpret_cast<float*>(take(plane * 4));
+    w.B = reinterpret_cast<float*>(take(plane * 4));
+    w.prefix = reinterpret_cast<float*>(take(plane * 4));
+    w.suffix = reinterpret_cast<float*>(take(plane * 4));
+  }
+  w.state = take(plane * 2);
+  w.bytes = off;
+  return w;
+}
+
+int vdn_vda_factor_inverse(const float* A, int64_t n, void* planes, cudaStream_t stream) {
+  return launch_factor_split(A, n, planes, stream);
+}
+
+int vdn_vda_scan_tc(const void* planes, const float* B, const float* alpha, const float* seed, int F, int H,
+                    float* prefix, float* suffix, int* status, cudaStream_t stream) {
+  return launch_scan_tc(planes, B, alpha, seed, F, H, prefix, suffix, status, stream);
+}
+
 size_t vdn_vda_workspace_size(int F, int S, int H, int d) {
   (void)S;
-  const size_t plane = (size_t)F * H * d * d;
-  // A/T and B/J (fp32, factors overwrite statistics in place), prefix, suffix
-  // (fp32) and the gathered state (bf16), each region 256-byte aligned.
-  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
-  return 4 * up(plane * 4) + up(plane * 2);
+  return vda_workspace(nullptr, F, H, d).bytes;
 }
 
 int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss, int64_t qkv_sh,
@@ -746,20 +837,21 @@ int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss,
   VDN_CHECK_ARG(aligned16(workspace), "workspace must be 16-byte aligned");
   FrameBounds fb;
   if (int rc = fill_bounds(bounds, F, &fb)) return rc;
-  const size_t plane = (size_t)F * H * d * d;
-  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
-  char* ws = static_cast<char*>(workspace);
-  float* A = reinterpret_cast<float*>(ws);
-  float* B = reinterpret_cast<float*>(ws + up(plane * 4));
-  float* prefix = reinterpret_cast<float*>(ws + 2 * up(plane * 4));
-  float* suffix = reinterpret_cast<float*>(ws + 3 * up(plane * 4));
-  void* state = ws + 4 * up(plane * 4);
+  const VdaWorkspace w = vda_workspace(workspace, F, H, d);
+  float *A = w.A, *B = w.B, *prefix = w.prefix, *suffix = w.suffix;
+  void* state = w.state;
   const int64_t sf = (int64_t)S * qkv_ss;
   if (int rc = launch_stats(k, sf, qkv_ss, qkv_sh, v, sf, qkv_ss, qkv_sh, beta, (int64_t)S * b_ss,
                             b_ss, b_sh, 0, F, S, H, d, A, B, stream))
     return rc;
-  if (int rc = launch_factors(A, B, alpha, (int64_t)F * H, d, A, B, stream)) return rc;
-  if (int rc = launch_scan(A, B, seed, F, H, d, prefix, suffix, stream)) return rc;
+  if (d == 128) {  // inverse only, then the tensor-core scan folds alpha and B into each step
+    VDN_CHECK_ARG(aligned16(alpha) && (!seed || aligned16(seed)), "alpha and seed must be 16-byte aligned");
+    if (int rc = launch_factor_split(A, (int64_t)F * H, w.planes, stream)) return rc;
+    if (int rc = launch_scan_tc(w.planes, B, alpha, seed, F, H, prefix, suffix, nullptr, stream)) return rc;
+  } else {
+    if (int rc = launch_factors(A, B, alpha, (int64_t)F * H, d, A, B, stream)) return rc;
+    if (int rc = launch_scan(A, B, seed, F, H, d, prefix, suffix, stream)) return rc;
+  }
   if (int rc = launch_gather(prefix, suffix, alpha, bounds, seed, bridge, F, H, d, state,
                              VDN_DTYPE_BF16, stream))
     return rc;

@@ -1,0 +1,229 @@
+// Bidirectional VDA scan on sm_100a tensor cores (d = 128).
+//
+// One CTA per (head, direction) carries the whole fp32 state through the F frames:
+//     P_f = (P_{f-1} diag(alpha_f) + B_f) (I + A_f)^-1
+// which is the reference recurrence s_t = s_{t-1} T_t + J_t with T = diag(alpha) inv
+// and J = B inv (scan.py:176-261, delta_rule.py:45-60) with the injection folded into
+// the step, so the factor stage only inverts.  Each step's product runs on tcgen05
+// (kind::f16, fp32 accumulator in TMEM) with both operands split into three bf16
+// parts (x = x1 + x2 + x3 exactly): the six products x_i inv_j with i + j <= 4 give
+// the fp32 result to within 2^-27 of each term, the accuracy of an fp32 GEMM.
+//
+// Roles (192 threads):
+//   warp 0 lane 0   bulk-copies the next frame's split inverse (96 KB, written in
+//                   the operand layout by the factor kernel) into shared memory
+//   warp 1          TMEM allocation; lane 0 issues the 48 MMAs of a step
+//   warps 2-5       one state row per thread (thread = TMEM lane): read P_{f-1}
+//                   from TMEM, store it to the frame's bank row, form
+//                   X_f = P_{f-1} alpha_f + B_f and write its three bf16 parts into
+//                   the A operand (128B-swizzled, K-major)
+// The copy of inverse f+1 lands while the rows of step f are formed.  Every wait
+// is bounded (2 s); a timeout aborts all roles, lets copies and MMAs in flight
+// finish, frees TMEM and reports VDN_ERR_TIMEOUT through `status`.
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace vdn {
+namespace vscan {
+
+using namespace sm100;
+
+constexpr int D = 128;
+constexpr int PLANE = D * D * 2;            // one bf16 part: 2 x (128 rows x 128 B) = 32 KB
+constexpr int OPER = 3 * PLANE;             // three parts = 96 KB
+constexpr int THREADS = 192;                // warp 0 producer, warp 1 MMA, warps 2-5 rows
+constexpr size_t SMEM = 1024 + 2 * OPER + 256;
+
+struct Params {
+  const uint8_t* inv;      // [F, H] split inverses, OPER bytes each
+  const float* B;          // [F, H, d, d] fp32 (B of the statistics)
+  const float* alpha;      // [F, H, d] fp32
+  const float* seed;       // [H, d, d] or null
+  float* prefix;           // [F, H, d, d] forward states
+  float* suffix;           // [F, H, d, d] reverse states
+  int F, H;
+  int* status;
+};
+
+// Byte offset of 16-byte chunk `c` (0..15 along K) of row `r` in a K-major
+// 128B-swizzled part (two 64-column halves of 16 KB).
+__device__ __forceinline__ uint32_t oper_off(uint32_t r, uint32_t c) {
+  return (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sX = smem;                        // A operand: X_f parts
+  uint8_t* sI = smem + OPER;                 // B operand: inv_f parts
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * OPER);
+  uint64_t* inv_full = bars;
+  uint64_t* inv_empty = bars + 1;
+  uint64_t* x_ready = bars + 2;
+  uint64_t* acc_full = bars + 3;
+  uint64_t* mma_drain = bars + 4;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.x >> 1, dir = blockIdx.x & 1;
+  const int F = p.F, H = p.H;
+  auto frame = [&](int step) { return dir == 0 ? step : F - 1 - step; };
+
+  if (tid == 0) {
+    mbar_init(inv_full, 1);
+    mbar_init(inv_empty, 1);
+    mbar_init(x_ready, 128);
+    mbar_init(acc_full, 1);
+    mbar_init(mma_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      int issued = 0;
+      for (int step = 0; step < F && !*abort_flag; ++step) {
+        if (!mbar_wait(inv_empty, (step & 1) ^ 1, abort_flag)) break;
+        const uint8_t* src = p.inv + ((int64_t)frame(step) * H + h) * OPER;
+        mbar_arrive_expect_tx(inv_full, OPER);
+#pragma unroll
+        for (int part = 0; part < 3; ++part) bulk_load(sI + part * PLANE, src + part * PLANE, PLANE, inv_full);
+        ++issued;
+      }
+      if (*abort_flag && issued) {  // the last copy must land before the CTA may exit
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(inv_full, (issued - 1) & 1) && globaltimer() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // --------------------------------------------------------------- MMA
+      constexpr uint32_t kIdesc = idesc_bf16(128, 128, 0, 0);
+      // Split products x_i inv_j kept: i + j <= 4 (parts counted from 1).
+      constexpr int kPairs[6][2] = {{0, 0}, {0, 1}, {1, 0}, {0, 2}, {1, 1}, {2, 0}};
+      bool issued = false;
+      for (int step = 0; step < F; ++step) {
+        if (!mbar_wait(x_ready, step & 1, abort_flag) || !mbar_wait(inv_full, step & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t xa = smem_u32(sX), ib = smem_u32(sI);
+#pragma unroll
+        for (int pr = 0; pr < 6; ++pr) {
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {  // 16 K per MMA: +32 B inside a 128-B row
+            const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
+            mma_bf16(tmem, desc_k_sw128(xa + kPairs[pr][0] * PLANE + koff),
+                     desc_k_sw128(ib + kPairs[pr][1] * PLANE + koff), kIdesc, (pr | ks) != 0);
+          }
+        }
+        issued = true;
+        tc_commit(inv_empty);
+        tc_commit(acc_full);
+      }
+      if (*abort_flag && issued) {
+        tc_commit(mma_drain);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(mma_drain, 0) && globaltimer() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------------- state rows
+    const int quad = warp & 3;                 // warps 2..5 -> TMEM lane quadrants 2, 3, 0, 1
+    const int row = quad * 32 + lane;
+    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16);
+    float* const banks = dir == 0 ? p.prefix : p.suffix;
+    uint32_t prev[D];                          // this row of the state, fp32 bits
+    if (p.seed) {
+      const uint4* s4 = reinterpret_cast<const uint4*>(p.seed + ((int64_t)h * D + row) * D);
+#pragma unroll
+      for (int i = 0; i < D / 4; ++i) {
+        const uint4 v = s4[i];
+        prev[4 * i] = v.x; prev[4 * i + 1] = v.y; prev[4 * i + 2] = v.z; prev[4 * i + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < D; ++i) prev[i] = 0u;
+    }
+    for (int step = 0; step <= F; ++step) {
+      if (step > 0) {
+        // P of the previous step: TMEM -> registers -> its bank row.  tcgen05.ld is
+        // warp-collective, so a warp proceeds only if none of its lanes gave up.
+        if (!__all_sync(0xffffffffu, mbar_wait(acc_full, (step - 1) & 1, abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(taddr + c * 32, prev + 32 * c);
+        tmem_ld_wait();
+        tc_fence_before();
+        uint4* dst = reinterpret_cast<uint4*>(banks + (((int64_t)frame(step - 1) * H + h) * D + row) * D);
+#pragma unroll
+        for (int i = 0; i < D / 4; ++i) dst[i] = make_uint4(prev[4 * i], prev[4 * i + 1], prev[4 * i + 2], prev[4 * i + 3]);
+      }
+      if (step == F) break;
+      // X = P diag(alpha_f) + B_f, split into three bf16 parts in the A operand.
+      const int fr = frame(step);
+      const float4* a4 = reinterpret_cast<const float4*>(p.alpha + ((int64_t)fr * H + h) * D);
+      const float4* b4 = reinterpret_cast<const float4*>(p.B + (((int64_t)fr * H + h) * D + row) * D);
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        const float4 al0 = __ldg(a4 + 2 * c), al1 = __ldg(a4 + 2 * c + 1);
+        const float4 b0 = b4[2 * c], b1 = b4[2 * c + 1];
+        const float x[8] = {fmaf(__uint_as_float(prev[8 * c]), al0.x, b0.x),
+                            fmaf(__uint_as_float(prev[8 * c + 1]), al0.y, b0.y),
+                            fmaf(__uint_as_float(prev[8 * c + 2]), al0.z, b0.z),
+                            fmaf(__uint_as_float(prev[8 * c + 3]), al0.w, b0.w),
+                            fmaf(__uint_as_float(prev[8 * c + 4]), al1.x, b1.x),
+                            fmaf(__uint_as_float(prev[8 * c + 5]), al1.y, b1.y),
+                            fmaf(__uint_as_float(prev[8 * c + 6]), al1.z, b1.z),
+                            fmaf(__uint_as_float(prev[8 * c + 7]), al1.w, b1.w)};
+        uint32_t w[3][4];
+        split3_bf16x8(x, w);
+        const uint32_t off = oper_off(row, c);
+#pragma unroll
+        for (int part = 0; part < 3; ++part)
+          *reinterpret_cast<uint4*>(sX + part * PLANE + off) = make_uint4(w[part][0], w[part][1], w[part][2], w[part][3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(x_ready);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, 128);
+  }
+  if (tid == 0 && *abort_flag && p.status) atomicExch(p.status, VDN_ERR_TIMEOUT);
+}
+
+}  // namespace vscan
+
+int launch_scan_tc(const void* inv_planes, const float* B, const float* alpha, const float* seed, int F,
+                   int H, float* prefix, float* suffix, int* status, cudaStream_t stream) {
+  using namespace vscan;
+  VDN_CHECK_ARG(F >= 1 && H >= 1, "positive F and H required");
+  VDN_CHECK_ARG(inv_planes && B && alpha && prefix && suffix, "null pointer");
+  VDN_CHECK_ARG(aligned16(inv_planes) && aligned16(B) && aligned16(alpha) && aligned16(prefix) &&
+                    aligned16(suffix) && (!seed || aligned16(seed)),
+                "scan operands must be 16-byte aligned");
+  static bool attr_set = false;
+  if (!attr_set) {
+    VDN_CUDA_TRY(cudaFuncSetAttribute(scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM));
+    attr_set = true;
+  }
+  Params p{static_cast<const uint8_t*>(inv_planes), B, alpha, seed, prefix, suffix, F, H, status};
+  scan_tc_kernel<<<2 * H, THREADS, SMEM, stream>>>(p);
+  VDN_LAUNCH_CHECK("vda scan (tcgen05)");
+  return VDN_OK;
+}
+
+}  // namespace vdn

@@ -176,6 +176,61 @@ def vda_scan(transitions, injections, seed=None):
     return prefix, suffix
 
 
+SPLIT_INVERSE_BYTES = 3 * 2 * 128 * 128   # three bf16 operand planes per 128 x 128 inverse
+
+
+def vda_factor_inverse(A):
+    """(I + A)^-1 of [..., 128, 128] fp32 matrices as three bf16 tensor-core operand
+    planes per matrix (uint8 [..., 98304]): the factor stage of the d = 128 forward."""
+    if A.dtype != torch.float32 or not A.is_cuda or A.shape[-2:] != (128, 128):
+        raise ValueError("A must be CUDA fp32 [..., 128, 128]")
+    _lib.require_device(A)
+    A = A.contiguous()
+    n = A.numel() // (128 * 128)
+    planes = torch.empty(*A.shape[:-2], SPLIT_INVERSE_BYTES, dtype=torch.uint8, device=A.device)
+    _lib.call("vdn_vda_factor_inverse", _lib.ptr(A), n, _lib.ptr(planes), _lib.stream_of(A.device))
+    return planes
+
+
+def split_inverse_values(planes):
+    """Decode the planes of vda_factor_inverse back to the fp32 matrices [..., 128, 128]
+    (un-swizzle the 16-byte chunks, sum the three bf16 parts: exact)."""
+    lead = planes.shape[:-1]
+    raw = planes.reshape(-1, 3, 2, 128, 8, 16).view(torch.int16)          # [n, part, half, row, chunk, 8]
+    rows = torch.arange(128, device=planes.device)
+    logical = torch.arange(8, device=planes.device)[None, :] ^ (rows[:, None] & 7)   # physical chunk
+    idx = logical[None, None, None, :, :, None].expand(raw.shape[0], 3, 2, 128, 8, 8)
+    ordered = torch.gather(raw, 4, idx)                                    # [n, part, half, row, chunk, 8]
+    vals = ordered.view(torch.bfloat16).float()
+    full = vals.permute(0, 1, 3, 2, 4, 5).reshape(-1, 3, 128, 128).sum(1)
+    return full.reshape(*lead, 128, 128)
+
+
+def vda_scan_tc(planes, B, alpha, seed=None):
+    """Forward / reverse banks [F, H, 128, 128] fp32 from split inverses [F, H, 98304],
+    B [F, H, 128, 128] and alpha [F, H, 128]: P_f = (P_{f-1} diag(alpha_f) + B_f) inv_f
+    on the tensor cores (the d = 128 scan of vda_forward)."""
+    f, h = B.shape[:2]
+    if B.shape != (f, h, 128, 128) or B.dtype != torch.float32 or planes.shape != (f, h, SPLIT_INVERSE_BYTES):
+        raise ValueError("B must be fp32 [F,H,128,128] and planes uint8 [F,H,98304]")
+    if alpha.shape != (f, h, 128):
+        raise ValueError("alpha must be [F,H,128]")
+    _lib.require_device(B)
+    if seed is not None:
+        seed = seed.float().contiguous()
+        if seed.shape != (h, 128, 128):
+            raise ValueError("seed must be fp32 [H,128,128]")
+    prefix = torch.empty_like(B)
+    suffix = torch.empty_like(B)
+    status = torch.zeros(1, dtype=torch.int32, device=B.device)
+    _lib.call("vdn_vda_scan_tc", _lib.ptr(planes.contiguous()), _lib.ptr(B.contiguous()),
+              _lib.ptr(alpha.float().contiguous()), _lib.ptr(seed), f, h, _lib.ptr(prefix), _lib.ptr(suffix),
+              _lib.ptr(status), _lib.stream_of(B.device))
+    if int(status.item()):
+        raise RuntimeError("VDA tensor-core scan wait timed out on the device")
+    return prefix, suffix
+
+
 def _bounds_buffer(bounds, frames):
     if len(bounds) != frames or frames < 1 or frames > MAX_FRAMES:
         raise ValueError(f"one bound per frame required (1..{MAX_FRAMES} frames)")

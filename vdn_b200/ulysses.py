@@ -493,6 +493,8 @@ def _ulysses_block_forward(self, x, temb, frames, tokens, runtime=None, text_row
     _ulysses_attention_forward / _branch_parallel_attention_forward, ulysses.py:271-598)."""
     from .block import HybridBlock
     rt = self._ulysses_runtime if runtime is None else runtime
+    if rt is not None and rt.world_size == 1:
+        rt = None                         # one rank: the unsharded block, no collectives
     return HybridBlock.forward(self, x, temb, frames, tokens, rt, text_rows=text_rows)
 
 
