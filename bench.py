@@ -563,19 +563,17 @@ def bench_block(args, torch, dist, rank, world):
             out_host[0].copy_(y, non_blocking=True)
 
         e2e_ms = time_steps(torch, e2e_step, e2e_steps, 1, dist, stream) / e2e_steps
-    elif world == 1:
+    else:
+        # Two captured forwards alternate; each batch's host-to-device and device-to-host
+        # copies run on the copy engines while the neighbouring batches compute (under
+        # Ulysses every rank streams its own rows; the graphs share the peer exchange,
+        # whose replays are serialised on the compute stream).
         from vdn_b200.block import BlockPipeline
         pipe = BlockPipeline(block, rows, temb, F, S, runtime)
         ins = [x_host[i & 1] for i in range(e2e_steps)]
         outs = [out_host[i & 1] for i in range(e2e_steps)]
         e2e_ms = time_steps(torch, lambda: pipe.run(ins, outs), 1, 1, dist, stream) / e2e_steps
         del pipe
-    else:  # Ulysses ranks: the captured forward with its copies in order
-        def e2e_step():
-            graph.x.copy_(x_host[0], non_blocking=True)
-            out_host[0].copy_(graph.replay(), non_blocking=True)
-
-        e2e_ms = time_steps(torch, e2e_step, e2e_steps, 1, dist, stream) / e2e_steps
     rec = {
         "metric": "hybrid-block tokens/s (BASELINE config 3, 32760 tokens)",
         "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -591,7 +589,7 @@ def bench_block(args, torch, dist, rank, world):
         "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": x_host[0].numel() * 2, "d2h_bytes_per_step": out_host[0].numel() * 2,
                 "steps": e2e_steps, "copies": "per step; overlapped with neighbouring steps"
-                if not args.eager and world == 1 else "per step; serial"},
+                if not args.eager else "per step; serial"},
         "gpu_launches": block.launches_per_forward(world, runtime) * args.steps,
         "launch": "eager" if args.eager else "cuda_graph",
         "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (QKV, %d x 15360 x 5120)" % rows,

@@ -341,7 +341,7 @@ int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss,
  * take cudaMalloc's device synchronisation).  Same kernels and results as
  * vdn_vda_forward; the scratch is a 64 MiB array built into the library.
  * Geometries whose vdn_vda_workspace_size exceeds 64 MiB return VDN_ERR_VALUE
- * (at d = 128: 22 frames x 10 heads fit, 23 x 10 do not).  The first call on a
+ * (at d = 128: 20 frames x 10 heads fit, 21 x 10 do not).  The first call on a
  * device looks the array's address up; under CUDA's lazy module loading that is
  * also when the device reserves the 64 MiB (kept until the process exits) and
  * it may synchronise the device, so make one warm-up call outside latency-

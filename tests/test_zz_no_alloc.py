@@ -10,8 +10,8 @@ row (with different inputs, so stale scratch contents would show) give exactly
 the output of the regular workspace entry point, vdn_vda_forward (the two run
 the same deterministic kernels, so the results are bit-identical), that the
 second call leaves the device's free memory unchanged (it allocates nothing),
-and that the size limit sits exactly where the 64 MiB scratch runs out: 22
-frames x 10 heads at d = 128 are accepted, 23 x 10 are rejected with a clear
+and that the size limit sits exactly where the 64 MiB scratch runs out: 20
+frames x 10 heads at d = 128 are accepted, 21 x 10 are rejected with a clear
 error.
 
 The file is named so that pytest collects it last.
@@ -80,7 +80,7 @@ def test_noalloc_matches_workspace_entry_point_twice():
 
 
 @torch.no_grad()
-@pytest.mark.parametrize("frames,accepted", [(22, True), (23, False)])
+@pytest.mark.parametrize("frames,accepted", [(20, True), (21, False)])
 def test_noalloc_size_limit(frames, accepted):
     from vdn_b200 import _lib
     dev = torch.device("cuda", 0)

@@ -490,7 +490,7 @@ constexpr int P_A_BYTES = 2 * P_SUB;  // 32 KB
 constexpr int P_B_BYTES = 2 * P_SUB;  // 32 KB
 constexpr int P_SF_STAGE = 512 * 6;   // SFA: 2 K-atoms; SFB: 2 N-halves x 2 K-atoms
 constexpr int P_SF_COLS = 24;         // TMEM scale columns per stage
-constexpr int P_GROUP_M = 8;         // 256-row tiles per group
+constexpr int P_GROUP_M = 16;        // 256-row tiles per group (4096 rows: measured best of 4 / 8 / 16 / 32)
 constexpr size_t P_SMEM_BYTES =
     1024 + P_STAGES * (P_A_BYTES + P_B_BYTES + P_SF_STAGE) + BAR_BYTES + 8 * STAGE_BYTES;
 static_assert(P_SMEM_BYTES <= 232448, "shared memory per CTA");

@@ -176,13 +176,16 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const float* a_in = A + mat * D * D;
   const float* b_in = B + mat * D * D;
-  float m[T][T];
+  // Thread's T x T register tile, column pairs packed for the paired FMA (fma.rn.f32x2):
+  // element (i, j) is component j & 1 of m2[i][j / 2].
+  float2 m2[T][T / 2];
+#define MV(i, j) ((((j) & 1) ? m2[i][(j) >> 1].y : m2[i][(j) >> 1].x))
 #pragma unroll
   for (int i = 0; i < T; ++i)
 #pragma unroll
     for (int j = 0; j < T; ++j) {
       const int r = ty + 16 * i, c = tx + 16 * j;
-      m[i][j] = a_in[r * D + c] + (r == c ? 1.0f : 0.0f);
+      MV(i, j) = a_in[r * D + c] + (r == c ? 1.0f : 0.0f);
     }
   // Pivot p = o + 16 jj lives in row slot jj of threads ty == o and column slot
   // jj of threads tx == o: the slot is a compile-time index (m stays in registers).
@@ -194,12 +197,12 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
       float* cb = colbuf + (p & 1) * D;
       if (ty == o) {
 #pragma unroll
-        for (int j = 0; j < T; ++j) rb[tx + 16 * j] = m[jj][j];
-        if (tx == o) piv[p & 1] = __fdiv_rn(1.0f, m[jj][jj]);
+        for (int j = 0; j < T; ++j) rb[tx + 16 * j] = MV(jj, j);
+        if (tx == o) piv[p & 1] = __fdiv_rn(1.0f, MV(jj, jj));
       }
       if (tx == o) {
 #pragma unroll
-        for (int i = 0; i < T; ++i) cb[ty + 16 * i] = m[i][jj];
+        for (int i = 0; i < T; ++i) cb[ty + 16 * i] = MV(i, jj);
       }
       __syncthreads();
       const float ip = piv[p & 1];
@@ -209,17 +212,20 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
 #pragma unroll
       for (int i = 0; i < T; ++i) pcol[i] = cb[ty + 16 * i];
 #pragma unroll
-      for (int i = 0; i < T; ++i)
+      for (int i = 0; i < T; ++i) {
+        const float2 c2 = make_float2(-pcol[i], -pcol[i]);
 #pragma unroll
-        for (int j = 0; j < T; ++j) m[i][j] = fmaf(-pcol[i], prow[j], m[i][j]);
+        for (int jp = 0; jp < T / 2; ++jp)
+          m2[i][jp] = __ffma2_rn(c2, make_float2(prow[2 * jp], prow[2 * jp + 1]), m2[i][jp]);
+      }
       if (ty == o) {
 #pragma unroll
-        for (int j = 0; j < T; ++j) m[jj][j] = prow[j];
+        for (int j = 0; j < T; ++j) MV(jj, j) = prow[j];
       }
       if (tx == o) {
 #pragma unroll
-        for (int i = 0; i < T; ++i) m[i][jj] = -pcol[i] * ip;
-        if (ty == o) m[jj][jj] = ip;
+        for (int i = 0; i < T; ++i) MV(i, jj) = -pcol[i] * ip;
+        if (ty == o) MV(jj, jj) = ip;
       }
     }
   }
@@ -228,7 +234,7 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
 #pragma unroll
     for (int i = 0; i < T; ++i)
 #pragma unroll
-      for (int j = 0; j < T; ++j) inv_s[(ty + 16 * i) * D + tx + 16 * j] = m[i][j];
+      for (int j = 0; j < T; ++j) inv_s[(ty + 16 * i) * D + tx + 16 * j] = MV(i, j);
     __syncthreads();
     uint8_t* planes = reinterpret_cast<uint8_t*>(Tout) + mat * (3 * 2 * D * D);
     for (int q = threadIdx.x; q < D * (D / 8); q += blockDim.x) {
@@ -253,8 +259,8 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
 #pragma unroll
     for (int j = 0; j < T; ++j) {
       const int r = ty + 16 * i, c = tx + 16 * j;
-      inv_s[r * D + c] = m[i][j];
-      t_out[r * D + c] = al ? al[r] * m[i][j] : m[i][j];
+      inv_s[r * D + c] = MV(i, j);
+      t_out[r * D + c] = al ? al[r] * MV(i, j) : MV(i, j);
     }
   __syncthreads();
   // J = B inv
@@ -287,6 +293,7 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
 #pragma unroll
     for (int j = 0; j < T; ++j) j_out[(ty + 16 * i) * D + tx + 16 * j] = acc[i][j];
 }
+#undef MV
 
 // ----------------------------------------------------------------------- scan
 // grid (H, 2 directions, D/R row blocks); 256 threads in a 16 x 16 grid.  Rows of

@@ -12,8 +12,8 @@
 // Limits and rules:
 //  * The array holds kScratchBytes = 64 MiB.  A geometry whose
 //    vdn_vda_workspace_size exceeds it is rejected with VDN_ERR_VALUE before
-//    anything is launched; at d = 128 and 10 heads that is 23 frames or more
-//    (22 frames x 10 heads needs 64,880,640 bytes and is accepted).
+//    anything is launched; at d = 128 and 10 heads that is 21 frames or more
+//    (20 frames x 10 heads needs 65,536,000 bytes and is accepted).
 //  * Host code cannot use the array's name as a device address.  The first call
 //    on each device (with that device current) looks the address up with
 //    cudaGetSymbolAddress.  With CUDA's lazy module loading that first lookup is

@@ -9,14 +9,17 @@
 // parts (x = x1 + x2 + x3 exactly): the six products x_i inv_j with i + j <= 4 give
 // the fp32 result to within 2^-27 of each term, the accuracy of an fp32 GEMM.
 //
-// Roles (192 threads):
+// Roles (576 threads):
 //   warp 0 lane 0   bulk-copies the next frame's split inverse (96 KB, written in
 //                   the operand layout by the factor kernel) into shared memory
-//   warp 1          TMEM allocation; lane 0 issues the 48 MMAs of a step
-//   warps 2-5       one state row per thread (thread = TMEM lane): read P_{f-1}
-//                   from TMEM, store it to the frame's bank row, form
-//                   X_f = P_{f-1} alpha_f + B_f and write its three bf16 parts into
-//                   the A operand (128B-swizzled, K-major)
+//   warp 1          TMEM allocation; lane 0 issues the 48 MMAs of a step (each
+//                   64-deep K half into its own 128 columns)
+//   warps 2-17      a quarter row of the state per thread (thread = TMEM lane x 32
+//                   columns): read P_{f-1} from TMEM, store it to the frame's bank
+//                   row, form X_f = P_{f-1} alpha_f + B_f (alpha of the chain staged
+//                   in shared memory at the start, B requested before the wait for
+//                   the product) and write its three bf16 parts into the A operand
+//                   (128B-swizzled, K-major)
 // The copy of inverse f+1 lands while the rows of step f are formed.  Every wait
 // is bounded (2 s); a timeout aborts all roles, lets copies and MMAs in flight
 // finish, frees TMEM and reports VDN_ERR_TIMEOUT through `status`.
@@ -31,8 +34,10 @@ using namespace sm100;
 constexpr int D = 128;
 constexpr int PLANE = D * D * 2;            // one bf16 part: 2 x (128 rows x 128 B) = 32 KB
 constexpr int OPER = 3 * PLANE;             // three parts = 96 KB
-constexpr int THREADS = 192;                // warp 0 producer, warp 1 MMA, warps 2-5 rows
-constexpr size_t SMEM = 1024 + 2 * OPER + 256;
+constexpr int ROW_WARPS = 16;               // four warps per TMEM lane quadrant (column quarters)
+constexpr int THREADS = 64 + 32 * ROW_WARPS;  // warp 0 producer, warp 1 MMA, warps 2-17 rows
+constexpr int ALPHA_FRAMES = 64;            // alpha of up to this many frames staged in shared memory
+constexpr size_t SMEM = 1024 + 2 * OPER + ALPHA_FRAMES * D * 4 + 256;
 
 struct Params {
   const uint8_t* inv;      // [F, H] split inverses, OPER bytes each
@@ -56,7 +61,8 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sX = smem;                        // A operand: X_f parts
   uint8_t* sI = smem + OPER;                 // B operand: inv_f parts
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * OPER);
+  float* sAlpha = reinterpret_cast<float*>(smem + 2 * OPER);   // [F][D] when F <= ALPHA_FRAMES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * OPER + ALPHA_FRAMES * D * 4);
   uint64_t* inv_full = bars;
   uint64_t* inv_empty = bars + 1;
   uint64_t* x_ready = bars + 2;
@@ -73,13 +79,18 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
   if (tid == 0) {
     mbar_init(inv_full, 1);
     mbar_init(inv_empty, 1);
-    mbar_init(x_ready, 128);
+    mbar_init(x_ready, 32 * ROW_WARPS);
     mbar_init(acc_full, 1);
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_holder, 128);
+  const bool alpha_smem = F <= ALPHA_FRAMES;
+  if (alpha_smem)
+    for (int i = tid; i < F * D / 4; i += THREADS)
+      reinterpret_cast<float4*>(sAlpha)[i] =
+          __ldg(reinterpret_cast<const float4*>(p.alpha + ((int64_t)(i / (D / 4)) * H + h) * D) + i % (D / 4));
+  if (warp == 1) tmem_alloc(tmem_holder, 256);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -95,6 +106,9 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
         mbar_arrive_expect_tx(inv_full, OPER);
 #pragma unroll
         for (int part = 0; part < 3; ++part) bulk_load(sI + part * PLANE, src + part * PLANE, PLANE, inv_full);
+        // The next frame's inverse moves into L2 during this step, so its copy into
+        // shared memory (which has to wait for this step's MMAs) reads from L2.
+        if (step + 1 < F) bulk_prefetch_l2(p.inv + ((int64_t)frame(step + 1) * H + h) * OPER, OPER);
         ++issued;
       }
       if (*abort_flag && issued) {  // the last copy must land before the CTA may exit
@@ -107,20 +121,26 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
     if (lane == 0) {
       // --------------------------------------------------------------- MMA
       constexpr uint32_t kIdesc = idesc_bf16(128, 128, 0, 0);
-      // Split products x_i inv_j kept: i + j <= 4 (parts counted from 1).
-      constexpr int kPairs[6][2] = {{0, 0}, {0, 1}, {1, 0}, {0, 2}, {1, 1}, {2, 0}};
+      // Split products x_i inv_j kept: i + j <= 4 (parts counted from 1), smallest
+      // first.  Each 64-deep K half accumulates into its own TMEM columns (the
+      // epilogue adds the two in fp32): shorter accumulation chains keep the tensor
+      // core's fp32 sums at the accuracy of an FMA chain.
+      constexpr int kPairs[6][2] = {{2, 0}, {1, 1}, {0, 2}, {1, 0}, {0, 1}, {0, 0}};
       bool issued = false;
       for (int step = 0; step < F; ++step) {
         if (!mbar_wait(x_ready, step & 1, abort_flag) || !mbar_wait(inv_full, step & 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t xa = smem_u32(sX), ib = smem_u32(sI);
 #pragma unroll
-        for (int pr = 0; pr < 6; ++pr) {
+        for (int kh = 0; kh < 2; ++kh) {
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {  // 16 K per MMA: +32 B inside a 128-B row
-            const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
-            mma_bf16(tmem, desc_k_sw128(xa + kPairs[pr][0] * PLANE + koff),
-                     desc_k_sw128(ib + kPairs[pr][1] * PLANE + koff), kIdesc, (pr | ks) != 0);
+          for (int pr = 0; pr < 6; ++pr) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {  // 16 K per MMA: +32 B inside a 128-B row
+              const uint32_t koff = kh * 16384 + ks * 32;
+              mma_bf16(tmem + kh * 128, desc_k_sw128(xa + kPairs[pr][0] * PLANE + koff),
+                       desc_k_sw128(ib + kPairs[pr][1] * PLANE + koff), kIdesc, (pr | ks) != 0);
+            }
           }
         }
         issued = true;
@@ -136,45 +156,61 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
     }
   } else {
     // -------------------------------------------------------- state rows
-    const int quad = warp & 3;                 // warps 2..5 -> TMEM lane quadrants 2, 3, 0, 1
+    // Thread = (state row, column quarter): warps 2-17 cover lane quadrant warp % 4
+    // (the lanes a warp may read) and column quarter (warp - 2) / 4.  Each thread's
+    // whole slice of the B row is requested at the start of the step, before the
+    // wait for the previous product: all of its loads are in flight at once.
+    constexpr int QC = D / 4;                  // columns per thread
+    const int quad = warp & 3;
+    const int quarter = (warp - 2) >> 2;
     const int row = quad * 32 + lane;
-    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16);
+    const int col0 = quarter * QC;
+    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + col0;
     float* const banks = dir == 0 ? p.prefix : p.suffix;
-    uint32_t prev[D];                          // this row of the state, fp32 bits
+    uint32_t prev[QC];                         // this quarter row of the state, fp32 bits
     if (p.seed) {
-      const uint4* s4 = reinterpret_cast<const uint4*>(p.seed + ((int64_t)h * D + row) * D);
+      const uint4* s4 = reinterpret_cast<const uint4*>(p.seed + ((int64_t)h * D + row) * D + col0);
 #pragma unroll
-      for (int i = 0; i < D / 4; ++i) {
+      for (int i = 0; i < QC / 4; ++i) {
         const uint4 v = s4[i];
         prev[4 * i] = v.x; prev[4 * i + 1] = v.y; prev[4 * i + 2] = v.z; prev[4 * i + 3] = v.w;
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < D; ++i) prev[i] = 0u;
+      for (int i = 0; i < QC; ++i) prev[i] = 0u;
     }
     for (int step = 0; step <= F; ++step) {
+      const int fr = frame(step < F ? step : F - 1);
+      float4 bq[QC / 4];
+      if (step < F) {
+        const float4* b4 = reinterpret_cast<const float4*>(p.B + (((int64_t)fr * H + h) * D + row) * D + col0);
+#pragma unroll
+        for (int i = 0; i < QC / 4; ++i) bq[i] = b4[i];
+      }
       if (step > 0) {
         // P of the previous step: TMEM -> registers -> its bank row.  tcgen05.ld is
         // warp-collective, so a warp proceeds only if none of its lanes gave up.
         if (!__all_sync(0xffffffffu, mbar_wait(acc_full, (step - 1) & 1, abort_flag))) break;
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(taddr + c * 32, prev + 32 * c);
+        uint32_t hi[QC];
+        tmem_ld_32x32b_x32(taddr, prev);
+        tmem_ld_32x32b_x32(taddr + 128, hi);
         tmem_ld_wait();
         tc_fence_before();
-        uint4* dst = reinterpret_cast<uint4*>(banks + (((int64_t)frame(step - 1) * H + h) * D + row) * D);
 #pragma unroll
-        for (int i = 0; i < D / 4; ++i) dst[i] = make_uint4(prev[4 * i], prev[4 * i + 1], prev[4 * i + 2], prev[4 * i + 3]);
+        for (int i = 0; i < QC; ++i) prev[i] = __float_as_uint(__uint_as_float(prev[i]) + __uint_as_float(hi[i]));
+        uint4* dst = reinterpret_cast<uint4*>(banks + (((int64_t)frame(step - 1) * H + h) * D + row) * D + col0);
+#pragma unroll
+        for (int i = 0; i < QC / 4; ++i) dst[i] = make_uint4(prev[4 * i], prev[4 * i + 1], prev[4 * i + 2], prev[4 * i + 3]);
       }
       if (step == F) break;
       // X = P diag(alpha_f) + B_f, split into three bf16 parts in the A operand.
-      const int fr = frame(step);
-      const float4* a4 = reinterpret_cast<const float4*>(p.alpha + ((int64_t)fr * H + h) * D);
-      const float4* b4 = reinterpret_cast<const float4*>(p.B + (((int64_t)fr * H + h) * D + row) * D);
+      const float* al = alpha_smem ? sAlpha + fr * D + col0 : p.alpha + ((int64_t)fr * H + h) * D + col0;
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        const float4 al0 = __ldg(a4 + 2 * c), al1 = __ldg(a4 + 2 * c + 1);
-        const float4 b0 = b4[2 * c], b1 = b4[2 * c + 1];
+      for (int c = 0; c < QC / 8; ++c) {
+        const float4 al0 = *reinterpret_cast<const float4*>(al + 8 * c);
+        const float4 al1 = *reinterpret_cast<const float4*>(al + 8 * c + 4);
+        const float4 b0 = bq[2 * c], b1 = bq[2 * c + 1];
         const float x[8] = {fmaf(__uint_as_float(prev[8 * c]), al0.x, b0.x),
                             fmaf(__uint_as_float(prev[8 * c + 1]), al0.y, b0.y),
                             fmaf(__uint_as_float(prev[8 * c + 2]), al0.z, b0.z),
@@ -185,7 +221,7 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
                             fmaf(__uint_as_float(prev[8 * c + 7]), al1.w, b1.w)};
         uint32_t w[3][4];
         split3_bf16x8(x, w);
-        const uint32_t off = oper_off(row, c);
+        const uint32_t off = oper_off(row, quarter * (QC / 8) + c);
 #pragma unroll
         for (int part = 0; part < 3; ++part)
           *reinterpret_cast<uint4*>(sX + part * PLANE + off) = make_uint4(w[part][0], w[part][1], w[part][2], w[part][3]);
@@ -200,7 +236,7 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
   if (tid == 0 && *abort_flag && p.status) atomicExch(p.status, VDN_ERR_TIMEOUT);
 }

@@ -209,15 +209,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         return s < p.S ? bf16_bits_to_f32(p.beta[(int64_t)f * p.b_sf + (int64_t)s * p.b_ss + (int64_t)h * p.b_sh])
                        : 0.f;
       };
-      float bt_next = load_beta(0);
-      bool ok = true;
-      for (int c = 0; c < nch; ++c, ++g) {
+      // One chunk: features, beta and the khi / klo split, in place in its stage.
+      // Returns false when a wait gave up.
+      auto chunk = [&](float bt) -> bool {
         const int s = g % ST_STAGES;
-        const float bt = bt_next;
-        if (c + 1 < nch) bt_next = load_beta(c + 1);
         if (!mbar_wait(&full[s], (g / ST_STAGES) & 1, abort_flag)) {
-          ok = false;
-          break;
+          return false;
         }
         uint8_t* st = stages + s * ST_STAGE_BYTES;
         const uint32_t off = r * ST_REGION + swz(row, cc);
@@ -268,6 +265,31 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         *reinterpret_cast<uint4*>(st + 6 * ST_REGION + off) = make_uint4(lo2[0], lo2[1], lo2[2], lo2[3]);
         fence_proxy_async_smem();
         mbar_arrive(&ready[s]);
+        ++g;
+        return true;
+      };
+      // beta of the next four chunks stays in four registers (each refilled four
+      // chunks ahead), so its global load latency hides behind four chunks of work
+      // (with one chunk of lead the load latency bounded the chunk rate).
+      float bq0 = load_beta(0), bq1 = nch > 1 ? load_beta(1) : 0.f;
+      float bq2 = nch > 2 ? load_beta(2) : 0.f, bq3 = nch > 3 ? load_beta(3) : 0.f;
+      bool ok = true;
+      for (int c = 0; c < nch && ok; c += 4) {
+        float bt = bq0;
+        if (c + 4 < nch) bq0 = load_beta(c + 4);
+        ok = chunk(bt);
+        if (!ok || c + 1 >= nch) break;
+        bt = bq1;
+        if (c + 5 < nch) bq1 = load_beta(c + 5);
+        ok = chunk(bt);
+        if (!ok || c + 2 >= nch) break;
+        bt = bq2;
+        if (c + 6 < nch) bq2 = load_beta(c + 6);
+        ok = chunk(bt);
+        if (!ok || c + 3 >= nch) break;
+        bt = bq3;
+        if (c + 7 < nch) bq3 = load_beta(c + 7);
+        ok = chunk(bt);
       }
       if (!ok) break;
     }
