@@ -607,6 +607,8 @@ def bench_block(args, torch, dist, rank, world):
     if world > 1:
         rec["parity"] = block_parity(torch, dist, block, step, x_full, temb, F, S, lo, hi)
         del x_full
+        if runtime.exchange_mode == "peer" and not runtime.branch_parallel:
+            rec["phases"] = block_phases(torch, dist, block, x, temb, F, S, runtime)
     elif not args.no_sub:
         rec.update(sub_records(args, torch))
     if runtime is not None:
@@ -635,6 +637,41 @@ def block_parity(torch, dist, block, step, x_full, temb, F, S, lo, hi, tol=2e-3)
     rel, mx = float(t[0]), float(t[1])
     return {"rel_l2_max": rel, "max_abs": mx, "tol_rel_l2": tol, "ok": bool(rel < tol),
             "reference": "unsharded block on each rank (same seeded weights and input)"}
+
+
+PEER_PHASES = ("adaln_prenorm", "gates_and_side_rows", "qkv_gemm_scatter", "fence_heads", "window_softmax",
+               "softmax_quantize_scatter", "vda_branch", "vda_quantize_scatter", "fence_rows", "out_gemm", "ffn")
+
+
+def block_phases(torch, dist, block, x, temb, F, S, runtime):
+    """One eager forward with CUDA events around the phases of the peer-exchange block
+    (the softmax phases on the caller's stream, the VDA phases on the side stream,
+    which overlap them), max over ranks; plus the bytes each rank moves over NVLink."""
+    runtime.reset_profile()
+    runtime.profile_enabled = True
+    block(x, temb, F, S, runtime)
+    ms = runtime.profile_milliseconds()
+    runtime.profile_enabled = False
+    runtime.reset_profile()
+    t = torch.tensor([ms.get(k, 0.0) for k in PEER_PHASES], device=x.device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    P, T = runtime.world_size, F * S
+    cfg = block.cfg
+    hd, H, d = cfg.hidden, cfg.heads, cfg.head_dim
+    rows = runtime.local_end - runtime.local_start
+    r = block.output_gate.down.weight.shape[0]
+    remote = (P - 1) / P
+    out_bytes = {  # bytes this rank stores into other ranks' memory per block
+        "qkv_scatter": int(rows * 3 * hd * 2 * remote),
+        "side_rows_and_frame_sums": int((rows * (2 * H + r) * 2 + F * hd * 4) * (P - 1)),
+        "results_mxfp8_scatter": int(2 * T * (H // P) * d * (1 + 1 / 32) * remote),
+    }
+    phases = {k: round(float(v), 4) for k, v in zip(PEER_PHASES, t.tolist())}
+    ret_ms = phases["softmax_quantize_scatter"] + phases["vda_quantize_scatter"]
+    return {"ms_max_over_ranks": phases, "launch": "eager, one forward after the timed region",
+            "nvlink_bytes_out_per_rank": out_bytes,
+            "result_scatter_gbs": round(out_bytes["results_mxfp8_scatter"] / (ret_ms * 1e-3) / 1e9, 1)
+            if ret_ms > 0 else None}
 
 
 def sub_records(args, torch):

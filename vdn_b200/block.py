@@ -251,10 +251,13 @@ class HybridBlock(nn.Module):
             if rows != text_rows + T:
                 raise ValueError("x must hold text_rows + frames * tokens rows")
             return self._forward_general(x, temb, frames, tokens, text_rows)
+        ev = runtime.profile_start() if runtime is not None else None
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self._adaln(temb)
         idx = torch.zeros(rows, dtype=torch.int64, device=dev)
         y1, q1, s1, _ = launch_prenorm_quantize(x, self.norm1, cfg.eps, scale_msa.view(1, hd),
                                                 shift_msa.view(1, hd), idx, write_bf16=True)
+        if runtime is not None:
+            runtime.profile_end("adaln_prenorm", ev)
         if runtime is not None and runtime.world_size > 1 and runtime.branch_parallel:
             qkv = torch.empty(rows, 3 * hd, device=dev, dtype=torch.bfloat16)
             self._gemm(q1, s1, self.qkv, rows, qkv, bias=self.qkv.bias)
@@ -262,6 +265,15 @@ class HybridBlock(nn.Module):
                                                             tokens, runtime)
         elif runtime is not None and runtime.world_size > 1 and runtime.exchange_mode == "peer":
             first, second = self._attention_peer(y1, q1, s1, frames, tokens, runtime)
+            ev = runtime.profile_start()
+            x1 = torch.empty_like(x)
+            self._gemm(first[0], first[1], self.o, rows, x1, second=(second, self.ol),
+                       bias=self.o_bias, resid=x, gate=gate_msa.contiguous())
+            runtime.profile_end("out_gemm", ev)
+            ev = runtime.profile_start()
+            x2 = self._ffn(x1, shift_mlp, scale_mlp, gate_mlp, idx)
+            runtime.profile_end("ffn", ev)
+            return x2
         else:
             qkv = torch.empty(rows, 3 * hd, device=dev, dtype=torch.bfloat16)
             self._gemm(q1, s1, self.qkv, rows, qkv, bias=self.qkv.bias)
@@ -560,16 +572,22 @@ class HybridBlock(nn.Module):
         ex = rt.exchange(H, d, frames, 2 * H + r)
         hl, h0 = ex.hl, ex.head0
         # Side inputs into this rank's slot of every rank's buffers (copy engines).
+        ev = rt.profile_start()
         rt.local_frame_sums(y1, frames, tokens, out=ex.sums()[rt.rank])
         ex.publish_sums()
         self._gate_projections(y1, out=ex.local_rows())                  # [rows, 2H + r]
         ex.publish_rows()
+        rt.profile_end("gates_and_side_rows", ev)
+        ev = rt.profile_start()
         w = self.qkv
         _lib.call("vdn_mxfp8_gemm_scatter", _lib.ptr(q1), _lib.ptr(s1), _lib.ptr(w.q), _lib.ptr(w.s),
                   w.k_pad, _lib.ptr(w.bias), q1.shape[0], w.n, w.n_pad, y1.shape[0],
                   _lib.ptr(ex.chunk_dst), ex.dst_ld, rt.local_start, _lib.ptr(self._status),
                   _lib.stream_of(y1.device))
+        rt.profile_end("qkv_gemm_scatter", ev)
+        ev = rt.profile_start()
         ex.fence()
+        rt.profile_end("fence_heads", ev)
         gathered = ex.rows()                                              # [T, 2H + r]
         frame_mean = ex.sums().sum(0) / tokens                            # fixed rank order
         recv = ex.qkv()                                                   # [T, hl, 3d]
@@ -579,18 +597,28 @@ class HybridBlock(nn.Module):
         bounds = window_bounds(frames, cfg.radius)
 
         def branch():  # VDA and its return scatter, on the side stream
+            ev = rt.profile_start()
             alpha = self.alpha.forward_native(frame_mean, heads=slice(h0, h0 + hl))
             lin = vda_forward(q, k, v, gathered[:, H + h0:H + h0 + hl], lgate.view(T, hl, d), alpha,
                               bounds, frames, tokens, self.vda_norm)
+            rt.profile_end("vda_branch", ev)
+            ev = rt.profile_start()
             ex.scatter_quantize(lin.view(T, hl, d), ex.lin_dst)
+            rt.profile_end("vda_quantize_scatter", ev)
             return lin
 
         join = self._vda_side(branch, y1.device)
+        ev = rt.profile_start()
         att = torch.empty(T, hl, d, device=y1.device, dtype=torch.bfloat16)
         window_softmax(q, k, v, gathered[:, h0:h0 + hl], frames, tokens, cfg.radius, out=att)
+        rt.profile_end("window_softmax", ev)
+        ev = rt.profile_start()
         ex.scatter_quantize(att, ex.att_dst)
+        rt.profile_end("softmax_quantize_scatter", ev)
         join()
+        ev = rt.profile_start()
         ex.fence()
+        rt.profile_end("fence_rows", ev)
         return ex.operands()
 
     def _quantize_grouped(self, flat, offset, rows):

@@ -365,6 +365,9 @@ class UlyssesRuntime:
         e.record()
         self.profile_events.setdefault(name, []).append((start, e))
 
+    def reset_profile(self) -> None:
+        self.profile_events.clear()
+
     def profile_milliseconds(self):
         torch.cuda.synchronize(self.device)
         return {k: sum(a.elapsed_time(b) for a, b in v) for k, v in self.profile_events.items()}
