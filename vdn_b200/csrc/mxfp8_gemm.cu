@@ -65,6 +65,7 @@ struct Params {
   int64_t n;
   int m_tiles, n_tiles, k_blocks, k_blocks2, n_groups;  // n_groups = n_pad / 128
   int vec_ok;                // 16-byte vector epilogue allowed (alignment of y / bias / resid / gate)
+  int tma_y;                 // pair kernel, plain / residual store: y leaves by TMA stores (tmap_y)
   // Scatter epilogue (chunk_dst != null): the 128 output columns of chunk c go to
   // chunk_dst[c] + (dst_row0 + row) * dst_ld, e.g. each head's q / k / v slice
   // straight into the receive buffer of the rank that owns the head.
@@ -163,6 +164,77 @@ __device__ __forceinline__ void store_row(const Params& p, const uint32_t (&r)[1
       if (p.resid)
         v = bf16_bits_to_f32(p.resid[row * p.ldr + col]) + round_bf16(bf16_bits_to_f32(p.gate[col]) * v);
       dst[i] = f32_to_bf16_bits(v);
+    }
+  }
+}
+
+// Bulk-store form of store_row for one warp (32 consecutive rows from row0, 128
+// columns from col0, n % 128 == 0): the same arithmetic, but each 32-column piece of
+// the warp's rows is written into a 32 x 64-byte bf16 buffer in shared memory
+// (64-byte swizzle: the 32 row writers hit distinct banks) and leaves by one TMA
+// store, instead of 16-byte stores that touch 32 rows per instruction.  Rows past
+// rows_out are clipped by the tensor map.  The buffer is refilled once the previous
+// piece's store has read it (buf 512-byte aligned: the swizzle phase is the row's).
+__device__ __forceinline__ void store_rows_tma(const Params& p, const CUtensorMap* ymap, const uint32_t (&r)[128],
+                                               int64_t row0, int lane, int64_t col0, uint8_t* buf) {
+  const int64_t row = row0 + lane;
+  const uint4* rrow = (p.resid && row < p.rows_out) ? reinterpret_cast<const uint4*>(p.resid + row * p.ldr + col0)
+                                                    : nullptr;
+  const uint4* bias = p.bias ? reinterpret_cast<const uint4*>(p.bias + col0) : nullptr;
+  const uint4* gate = p.resid ? reinterpret_cast<const uint4*>(p.gate + col0) : nullptr;
+  uint8_t* mine = buf + lane * 64;
+  const uint32_t phase = (lane >> 1) & 3;
+#pragma unroll
+  for (int piece = 0; piece < 4; ++piece) {
+    uint4 out[4];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = 4 * piece + jj;
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        v[i] = __uint_as_float(r[8 * j + i]);
+        v[i + 1] = __uint_as_float(r[8 * j + i + 1]);
+        round_bf16_pair(v[i], v[i + 1]);
+      }
+      if (bias) {
+        float b[8];
+        unpack8(__ldg(bias + j), b);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          v[i] += b[i];
+          v[i + 1] += b[i + 1];
+          round_bf16_pair(v[i], v[i + 1]);
+        }
+      }
+      if (gate) {
+        float g[8], x[8];
+        unpack8(__ldg(gate + j), g);
+        if (rrow) {
+          unpack8(__ldg(rrow + j), x);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] = 0.f;  // a clipped row
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          float a = g[i] * v[i], b = g[i + 1] * v[i + 1];
+          round_bf16_pair(a, b);
+          v[i] = x[i] + a;
+          v[i + 1] = x[i + 1] + b;
+        }
+      }
+      out[jj] = pack8(v);
+    }
+    if (lane == 0) bulk_wait_group_read<0>();  // the previous piece has left the buffer
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(mine + ((c ^ phase) << 4)) = out[c];
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(ymap, buf, (int)(col0 + 32 * piece), (int)row0);
+      bulk_commit_group();
     }
   }
 }
@@ -508,12 +580,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                            const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_a2,
                            const __grid_constant__ CUtensorMap tmap_b2,
-                           const __grid_constant__ PairMaps sf, const Params p) {
+                           const __grid_constant__ PairMaps sf, const __grid_constant__ CUtensorMap tmap_y,
+                           const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + P_STAGES * P_A_BYTES;
-  uint8_t* sSF = sB + P_STAGES * P_B_BYTES;
+  uint8_t* stage_base = sB + P_STAGES * P_B_BYTES;  // 1024-aligned; 8 epilogue buffers of 2560 B
+  uint8_t* sSF = stage_base + 8 * STAGE_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(sSF + P_STAGES * P_SF_STAGE);
   uint64_t* empty = full + P_STAGES;
   uint64_t* acc_full = empty + P_STAGES;
@@ -521,7 +595,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   uint64_t* mma_done = acc_empty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  uint8_t* stage_base = sSF + P_STAGES * P_SF_STAGE + BAR_BYTES;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -708,9 +781,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       } else if constexpr (EPI == EPI_SCATTER) {
         if (col0 < p.n) store_rows_staged(p, r, row_base + quad * 32, lane, col0, stage_base + (warp - 2) * STAGE_BYTES);
       } else {
-        if (live) store_row(p, r, row, col0);
+        if (p.tma_y) {
+          if (row_base + quad * 32 < p.rows_out && col0 < p.n)
+            store_rows_tma(p, &tmap_y, r, row_base + quad * 32, lane, col0, stage_base + (warp - 2) * STAGE_BYTES);
+        } else if (live) {
+          store_row(p, r, row, col0);
+        }
       }
     }
+    if (EPI == EPI_STORE && lane == 0) bulk_wait_group<0>();  // stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -750,6 +829,22 @@ static int make_map(CUtensorMap* map, const void* base, int64_t k_pad, int64_t r
                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(VDN_ERR_RUNTIME, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return VDN_OK;
+}
+
+// bf16 output y [rows_out, n] (row stride ldy) for the bulk-store epilogue: 32 x 32
+// boxes with 64-byte swizzle.
+static int make_y_map(CUtensorMap* map, const void* y, int64_t n, int64_t rows_out, int64_t ldy) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(VDN_ERR_RUNTIME, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows_out};
+  cuuint64_t strides[1] = {(cuuint64_t)ldy * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(y), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VDN_ERR_RUNTIME, "cuTensorMapEncodeTiled (y) failed (%d)", (int)r);
   return VDN_OK;
 }
 
@@ -901,6 +996,7 @@ static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, 
   p.act = act;
   p.q_out = q_out;
   p.s_out = s_out;
+  p.tma_y = 0;
   static const bool pair_off = [] {
     const char* e = getenv("VDN_GEMM_PAIR");
     return e && e[0] == '0';
@@ -929,14 +1025,19 @@ static int launch_gemm(const uint8_t* xq, const uint8_t* xs, const uint8_t* wq, 
     const int tiles = p.m_tiles * p.n_tiles;
     const int pairs = tiles < info->pairs ? tiles : info->pairs;
     const dim3 grid(2 * pairs);
+    CUtensorMap my = ma;  // unused unless the bulk-store epilogue runs
+    if (!q_out && !chunk_dst && p.vec_ok && n % 128 == 0) {
+      if (int rc = make_y_map(&my, y, n, rows_out, ldy)) return rc;
+      p.tma_y = 1;
+    }
     if (q_out && act == VDN_ACT_GELU_TANH)
-      mxfp8_gemm_pair_kernel<EPI_QUANT_GELU><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, p);
+      mxfp8_gemm_pair_kernel<EPI_QUANT_GELU><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, my, p);
     else if (q_out)
-      mxfp8_gemm_pair_kernel<EPI_QUANT><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, p);
+      mxfp8_gemm_pair_kernel<EPI_QUANT><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, my, p);
     else if (chunk_dst)
-      mxfp8_gemm_pair_kernel<EPI_SCATTER><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, p);
+      mxfp8_gemm_pair_kernel<EPI_SCATTER><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, my, p);
     else
-      mxfp8_gemm_pair_kernel<EPI_STORE><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, p);
+      mxfp8_gemm_pair_kernel<EPI_STORE><<<grid, THREADS, P_SMEM_BYTES, stream>>>(ma, mb, ma2, mb2, sf, my, p);
     VDN_LAUNCH_CHECK("mxfp8 gemm (CTA pairs)");
     return VDN_OK;
   }

@@ -555,7 +555,8 @@ int launch_stats_tc(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, con
                     int64_t b_sh, int features_applied, int F, int S, int H, float* A, float* B,
                     int* status, cudaStream_t stream);
 bool tc_readout_supported(int d, const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh,
-                          const void* state, const void* gate, int64_t g_ss, int64_t g_sh);
+                          const void* state, const void* gate, int64_t g_sf, int64_t g_ss, int64_t g_sh,
+                          const void* out);
 int launch_readout_tc(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, const void* state,
                       const void* gate, int64_t g_sf, int64_t g_ss, int64_t g_sh, const float* norm_w,
                       float eps, int F, int S, int H, void* out, int* status, cudaStream_t stream);
@@ -713,7 +714,7 @@ int launch_readout(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, cons
   if (int rc = check_d(d)) return rc;
   VDN_CHECK_ARG(F >= 1 && S >= 1 && H >= 1, "positive F, S, H required");
   VDN_CHECK_ARG(q && state && gate && norm_weight && out, "null pointer");
-  if (tc_readout_supported(d, q, q_sf, q_ss, q_sh, state, gate, g_ss, g_sh) && aligned16(out))
+  if (tc_readout_supported(d, q, q_sf, q_ss, q_sh, state, gate, g_sf, g_ss, g_sh, out))
     return launch_readout_tc(q, q_sf, q_ss, q_sh, state, gate, g_sf, g_ss, g_sh, norm_weight, eps, F, S,
                              H, out, nullptr, stream);
   const size_t smem = ((size_t)d * d + 8 * d * 8) * sizeof(float);

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
   if (tid == 0) {
     for (int s = 0; s < ST_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], 512);
+      mbar_init(&ready[s], 16);  // one arrival per transform warp
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -213,7 +213,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       // Returns false when a wait gave up.
       auto chunk = [&](float bt) -> bool {
         const int s = g % ST_STAGES;
-        if (!mbar_wait(&full[s], (g / ST_STAGES) & 1, abort_flag)) {
+        // Warp-uniform outcome: the warp's lanes meet again at the __syncwarp below.
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (g / ST_STAGES) & 1, abort_flag))) {
           return false;
         }
         uint8_t* st = stages + s * ST_STAGE_BYTES;
@@ -264,7 +265,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         *reinterpret_cast<uint4*>(st + 4 * ST_REGION + off) = make_uint4(hi2[0], hi2[1], hi2[2], hi2[3]);
         *reinterpret_cast<uint4*>(st + 6 * ST_REGION + off) = make_uint4(lo2[0], lo2[1], lo2[2], lo2[3]);
         fence_proxy_async_smem();
-        mbar_arrive(&ready[s]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[s]);
         ++g;
         return true;
       };
@@ -347,43 +349,49 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 // --------------------------------------------------------------------- readout
 // Persistent, warp-specialised: grid = min(F*H, SMs), one CTA per SM walking
 // (frame, head) items.  Warp 0 lane 0 streams the item's bf16 state (double
-// buffered) and its 128-token q tiles (4-stage ring) by TMA; warps 2-9 turn the
-// tile into features in place (two threads per token row, 64 columns each:
-// measured 10% faster than four warps); warp 1 lane 0 issues q.state^T into one
-// of two TMEM accumulators; warps 10-13 drain them (thread = TMEM lane =
-// token): bf16 readout, RMSNorm over the row, * w, * gate, token-major store.
-// (Splitting the drain over eight warps, two per TMEM lane quadrant, measured
-// 27% slower.)  Hand-offs are mbarriers; every wait is bounded.
+// buffered), its 128-token q tiles (2-stage ring) and the matching gate tiles
+// (3-stage ring) by TMA; warps 2-9 turn the q tile into features in place (two
+// threads per token row, 64 columns each: measured 10% faster than four warps);
+// warp 1 lane 0 issues q.state^T into one of two TMEM accumulators; warps 10-13
+// drain them (thread = TMEM lane = token): bf16 readout, RMSNorm over the row, * w,
+// * the gate row read from the staged gate tile.  The result overwrites the gate in
+// shared memory and leaves by one TMA store per 64-column half, so global memory
+// sees only bulk tensor copies (a row-per-thread epilogue touches 32 rows per load
+// or store instruction).  Hand-offs are mbarriers; every wait is bounded.
 constexpr int RO_TOK = 128;
-constexpr int RO_STAGES = 4;
+constexpr int RO_STAGES = 2;                    // q tiles
+constexpr int RO_GSTAGES = 3;                   // gate / output tiles
 constexpr int RO_THREADS = 448;
 constexpr int RO_TILE = 2 * RO_TOK * 128;       // 2 regions x 128 rows x 128 B = 32 KB
-constexpr int RO_NBAR = 3 * RO_STAGES + 2 * 2 + 2 * 2 + 1;
-constexpr size_t RO_SMEM = 1024 + 2 * RO_TILE + RO_STAGES * RO_TILE + 128 * 4 + RO_NBAR * 8 + 64;
+constexpr int RO_NBAR = 3 * RO_STAGES + 2 * RO_GSTAGES + 2 * 2 + 2 * 2 + 1;
+constexpr size_t RO_SMEM =
+    1024 + 2 * RO_TILE + (RO_STAGES + RO_GSTAGES) * RO_TILE + 128 * 4 + RO_NBAR * 8 + 64;
+static_assert(RO_SMEM <= 232448, "shared memory per CTA");
 
 struct ReadoutParams {
-  const uint16_t* gate;
-  int64_t g_sf, g_ss, g_sh;
   const float* norm_w;
   float eps;
-  uint16_t* out;
   int S, H, items;
   int* status;
 };
 
 __global__ void __launch_bounds__(RO_THREADS, 1)
     readout_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tstate,
+                      const __grid_constant__ CUtensorMap tgate, const __grid_constant__ CUtensorMap tout,
                       const ReadoutParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* st_s = smem;                           // 2 state buffers
   uint8_t* q_s = smem + 2 * RO_TILE;              // RO_STAGES q tiles
-  float* w_s = reinterpret_cast<float*>(q_s + RO_STAGES * RO_TILE);
+  uint8_t* g_s = q_s + RO_STAGES * RO_TILE;       // RO_GSTAGES gate / output tiles
+  float* w_s = reinterpret_cast<float*>(g_s + RO_GSTAGES * RO_TILE);
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_s + 128);
   uint64_t* q_full = bars;
   uint64_t* q_ready = q_full + RO_STAGES;
   uint64_t* q_empty = q_ready + RO_STAGES;
-  uint64_t* acc_full = q_empty + RO_STAGES;
+  uint64_t* g_full = q_empty + RO_STAGES;
+  uint64_t* g_empty = g_full + RO_GSTAGES;
+  uint64_t* acc_full = g_empty + RO_GSTAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* st_full = acc_empty + 2;
   uint64_t* st_empty = st_full + 2;
@@ -397,8 +405,12 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
   if (tid == 0) {
     for (int s = 0; s < RO_STAGES; ++s) {
       mbar_init(&q_full[s], 1);
-      mbar_init(&q_ready[s], 256);
+      mbar_init(&q_ready[s], 8);  // one arrival per transform warp
       mbar_init(&q_empty[s], 1);
+    }
+    for (int s = 0; s < RO_GSTAGES; ++s) {
+      mbar_init(&g_full[s], 1);
+      mbar_init(&g_empty[s], 1);  // the store issuer, once the tile's store has read it
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -421,7 +433,7 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
     if (lane == 0) {
       // ------------------------------------------------------------ producer
       int g = 0, k = 0;
-      uint32_t pend = 0, pend_phase = 0;
+      uint32_t pend = 0, pend_phase = 0, gpend = 0, gpend_phase = 0;
       for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x, ++k) {
         const int f = item / p.H, h = item % p.H, sb = k & 1;
         if (!mbar_wait(&st_empty[sb], ((k >> 1) & 1) ^ 1, abort_flag)) break;
@@ -429,8 +441,8 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
         tma_load_2d(st_s + sb * RO_TILE, &tstate, &st_full[sb], 0, item * 128);
         tma_load_2d(st_s + sb * RO_TILE + RO_TILE / 2, &tstate, &st_full[sb], 64, item * 128);
         for (int i = 0; i < nt; ++i, ++g) {
-          const int s = g % RO_STAGES;
-          const uint32_t ph = (g / RO_STAGES) & 1;
+          const int s = g % RO_STAGES, gs = g % RO_GSTAGES;
+          const uint32_t ph = (g / RO_STAGES) & 1, gph = (g / RO_GSTAGES) & 1;
           if (!mbar_wait(&q_empty[s], ph ^ 1, abort_flag)) break;
           uint8_t* dst = q_s + s * RO_TILE;
           mbar_arrive_expect_tx(&q_full[s], RO_TILE);
@@ -438,6 +450,13 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
           tma_load_4d(dst + RO_TILE / 2, &tq, &q_full[s], 64, i * RO_TOK, h, f);
           pend |= 1u << s;
           pend_phase = (pend_phase & ~(1u << s)) | (ph << s);
+          if (!mbar_wait(&g_empty[gs], gph ^ 1, abort_flag)) break;
+          uint8_t* gdst = g_s + gs * RO_TILE;
+          mbar_arrive_expect_tx(&g_full[gs], RO_TILE);
+          tma_load_4d(gdst, &tgate, &g_full[gs], 0, i * RO_TOK, h, f);
+          tma_load_4d(gdst + RO_TILE / 2, &tgate, &g_full[gs], 64, i * RO_TOK, h, f);
+          gpend |= 1u << gs;
+          gpend_phase = (gpend_phase & ~(1u << gs)) | (gph << gs);
         }
       }
       if (*abort_flag) {  // let every issued copy land before the CTA may exit
@@ -445,6 +464,12 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
           if (!(pend >> s & 1)) continue;
           const uint64_t t0 = globaltimer();
           while (!mbar_try_wait(&q_full[s], (pend_phase >> s) & 1) && globaltimer() - t0 < kWaitLimitNs) {
+          }
+        }
+        for (int s = 0; s < RO_GSTAGES; ++s) {
+          if (!(gpend >> s & 1)) continue;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&g_full[s], (gpend_phase >> s) & 1) && globaltimer() - t0 < kWaitLimitNs) {
           }
         }
         for (int b = 0; b < 2 && k > b; ++b) {
@@ -504,7 +529,8 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
       bool ok = true;
       for (int i = 0; i < nt; ++i, ++g) {
         const int s = g % RO_STAGES;
-        if (!mbar_wait(&q_full[s], (g / RO_STAGES) & 1, abort_flag)) {
+        // Warp-uniform outcome: the warp's lanes meet again at the __syncwarp below.
+        if (!__all_sync(0xffffffffu, mbar_wait(&q_full[s], (g / RO_STAGES) & 1, abort_flag))) {
           ok = false;
           break;
         }
@@ -539,7 +565,8 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
           *ptr = pack8(x);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&q_ready[s]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_ready[s]);
       }
       if (!ok) break;
     }
@@ -547,23 +574,17 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;                   // warps 10..13
     const uint32_t erow = quad * 32 + lane;
+    const bool issuer = warp == 10 && lane == 0;
     int g = 0;
     for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
       const int f = item / p.H, h = item % p.H;
       bool ok = true;
       for (int i = 0; i < nt; ++i, ++g) {
-        const int b = g & 1;
-        const int s = i * RO_TOK + (int)erow;
-        const bool valid = s < p.S;
-        // The gate row does not depend on the accumulator: load all of it before
-        // waiting, so its DRAM latency overlaps the MMA instead of the epilogue.
-        const uint16_t* grow = p.gate + (int64_t)f * p.g_sf + (int64_t)s * p.g_ss + (int64_t)h * p.g_sh;
-        uint4 gv[16];
-        if (valid) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) gv[e] = *reinterpret_cast<const uint4*>(grow + 8 * e);
-        }
-        if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (g >> 1) & 1, abort_flag))) {
+        const int b = g & 1, gs = g % RO_GSTAGES;
+        const bool got = mbar_wait(&g_full[gs], (g / RO_GSTAGES) & 1, abort_flag) &&
+                         mbar_wait(&acc_full[b], (g >> 1) & 1, abort_flag);
+        // All four warps take the same branch: they meet at named barrier 1 below.
+        if (!bar_and(1, 128, got)) {
           ok = false;
           break;
         }
@@ -585,17 +606,18 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
         }
         const float nrm = sqrtf(ss);
         const float inv = round_bf16(__fdiv_rn(1.0f, sqrtf(nrm * nrm / 128.0f + p.eps)));
-        uint16_t* orow = p.out + ((int64_t)f * p.S + s) * ((int64_t)p.H * 128) + (int64_t)h * 128;
+        uint8_t* gt = g_s + gs * RO_TILE;
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(taddr + cb * 32, v);
           tmem_ld_wait();
-          if (!valid) continue;
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4) {
+            const int col = cb * 32 + 8 * e4;  // 8 columns in one 16-byte chunk of a 64-column half
+            uint4* cell = reinterpret_cast<uint4*>(gt + (col >> 6) * (RO_TILE / 2) + swz(erow, (col & 63) >> 3));
             float gf[8], y[8];
-            unpack8(gv[4 * cb + e4], gf);
+            unpack8(*cell, gf);
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
               const int c = 8 * e4 + e;
@@ -610,14 +632,27 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
               y[e] = r0 * gf[e];
               y[e + 1] = r1 * gf[e + 1];
             }
-            *reinterpret_cast<uint4*>(orow + cb * 32 + 8 * e4) = pack8(y);
+            *cell = pack8(y);
           }
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[b]);
+        // The tile's rows are in shared memory: one thread stores it (rows past S are
+        // clipped by the tensor map) once every epilogue thread's writes are visible
+        // to the async proxy.
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (issuer) {
+          tma_store_4d(&tout, gt, 0, i * RO_TOK, h, f);
+          tma_store_4d(&tout, gt + RO_TILE / 2, 64, i * RO_TOK, h, f);
+          bulk_commit_group();
+          bulk_wait_group_read<1>();  // the previous tile's store has read its buffer
+          if (g > 0) mbar_arrive(&g_empty[(g - 1) % RO_GSTAGES]);
+        }
       }
       if (!ok) break;
     }
+    if (issuer) bulk_wait_group<0>();  // every store written before the CTA exits
   }
   tc_fence_before();
   __syncthreads();
@@ -684,9 +719,10 @@ int launch_stats_tc(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, con
 }
 
 bool tc_readout_supported(int d, const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh,
-                          const void* state, const void* gate, int64_t g_ss, int64_t g_sh) {
-  return d == 128 && vtc::strides_ok(q, q_sf, q_ss, q_sh) && vtc::is16(state) && vtc::is16(gate) &&
-         g_ss % 8 == 0 && g_sh % 8 == 0;
+                          const void* state, const void* gate, int64_t g_sf, int64_t g_ss, int64_t g_sh,
+                          const void* out) {
+  return d == 128 && vtc::strides_ok(q, q_sf, q_ss, q_sh) && vtc::is16(state) &&
+         vtc::strides_ok(gate, g_sf, g_ss, g_sh) && vtc::is16(out);
 }
 
 int launch_readout_tc(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, const void* state,
@@ -699,8 +735,12 @@ int launch_readout_tc(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, c
   cuuint64_t strides[1] = {256};
   cuuint32_t box[2] = {64, 128};
   if (int rc = encode_map(&ms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, state, dims, strides, box)) return rc;
-  ReadoutParams p{static_cast<const uint16_t*>(gate), g_sf, g_ss, g_sh, norm_w, eps,
-                  static_cast<uint16_t*>(out), S, H, F * H, status};
+  CUtensorMap mg, mo;
+  if (int rc = map_tokens(&mg, gate, g_sf, g_ss, g_sh, F, S, H, RO_TOK)) return rc;
+  // out: token-major [F, S, H, 128] bf16.
+  const int64_t o_ss = (int64_t)H * 128;
+  if (int rc = map_tokens(&mo, out, (int64_t)S * o_ss, o_ss, 128, F, S, H, RO_TOK)) return rc;
+  ReadoutParams p{norm_w, eps, S, H, F * H, status};
   static bool attr_set = false;
   if (!attr_set) {
     VDN_CUDA_TRY(cudaFuncSetAttribute(readout_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RO_SMEM));
@@ -710,7 +750,7 @@ int launch_readout_tc(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh, c
   VDN_CUDA_TRY(cudaGetDevice(&dev));
   VDN_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = F * H < sms ? F * H : sms;
-  readout_tc_kernel<<<grid, RO_THREADS, RO_SMEM, stream>>>(mq, ms, p);
+  readout_tc_kernel<<<grid, RO_THREADS, RO_SMEM, stream>>>(mq, ms, mg, mo, p);
   VDN_LAUNCH_CHECK("vda readout (tcgen05)");
   return VDN_OK;
 }
