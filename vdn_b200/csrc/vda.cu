@@ -168,10 +168,9 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
                                                         float* Tout, float* Jout) {
   constexpr int T = D / 16;
   extern __shared__ float smem[];
-  float* rowbuf = smem;            // [2][D]
-  float* colbuf = smem + 2 * D;    // [2][D]
-  float* inv_s = smem + 4 * D;     // [D][D]
-  __shared__ float piv[2];
+  float* rowbuf = smem;            // [2 buffers][2 rows][D]
+  float* colbuf = smem + 4 * D;    // [2 buffers][2 columns][D]
+  float* inv_s = smem + 8 * D;     // [D][D]
   const int64_t mat = blockIdx.x;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const float* a_in = A + mat * D * D;
@@ -187,45 +186,68 @@ __global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const fl
       const int r = ty + 16 * i, c = tx + 16 * j;
       MV(i, j) = a_in[r * D + c] + (r == c ? 1.0f : 0.0f);
     }
-  // Pivot p = o + 16 jj lives in row slot jj of threads ty == o and column slot
-  // jj of threads tx == o: the slot is a compile-time index (m stays in registers).
+  // Pivots are taken two at a time, p = o + 16 jj and p + 1 (o even): rows p, p + 1
+  // live in row slot jj of threads ty == o, o + 1 and columns p, p + 1 in column slot
+  // jj of threads tx == o, o + 1, so every slot index is a compile-time constant and
+  // m stays in registers.  One step per pivot pair (64 barriers instead of 128):
+  // with P the 2 x 2 pivot block, R its two rows and C its two columns,
+  //   rows p, p+1    <- P^-1 R
+  //   other rows     <- M - C (P^-1 R)      (a rank-2 update, two paired FMAs)
+  //   columns p, p+1 <- -C P^-1,  P <- P^-1
+  // which is two consecutive Gauss-Jordan pivots computed as one block step (SPD:
+  // every leading 2 x 2 block of the Schur complements is SPD, so no pivoting).
 #pragma unroll
   for (int jj = 0; jj < T; ++jj) {
-    for (int o = 0; o < 16; ++o) {
+    for (int o = 0; o < 16; o += 2) {
       const int p = o + 16 * jj;
-      float* rb = rowbuf + (p & 1) * D;
-      float* cb = colbuf + (p & 1) * D;
-      if (ty == o) {
+      float* rb = rowbuf + ((o >> 1) & 1) * 2 * D;  // rows p, p + 1 of M:    rb[k * D + col]
+      float* cb = colbuf + ((o >> 1) & 1) * 2 * D;  // columns p, p + 1 of M: cb[k * D + row]
+      if (ty == o || ty == o + 1) {
+        float* dst = rb + (ty - o) * D;
 #pragma unroll
-        for (int j = 0; j < T; ++j) rb[tx + 16 * j] = MV(jj, j);
-        if (tx == o) piv[p & 1] = __fdiv_rn(1.0f, MV(jj, jj));
+        for (int j = 0; j < T; ++j) dst[tx + 16 * j] = MV(jj, j);
       }
-      if (tx == o) {
+      if (tx == o || tx == o + 1) {
+        float* dst = cb + (tx - o) * D;
 #pragma unroll
-        for (int i = 0; i < T; ++i) cb[ty + 16 * i] = MV(i, jj);
+        for (int i = 0; i < T; ++i) dst[ty + 16 * i] = MV(i, jj);
       }
       __syncthreads();
-      const float ip = piv[p & 1];
-      float prow[T], pcol[T];
+      const float pa = rb[p], pb = rb[p + 1], pc = rb[D + p], pd = rb[D + p + 1];
+      const float rdet = __fdiv_rn(1.0f, fmaf(pa, pd, -pb * pc));
+      const float i00 = pd * rdet, i01 = -pb * rdet, i10 = -pc * rdet, i11 = pa * rdet;
+      float r0[T], r1[T], c0[T], c1[T];
 #pragma unroll
-      for (int j = 0; j < T; ++j) prow[j] = rb[tx + 16 * j] * ip;
-#pragma unroll
-      for (int i = 0; i < T; ++i) pcol[i] = cb[ty + 16 * i];
+      for (int j = 0; j < T; ++j) {
+        const float x0 = rb[tx + 16 * j], x1 = rb[D + tx + 16 * j];
+        r0[j] = fmaf(i00, x0, i01 * x1);
+        r1[j] = fmaf(i10, x0, i11 * x1);
+      }
 #pragma unroll
       for (int i = 0; i < T; ++i) {
-        const float2 c2 = make_float2(-pcol[i], -pcol[i]);
-#pragma unroll
-        for (int jp = 0; jp < T / 2; ++jp)
-          m2[i][jp] = __ffma2_rn(c2, make_float2(prow[2 * jp], prow[2 * jp + 1]), m2[i][jp]);
+        c0[i] = cb[ty + 16 * i];
+        c1[i] = cb[D + ty + 16 * i];
       }
-      if (ty == o) {
 #pragma unroll
-        for (int j = 0; j < T; ++j) MV(jj, j) = prow[j];
+      for (int i = 0; i < T; ++i) {
+        const float2 n0 = make_float2(-c0[i], -c0[i]), n1 = make_float2(-c1[i], -c1[i]);
+#pragma unroll
+        for (int jp = 0; jp < T / 2; ++jp) {
+          m2[i][jp] = __ffma2_rn(n0, make_float2(r0[2 * jp], r0[2 * jp + 1]), m2[i][jp]);
+          m2[i][jp] = __ffma2_rn(n1, make_float2(r1[2 * jp], r1[2 * jp + 1]), m2[i][jp]);
+        }
       }
-      if (tx == o) {
+      if (ty == o || ty == o + 1) {
+        const bool second = ty != o;
 #pragma unroll
-        for (int i = 0; i < T; ++i) MV(i, jj) = -pcol[i] * ip;
-        if (ty == o) MV(jj, jj) = ip;
+        for (int j = 0; j < T; ++j) MV(jj, j) = second ? r1[j] : r0[j];
+      }
+      if (tx == o || tx == o + 1) {
+        const bool second = tx != o;
+        const float q0 = second ? i01 : i00, q1 = second ? i11 : i10;  // column k of P^-1
+#pragma unroll
+        for (int i = 0; i < T; ++i) MV(i, jj) = -fmaf(c0[i], q0, c1[i] * q1);
+        if (ty == o || ty == o + 1) MV(jj, jj) = ty == o ? q0 : q1;
       }
     }
   }
@@ -620,7 +642,7 @@ int launch_factors(const float* A, const float* B, const float* alpha, int64_t n
   VDN_CHECK_ARG(A && B && T && J, "null pointer");
   VDN_CHECK_ARG(aligned16(A) && aligned16(B), "A and B must be 16-byte aligned");
   VDN_CHECK_ARG(n < (1ll << 31), "too many matrices");
-  const size_t smem = (4 * d + d * d) * sizeof(float);
+  const size_t smem = (8 * d + d * d) * sizeof(float);
   if (d == 128) {
     if (int rc = set_smem(factor_kernel<128>, smem)) return rc;
     factor_kernel<128><<<(unsigned)n, 256, smem, stream>>>(A, B, alpha, T, J);
@@ -638,7 +660,7 @@ int launch_factor_split(const float* A, int64_t n, void* planes, cudaStream_t st
   VDN_CHECK_ARG(n >= 0 && n < (1ll << 31), "bad matrix count");
   if (n == 0) return VDN_OK;
   VDN_CHECK_ARG(A && planes && aligned16(A) && aligned16(planes), "A and planes must be 16-byte aligned");
-  const size_t smem = (4 * 128 + 128 * 128) * sizeof(float);
+  const size_t smem = (8 * 128 + 128 * 128) * sizeof(float);
   if (int rc = set_smem(factor_kernel<128, true>, smem)) return rc;
   factor_kernel<128, true><<<(unsigned)n, 256, smem, stream>>>(A, nullptr, nullptr, static_cast<float*>(planes),
                                                               nullptr);
