@@ -160,6 +160,19 @@ int vdn_mxfp8_gemm_act_quantize(const uint8_t* xq, const uint8_t* xs, const uint
                                 int64_t n, int64_t n_pad, int64_t rows_out, int act, uint8_t* q,
                                 uint8_t* s, int* status, cudaStream_t stream);
 
+/* bf16 GEMM with the gate epilogue: y[:rows, :n] = act(bf16(x w^T + bias)) with fp32
+ * accumulation and the bias added before the single bf16 rounding (an eager bf16
+ * nn.Linear), act = sigmoid followed by bf16 rounding on columns < n_sig (torch.sigmoid
+ * on the bf16 tensor), identity after.  x [rows, k] (row stride ldx), w [n, k] (row
+ * stride ldw), y [rows, n] (row stride ldy): bf16, 16-byte aligned, strides multiples
+ * of 8 elements; k % 64 == 0; bias [n] bf16 or NULL.  tcgen05 kind::f16, TMA in and out.
+ * Replaces the gate projections of src/models/hybrid_attention.py:108-255 (softmax gate
+ * and beta projection, sigmoid) and OutputGate of src/models/attention_gates.py:13-55
+ * (down, then up + sigmoid): the block calls it once for [softmax gate | beta | output
+ * gate down] over y1 and once for the output gate's up projection. */
+int vdn_gate_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias, int64_t rows,
+                  int64_t n, int64_t k, int64_t n_sig, void* y, int64_t ldy, int* status, cudaStream_t stream);
+
 /* Window-softmax combine: merges n_partials dense attentions of query frame f
  * against key frame f + delta_j (outs[j] bf16 [rows_j, H*d] token-major, lses[j]
  * fp32 [batches_j, H, S]; batch = f - batch0[j], valid for frame_lo[j] <= f <=

@@ -38,6 +38,7 @@ SIGNATURES = {
     "vdn_mxfp8_gemm": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "vdn_mxfp8_gemm_fused": (_i32, [_p, _p, _p, _p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64,
                                     _i64, _p, _i64, _p, _i64, _p, _p, _p]),
+    "vdn_gate_gemm": (_i32, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "vdn_mxfp8_quantize_grouped": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
     "vdn_mxfp8_gemm_scatter": (_i32, [_p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _i64,
                                       _p, _p]),

@@ -36,6 +36,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from . import _lib
+from .gates import gate_gemm
 from .linear_attention import FrameKDAAlpha, OutputGate, window_bounds
 from .mxfp8_kernels import launch_prenorm_quantize
 from .mxfp8_quant import quantize_cpu, quantize_activation
@@ -171,12 +172,14 @@ class HybridBlock(nn.Module):
             self._gate_b = bias
             self._gate_key = key
         H = self.cfg.heads
-        z = F.linear(y1, self._gate_w, self._gate_b)
-        z[:, :2 * H].sigmoid_()
-        if out is None:
-            return z
-        out.copy_(z)
-        return out
+        return gate_gemm(y1, self._gate_w, self._gate_b, n_sig=2 * H, out=out)
+
+    def _linear_gate(self, hidden, cols=slice(None)):
+        """The VDA output gate sigmoid(up(hidden)) for output columns `cols` (a head
+        range of H*d): [rows, len(cols)] bf16, on the tcgen05 gate GEMM."""
+        og = self.output_gate
+        w, b = og.up.weight[cols], og.up.bias[cols]
+        return gate_gemm(hidden, w, b, n_sig=w.shape[0])
 
     def _side(self, device):
         """The branch-overlap stream of this device (the reference's vda_on_side_stream,
@@ -280,7 +283,7 @@ class HybridBlock(nn.Module):
             g3 = self._gate_projections(y1)                               # [rows, 2H + r]
             sgate, beta = g3[:, :H], g3[:, H:2 * H]                       # [rows, H] each
             og = self.output_gate
-            lgate = torch.sigmoid(F.linear(g3[:, 2 * H:], og.up.weight, og.up.bias))  # [rows, H*d]
+            lgate = self._linear_gate(g3[:, 2 * H:])                      # [rows, H*d]
             if runtime is None:
                 frame_mean = y1.view(frames, tokens, hd).mean(1, dtype=torch.float32)
                 first, second = self._attention(qkv, sgate, beta, lgate, frame_mean, frames, tokens,
@@ -346,7 +349,7 @@ class HybridBlock(nn.Module):
             q = qkv[:, :hd].view(n, H, d)
             k = qkv[:, hd:2 * hd].view(n, H, d)
             v = qkv[:, 2 * hd:].view(n, H, d)
-            lgate = torch.sigmoid(F.linear(g3[L:, 2 * H:], og.up.weight, og.up.bias)).view(T, H, d)
+            lgate = self._linear_gate(g3[L:, 2 * H:]).view(T, H, d)
             frame_mean = y1[L:].view(frames, tokens, hd).mean(1, dtype=torch.float32)
             att = torch.empty(n, H, d, device=dev, dtype=torch.bfloat16)
             lin_q = self._layout_branches(q, k, v, g3[:, :H], g3[:, H:2 * H], lgate, frame_mean, frames,
@@ -361,7 +364,7 @@ class HybridBlock(nn.Module):
             hl = H // rt.world_size
             N = L + T
             sums, work = rt.video_frame_mean_async(y1, frames, tokens, video_start=L)
-            lgate = torch.sigmoid(F.linear(g3[:, 2 * H:], og.up.weight, og.up.bias))
+            lgate = self._linear_gate(g3[:, 2 * H:])
             # Per head: q | k | v | linear gate | softmax gate | beta | pad (W = 4d + 8).
             W = 4 * d + 8
             pack = torch.empty(n, H, W, device=dev, dtype=torch.bfloat16)
@@ -542,7 +545,7 @@ class HybridBlock(nn.Module):
         else:
             og = self.output_gate
             cols = slice(h0 * d, (h0 + hb) * d)
-            lgate = torch.sigmoid(F.linear(shared.contiguous(), og.up.weight[cols], og.up.bias[cols]))
+            lgate = self._linear_gate(shared, cols)
             alpha = self.alpha.forward_native(frame_mean, heads=slice(h0, h0 + hb))
             out = vda_forward(qh, kh, vh, scalar, lgate.view(T, hb, d), alpha,
                               window_bounds(frames, cfg.radius), frames, tokens,
@@ -593,7 +596,7 @@ class HybridBlock(nn.Module):
         recv = ex.qkv()                                                   # [T, hl, 3d]
         q, k, v = recv[:, :, 0:d], recv[:, :, d:2 * d], recv[:, :, 2 * d:3 * d]
         cols = slice(h0 * d, (h0 + hl) * d)
-        lgate = torch.sigmoid(F.linear(gathered[:, 2 * H:], og.up.weight[cols], og.up.bias[cols]))
+        lgate = self._linear_gate(gathered[:, 2 * H:], cols)
         bounds = window_bounds(frames, cfg.radius)
 
         def branch():  # VDA and its return scatter, on the side stream

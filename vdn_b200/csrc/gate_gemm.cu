@@ -1,0 +1,287 @@
+// bf16 tcgen05 GEMM with the gate epilogue of the hybrid block:
+//     y[:rows, :n] = act(bf16(x @ w^T + bias)),  act = sigmoid (then bf16) on columns < n_sig
+// i.e. an eager bf16 nn.Linear (fp32 accumulation, bias added before the one rounding)
+// followed by torch.sigmoid on the bf16 result, for the first n_sig output columns.
+// The block calls it twice per forward (reference hybrid_attention.py:108-255 and
+// attention_gates.py:13-55, branch.py beta_proj):
+//   * y1 [T, 5120] @ [softmax_gate; beta_proj; output_gate.down]^T -> [T, 2H + r],
+//     sigmoid on the 2H gate columns, the output gate's hidden r columns plain;
+//   * hidden [T, r] @ output_gate.up^T + up.bias -> sigmoid -> the VDA gate [T, H*d].
+//
+// Persistent and warp-specialised, one CTA per SM walking 128 x 256 output tiles
+// (N fastest, so a row tile's x stays in L2 while the N tiles sweep):
+//   warp 0 lane 0   TMA producer: x tile 128 x 64 and w tile 256 x 64 (bf16, 128B
+//                   swizzle; w rows past n read as zero) into a 4-stage ring
+//   warp 1          TMEM (512 columns: two 256-column accumulators); lane 0 issues
+//                   four 128x256x16 MMAs per stage
+//   warps 2-9       epilogue: warp = TMEM lane quadrant x 128-column half; per
+//                   32-column piece: tcgen05.ld, bias, bf16, sigmoid, bf16, written
+//                   into a 2 KB shared buffer (64-byte swizzle) and sent by one TMA
+//                   store (columns past n and rows past `rows` are clipped)
+// Every wait is bounded; a timeout aborts all roles and reports VDN_ERR_TIMEOUT.
+// No TMA multicast.
+#include "common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+namespace vdn {
+namespace ggemm {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 64;   // BK: 64 bf16 = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;           // 16 KB
+constexpr int B_BYTES = BN * BK * 2;           // 32 KB
+constexpr int THREADS = 320;
+constexpr int PIECE_BYTES = 32 * 64;           // 32 rows x 32 bf16
+constexpr int NBAR = 2 * STAGES + 2 * 2 + 1;
+constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + 8 * PIECE_BYTES + NBAR * 8 + 64;
+static_assert(SMEM <= 232448, "shared memory per CTA");
+
+struct Params {
+  const uint16_t* bias;  // [n] bf16 or null
+  int64_t rows, n;
+  int n_sig;
+  int m_tiles, n_tiles, k_blocks;
+  int* status;
+};
+
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gate_gemm_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
+                     const __grid_constant__ CUtensorMap ty, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* pieces = sB + STAGES * B_BYTES;       // 8 x 2 KB, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(pieces + 8 * PIECE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_drain = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp
+    }
+    mbar_init(mma_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tx);
+    prefetch_tensormap(&tw);
+    prefetch_tensormap(&ty);
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int stage = 0;
+      uint32_t phase = 0, pend = 0, pend_phase = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        const int mb = t / p.n_tiles, nb = t % p.n_tiles;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tx, &full[stage], kb * BK, mb * BM);
+          tma_load_2d(sB + stage * B_BYTES, &tw, &full[stage], kb * BK, nb * BN);
+          pend |= 1u << stage;
+          pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {  // copies already issued land before the CTA may exit
+        for (int s = 0; s < STAGES; ++s) {
+          if (!(pend >> s & 1)) continue;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&full[s], (pend_phase >> s) & 1) && globaltimer() - t0 < kWaitLimitNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ----------------------------------------------------------------- MMA
+      constexpr uint32_t kIdesc = idesc_bf16(BM, BN, 0, 0);
+      int stage = 0, k = 0;
+      uint32_t phase = 0;
+      bool issued = false;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++k) {
+        const int b = k & 1;
+        if (!mbar_wait(&acc_empty[b], ((k >> 1) & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES), b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks)
+            mma_bf16(tmem + b * BN, desc_k_sw128(a0 + ks * 32), desc_k_sw128(b0 + ks * 32), kIdesc,
+                     (kb | ks) != 0);
+          issued = true;
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[b]);
+      }
+      if (*abort_flag && issued) {
+        tc_commit(mma_drain);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(mma_drain, 0) && globaltimer() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3, half = (warp - 2) >> 2;
+    uint8_t* buf = pieces + (warp - 2) * PIECE_BYTES;
+    uint8_t* mine = buf + lane * 64;
+    const uint32_t phase64 = (lane >> 1) & 3;    // 64-byte swizzle phase of this row
+    int k = 0;
+    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++k) {
+      const int mb = t / p.n_tiles, nb = t % p.n_tiles, b = k & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (k >> 1) & 1, abort_flag))) break;
+      tc_fence_after();
+      const int64_t row0 = (int64_t)mb * BM + quad * 32;
+      const int64_t col0 = (int64_t)nb * BN + half * 128;
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + b * BN + half * 128;
+      const bool live = row0 < p.rows && col0 < p.n;   // warp-uniform
+#pragma unroll 1
+      for (int piece = 0; piece < 4; ++piece) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + piece * 32, r);
+        tmem_ld_wait();
+        if (!live) continue;
+        // lane j holds the bias of the piece's column j; every lane takes column i's by shuffle
+        const int64_t colj = col0 + piece * 32 + lane;
+        const float bj = (p.bias && colj < p.n) ? bf16_bits_to_f32(p.bias[colj]) : 0.f;
+        uint4 out[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t col = col0 + piece * 32 + c * 8 + i;
+            const float bias = __shfl_sync(0xffffffffu, bj, c * 8 + i);
+            float x = round_bf16(__uint_as_float(r[c * 8 + i]) + bias);
+            if (col < p.n_sig) x = round_bf16(sigmoid_f(x));
+            v[i] = x;
+          }
+          out[c] = pack_exact8(v);
+        }
+        if (lane == 0) bulk_wait_group_read<0>();  // the previous piece has left the buffer
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(mine + ((c ^ phase64) << 4)) = out[c];
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&ty, buf, (int)(col0 + piece * 32), (int)row0);
+          bulk_commit_group();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+    if (lane == 0) bulk_wait_group<0>();  // every store written before the CTA exits
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && *abort_flag && p.status) atomicExch(p.status, VDN_ERR_TIMEOUT);
+}
+
+}  // namespace ggemm
+}  // namespace vdn
+
+using namespace vdn;
+
+extern "C" int vdn_gate_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
+                             int64_t rows, int64_t n, int64_t k, int64_t n_sig, void* y, int64_t ldy,
+                             int* status, cudaStream_t stream) {
+  using namespace vdn::ggemm;
+  VDN_CHECK_ARG(rows >= 0 && n > 0 && k > 0 && k % BK == 0, "need rows >= 0, n > 0 and k a positive multiple of 64");
+  VDN_CHECK_ARG(n_sig >= 0 && n_sig <= n, "n_sig must lie in [0, n]");
+  VDN_CHECK_ARG(rows < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), "extents too large");
+  if (rows == 0) return VDN_OK;
+  VDN_CHECK_ARG(x && w && y, "null pointer");
+  VDN_CHECK_ARG(aligned16(x) && aligned16(w) && aligned16(y), "x, w and y must be 16-byte aligned");
+  VDN_CHECK_ARG(ldx >= k && ldw >= k && ldy >= n && ldx % 8 == 0 && ldw % 8 == 0 && ldy % 8 == 0,
+                "row strides must cover the extents and be multiples of 8 elements");
+  CUtensorMap mx, mw, my;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+    cuuint32_t box[2] = {BK, BM};
+    if (int rc = encode_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims, strides, box)) return rc;
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)n};
+    cuuint64_t strides[1] = {(cuuint64_t)ldw * 2};
+    cuuint32_t box[2] = {BK, BN};
+    if (int rc = encode_map(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, strides, box)) return rc;
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ldy * 2};
+    cuuint32_t box[2] = {32, 32};
+    if (int rc = encode_map_swizzle(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box,
+                                    CU_TENSOR_MAP_SWIZZLE_64B))
+      return rc;
+  }
+  Params p;
+  p.bias = static_cast<const uint16_t*>(bias);
+  p.rows = rows;
+  p.n = n;
+  p.n_sig = (int)n_sig;
+  p.m_tiles = (int)((rows + BM - 1) / BM);
+  p.n_tiles = (int)((n + BN - 1) / BN);
+  p.k_blocks = (int)(k / BK);
+  p.status = status;
+  static bool attr_set[64] = {};
+  int dev = 0, sms = 148;
+  VDN_CUDA_TRY(cudaGetDevice(&dev));
+  VDN_CHECK_ARG(dev >= 0 && dev < 64, "device index out of range");
+  if (!attr_set[dev]) {
+    VDN_CUDA_TRY(cudaFuncSetAttribute(gate_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM));
+    attr_set[dev] = true;
+  }
+  VDN_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+  const int grid = tiles < sms ? (int)tiles : sms;
+  gate_gemm_kernel<<<grid, THREADS, SMEM, stream>>>(mx, mw, my, p);
+  VDN_LAUNCH_CHECK("gate gemm");
+  return VDN_OK;
+}
