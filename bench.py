@@ -118,12 +118,13 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-# DRAM bytes (read + write) per launch of the dominant kernels at the full
-# BASELINE shapes, from a separate ncu capture (not measured in this run; the
-# capture is summarised under profiles/); reported as roofline "traffic" with
-# "traffic_source" saying so.
+# DRAM bytes (read + write) per launch of the dominant kernels, from separate ncu
+# captures of small cases of the same kernels (not measured in this run; summarised
+# under profiles/), scaled to the full BASELINE shapes by the units processed:
+# the QKV GEMM from 4096 rows (x 32760 / 4096), the VDA kernels from 5 frames
+# (x 21 / 5).  Reported as roofline "traffic" with "traffic_source" saying so.
 NCU_TRAFFIC_BYTES = {
-    "mxfp8_gemm_qkv": 1471.4e6 + 981.8e6,
+    "mxfp8_gemm_qkv": (104.2e6 + 97.6e6) * 32760 / 4096,
     "statistics": 674.4e6 + 89.9e6,
     "factors": None,
     "scan": None,
@@ -131,7 +132,8 @@ NCU_TRAFFIC_BYTES = {
     "readout": 698.8e6 + 297.0e6,
 }
 
-TRAFFIC_SOURCE = "from a separate ncu capture of this kernel (profiles/), not measured in this run"
+TRAFFIC_SOURCE = ("from a separate ncu capture of a small case of this kernel (profiles/), scaled to "
+                  "this shape by the units processed; not measured in this run")
 
 
 # ------------------------------------------------------------------ timing

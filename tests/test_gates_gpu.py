@@ -1,30 +1,46 @@
 """GPU: the gate GEMM (vdn_gate_gemm) against an fp64 composition of the reference's
 eager ops: sigmoid(bf16(x @ w^T + b)) rounded to bf16 on the first n_sig columns,
 bf16(x @ w^T + b) after them (reference src/models/attention_gates.py:13-55,
-src/models/hybrid_attention.py:108-255).  fp32 accumulation in a different order
-from the fp64 sum can move a value across a bf16 rounding boundary, so the bar is
-one bf16 ulp on at most 1 % of the outputs (no other difference)."""
+src/models/hybrid_attention.py:108-255).
+
+The kernel sums in fp32, the check in fp64, so the bf16 logit may land one bf16 step
+either side of the fp64 one (near a rounding boundary; more for a logit that cancels
+below the fp32 summation noise); the sigmoid of a logit one step away can differ by
+several bf16 steps of the (smaller) sigmoid value.  So: plain columns
+within one bf16 step of the fp64-rounded logit, sigmoid columns between the bf16
+sigmoids of the two neighbouring logits, and at most 1 % of all outputs different from
+the fp64 composition."""
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
 
-def _reference(x, w, b, n_sig):
+def _logits(x, w, b):
     z = x.double() @ w.double().T
     if b is not None:
         z = z + b.double()
-    z = z.float().bfloat16().float()                 # the Linear's bf16 output
+    return z.float().bfloat16().float()               # the Linear's bf16 output
+
+
+def _reference(x, w, b, n_sig):
+    z = _logits(x, w, b)
     z[:, :n_sig] = torch.sigmoid(z[:, :n_sig]).bfloat16().float()
     return z
 
 
-def _check(got, want):
+def _check(got, x, w, b, n_sig):
     got = got.float().cpu()
-    diff = (got - want).abs()
-    ulp = want.abs().clamp_min(2 ** -126) * 2 ** -7   # one bf16 ulp upper bound
-    assert bool((diff <= ulp).all()), float(diff.max())
-    frac = float((diff > 0).float().mean())
+    z = _logits(x, w, b)
+    # one bf16 step at z, plus the fp32 summation error of a sum that cancels (2^-16 of
+    # the sum of the terms' magnitudes: a small logit can sit below the fp32 noise)
+    step = torch.exp2(torch.floor(torch.log2(z.abs().clamp_min(2.0 ** -100))) - 7)
+    step = step + 2.0 ** -16 * (x.abs().double() @ w.abs().double().T).float()
+    assert bool(((got[:, n_sig:] - z[:, n_sig:]).abs() <= step[:, n_sig:]).all())
+    s_lo = torch.sigmoid(z[:, :n_sig] - step[:, :n_sig]).bfloat16().float()
+    s_hi = torch.sigmoid(z[:, :n_sig] + step[:, :n_sig]).bfloat16().float()
+    assert bool(((got[:, :n_sig] >= s_lo) & (got[:, :n_sig] <= s_hi)).all())
+    frac = float((got != _reference(x, w, b, n_sig)).float().mean())
     assert frac < 0.01, frac
 
 
@@ -39,7 +55,7 @@ def test_gate_gemm_matches_fp64(cuda, rows, n, k, n_sig):
     b = (torch.randn(n, generator=g) * 0.5).bfloat16()
     y = gate_gemm(x.to(cuda), w.to(cuda), b.to(cuda), n_sig=n_sig)
     torch.cuda.synchronize()
-    _check(y, _reference(x.float(), w.float(), b.float(), n_sig))
+    _check(y, x.float(), w.float(), b.float(), n_sig)
 
 
 @torch.no_grad()
@@ -54,7 +70,7 @@ def test_gate_gemm_strided_views_and_out(cuda):
         b = torch.randn(H * 128, generator=g).bfloat16().to(cuda)
         hidden = g3[:, 2 * H:]
         y = gate_gemm(hidden, w, b, n_sig=H * 128)
-        _check(y, _reference(hidden.float().cpu(), w.float().cpu(), b.float().cpu(), H * 128))
+        _check(y, hidden.float().cpu(), w.float().cpu(), b.float().cpu(), H * 128)
         buf = torch.zeros(777, H * 128 + 8, dtype=torch.bfloat16, device=cuda)
         out = buf[:, :H * 128]
         r = gate_gemm(hidden, w, b, n_sig=H * 128, out=out)

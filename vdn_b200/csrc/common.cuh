@@ -94,6 +94,24 @@ __device__ __forceinline__ uint4 pack_exact8(const float* v) {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
+// sigmoid(x) = 1 / (1 + t) for x >= 0 and t / (1 + t) for x < 0, with t = exp(-|x|) in
+// (0, 1].  The exponential is one MUFU operation; the divisor y = 1 + t lies in (1, 2],
+// so its reciprocal is taken on the FMA pipe: Newton-Raphson division from the textbook
+// linear seed 48/17 - 32/17 D for D = y / 2 in (1/2, 1] (relative error <= 1/17, squared
+// by each of three steps: below fp32 rounding).  For kernels whose MUFU / conversion pipe
+// is the limit (the gate GEMM's epilogue), this halves its load against exp + a hardware
+// reciprocal; kernels bound by issue are better off with the hardware reciprocal.
+__device__ __forceinline__ float sigmoid_nr(float x) {
+  const float t = __expf(-fabsf(x));
+  const float d = 0.5f * (1.0f + t);
+  float r = fmaf(-32.0f / 17.0f, d, 48.0f / 17.0f);
+  r = fmaf(r, fmaf(-d, r, 1.0f), r);
+  r = fmaf(r, fmaf(-d, r, 1.0f), r);
+  r = fmaf(r, fmaf(-d, r, 1.0f), r);
+  r *= 0.5f;
+  return x >= 0.0f ? r : t * r;
+}
+
 // Exact three-way bf16 split of eight fp32 values: x = x1 + x2 + x3 with each part
 // the round-to-nearest bf16 of what the earlier parts leave (every subtraction is
 // exact in fp32, and the three 8-bit significands cover fp32's 24).  w[p] holds

@@ -14,10 +14,15 @@
 //                   swizzle; w rows past n read as zero) into a 4-stage ring
 //   warp 1          TMEM (512 columns: two 256-column accumulators); lane 0 issues
 //                   four 128x256x16 MMAs per stage
-//   warps 2-9       epilogue: warp = TMEM lane quadrant x 128-column half; per
-//                   32-column piece: tcgen05.ld, bias, bf16, sigmoid, bf16, written
-//                   into a 2 KB shared buffer (64-byte swizzle) and sent by one TMA
-//                   store (columns past n and rows past `rows` are clipped)
+//   warps 2-17      epilogue: warp = TMEM lane quadrant x 64-column group; its 32
+//                   rows x 64 columns (tcgen05.ld, bias, bf16, sigmoid, bf16) are
+//                   written into a 4 KB shared buffer (128-byte swizzle) and sent by
+//                   one TMA store; the buffer is reused one tile later, so the store
+//                   never holds up the next tile's math (columns past n and rows past
+//                   `rows` are clipped by the tensor map).  Sixteen warps, four per
+//                   sub-partition, and the bias loaded before the accumulator wait:
+//                   the sigmoid's two MUFU operations per element are the kernel's
+//                   limit at K = 128, and with fewer warps their latency was.
 // Every wait is bounded; a timeout aborts all roles and reports VDN_ERR_TIMEOUT.
 // No TMA multicast.
 #include "common.cuh"
@@ -30,13 +35,14 @@ namespace ggemm {
 using namespace sm100;
 
 constexpr int BM = 128, BN = 256, BK = 64;   // BK: 64 bf16 = one 128-byte swizzle row
-constexpr int STAGES = 4;
+constexpr int STAGES = 3;
 constexpr int A_BYTES = BM * BK * 2;           // 16 KB
 constexpr int B_BYTES = BN * BK * 2;           // 32 KB
-constexpr int THREADS = 320;
-constexpr int PIECE_BYTES = 32 * 64;           // 32 rows x 32 bf16
+constexpr int THREADS = 576;                   // 2 + 16 epilogue warps
+constexpr int PIECE_BYTES = 32 * 128;          // 32 rows x 64 bf16 (one 128B-swizzled store box)
+constexpr int EPI_WARPS = 16;
 constexpr int NBAR = 2 * STAGES + 2 * 2 + 1;
-constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + 8 * PIECE_BYTES + NBAR * 8 + 64;
+constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * PIECE_BYTES + NBAR * 8 + 64;
 static_assert(SMEM <= 232448, "shared memory per CTA");
 
 struct Params {
@@ -47,7 +53,9 @@ struct Params {
   int* status;
 };
 
-__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// The sigmoid is sigmoid_nr (common.cuh): one MUFU exponential, the reciprocal on the
+// FMA pipe -- the MUFU / conversion pipe is this epilogue's limit.
+__device__ __forceinline__ float sigmoid_f(float x) { return sigmoid_nr(x); }
 
 __global__ void __launch_bounds__(THREADS, 1)
     gate_gemm_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
@@ -56,8 +64,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
-  uint8_t* pieces = sB + STAGES * B_BYTES;       // 8 x 2 KB, 1024-aligned
-  uint64_t* full = reinterpret_cast<uint64_t*>(pieces + 8 * PIECE_BYTES);
+  uint8_t* pieces = sB + STAGES * B_BYTES;       // 16 x 4 KB, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(pieces + EPI_WARPS * PIECE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -74,7 +82,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], EPI_WARPS);  // one arrival per epilogue warp
     }
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
@@ -160,56 +168,65 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3, half = (warp - 2) >> 2;
+    const int quad = warp & 3, group = (warp - 2) >> 2;   // TMEM lane quadrant, 64-column group
     uint8_t* buf = pieces + (warp - 2) * PIECE_BYTES;
-    uint8_t* mine = buf + lane * 64;
-    const uint32_t phase64 = (lane >> 1) & 3;    // 64-byte swizzle phase of this row
+    uint8_t* row_base = buf + lane * 128;
     int k = 0;
     for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++k) {
       const int mb = t / p.n_tiles, nb = t % p.n_tiles, b = k & 1;
+      const int64_t row0 = (int64_t)mb * BM + quad * 32;
+      const int64_t col0 = (int64_t)nb * BN + group * 64;
+      // lane j holds the bias of columns col0 + j and col0 + 32 + j (loaded while the
+      // tile's MMAs run); every lane takes column i's by shuffle
+      const float bj0 = (p.bias && col0 + lane < p.n) ? bf16_bits_to_f32(p.bias[col0 + lane]) : 0.f;
+      const float bj1 = (p.bias && col0 + 32 + lane < p.n) ? bf16_bits_to_f32(p.bias[col0 + 32 + lane]) : 0.f;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (k >> 1) & 1, abort_flag))) break;
       tc_fence_after();
-      const int64_t row0 = (int64_t)mb * BM + quad * 32;
-      const int64_t col0 = (int64_t)nb * BN + half * 128;
-      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + b * BN + half * 128;
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + b * BN + group * 64;
       const bool live = row0 < p.rows && col0 < p.n;   // warp-uniform
-#pragma unroll 1
-      for (int piece = 0; piece < 4; ++piece) {
+      if (live) {
+        if (lane == 0) bulk_wait_group_read<0>();  // the previous tile's store has left the buffer
+        __syncwarp();
+      }
+#pragma unroll
+      for (int sub = 0; sub < 2; ++sub) {            // 32 columns at a time
         uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + piece * 32, r);
+        tmem_ld_32x32b_x32(taddr + sub * 32, r);
         tmem_ld_wait();
         if (!live) continue;
-        // lane j holds the bias of the piece's column j; every lane takes column i's by shuffle
-        const int64_t colj = col0 + piece * 32 + lane;
-        const float bj = (p.bias && colj < p.n) ? bf16_bits_to_f32(p.bias[colj]) : 0.f;
-        uint4 out[4];
+        const float bj = sub ? bj1 : bj0;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float v[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int64_t col = col0 + piece * 32 + c * 8 + i;
-            const float bias = __shfl_sync(0xffffffffu, bj, c * 8 + i);
-            float x = round_bf16(__uint_as_float(r[c * 8 + i]) + bias);
-            if (col < p.n_sig) x = round_bf16(sigmoid_f(x));
-            v[i] = x;
-          }
-          out[c] = pack_exact8(v);
-        }
-        if (lane == 0) bulk_wait_group_read<0>();  // the previous piece has left the buffer
-        __syncwarp();
+          for (int i = 0; i < 8; ++i)
+            v[i] = __uint_as_float(r[c * 8 + i]) + __shfl_sync(0xffffffffu, bj, c * 8 + i);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(mine + ((c ^ phase64) << 4)) = out[c];
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&ty, buf, (int)(col0 + piece * 32), (int)row0);
-          bulk_commit_group();
+          for (int i = 0; i < 8; i += 2) round_bf16_pair(v[i], v[i + 1]);   // the Linear's bf16 output
+          const int64_t c8 = col0 + sub * 32 + c * 8;
+          if (c8 + 8 <= p.n_sig) {                   // all eight columns gated
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = sigmoid_f(v[i]);
+          } else if (c8 < p.n_sig) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              if (c8 + i < p.n_sig) v[i] = sigmoid_f(v[i]);
+          }
+          const uint32_t chunk = sub * 4 + c;        // 16-byte chunk within the 128-byte row
+          *reinterpret_cast<uint4*>(row_base + ((chunk ^ (lane & 7)) << 4)) = pack8(v);   // rounds to bf16
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (live) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&ty, buf, (int)col0, (int)row0);
+          bulk_commit_group();
+        }
+      }
     }
     if (lane == 0) bulk_wait_group<0>();  // every store written before the CTA exits
   }
@@ -256,10 +273,8 @@ extern "C" int vdn_gate_gemm(const void* x, int64_t ldx, const void* w, int64_t 
   {
     cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)ldy * 2};
-    cuuint32_t box[2] = {32, 32};
-    if (int rc = encode_map_swizzle(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box,
-                                    CU_TENSOR_MAP_SWIZZLE_64B))
-      return rc;
+    cuuint32_t box[2] = {64, 32};
+    if (int rc = encode_map(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box)) return rc;
   }
   Params p;
   p.bias = static_cast<const uint16_t*>(bias);

@@ -1,15 +1,16 @@
 // Tensor-core (tcgen05, kind::f16 bf16 -> fp32 in TMEM) VDA stages for d = 128.
 //
-// statistics  one CTA (256 threads) per (frame, head).  Raw k / v are streamed in
-//             32-token chunks by TMA (4D tensor maps: d, token, head, frame; tokens
-//             past S read as zero) into a 3-stage ring.  Eight threads per token
-//             apply the features (SiLU, L2 over d, the eager bf16 rounding points)
-//             and beta, and write four MN-major 128B-swizzled operands into one of
-//             two operand buffers: kf, khi, klo = exact bf16 split of the fp32
-//             product kf*beta (16 significant bits), vb = bf16(vf*beta).  One thread
-//             then issues A += khi.kf^T + klo.kf^T and B += vb.kf^T (M = N = 128,
-//             K = 16 tokens per MMA).  Epilogue: warps 0-3 read A, warps 4-7 read B
-//             from TMEM; A is symmetrised through shared memory, B rounded to bf16.
+// statistics  persistent, one CTA per SM walking (frame, head) items.  Raw k / v
+//             are streamed in 32-token chunks by TMA (4D tensor maps: d, token,
+//             head, frame; tokens past S read as zero) into a ring of stages.
+//             Sixteen threads per token apply the features (SiLU, L2 over d, the
+//             eager bf16 rounding points) and beta, and write four MN-major
+//             128B-swizzled operands in place: kf, khi + klo = the exact bf16 split
+//             of the fp32 product kf*beta (16 significant bits), vb = bf16(vf*beta).
+//             One thread then issues A2 += khi.kf^T + klo.kf^T + kf.khi^T + kf.klo^T
+//             (twice the symmetrised A, accumulated on the tensor cores) and
+//             B += vb.kf^T (M = N = 128, K = 16 tokens per MMA).  Epilogue: A = A2 / 2
+//             and B rounded to bf16, straight from TMEM.
 // readout     one CTA (128 threads, two per SM) per (frame, head).  The gathered bf16
 //             state [v][k] is the K-major B operand; 128-token q tiles arrive by TMA
 //             (2 stages), each thread turns its row into features in place, and one
@@ -49,28 +50,33 @@ __device__ __forceinline__ bool bar_and(uint32_t id, uint32_t count, bool pred) 
   return out != 0;
 }
 
-// x * sigmoid(x) with the fast exponential and divide (two MUFU operations).
+// x * sigmoid(x) with the fast exponential and divide (two MUFU operations).  The
+// reciprocal on the FMA pipe instead (sigmoid_nr) measured slower here (statistics
+// 0.37 -> 0.45 ms, readout 0.26 -> 0.33 ms): these transforms are bound by issue, not by
+// the MUFU pipe.
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // ------------------------------------------------------------------ statistics
 // Persistent, warp-specialised: grid = min(F*H, SMs), one CTA per SM walking
 // (frame, head) items.  Warp 0 lane 0 streams 32-token raw k / v chunks by TMA
-// into a 4-stage ring; warps 2-17 (16 threads per token, one 8-element chunk of
+// into a 6-stage ring; warps 2-17 (16 threads per token, one 8-element chunk of
 // k and of v each) apply features and beta and write kf / vb in place plus the
-// khi / klo split; warp 1 lane 0 issues A += khi.kf^T + klo.kf^T and
-// B += vb.kf^T into one of two TMEM accumulator pairs (512 columns); warps
-// 18-21 drain an item's A (symmetrised through shared memory) and B
-// (bf16-rounded) while the next item streams.  The transform is the kernel's
-// critical stage (MUFU-heavy SiLU), hence its sixteen warps.
+// khi / klo split; warp 1 lane 0 issues A2 += khi.kf^T + klo.kf^T + kf.khi^T +
+// kf.klo^T and B += vb.kf^T into one of two TMEM accumulator pairs (512 columns);
+// warps 18-21 drain an item's A = A2 / 2 and B (bf16-rounded) while the next item
+// streams.  A stage is held from its TMA load until its MMAs complete, and the
+// load alone takes ~3.2k cycles, so the ring depth sets the chunk rate: the
+// symmetrisation moved onto the tensor cores to free the 66 KB transpose buffer
+// for two more stages.
 constexpr int ST_CH = 32;                       // tokens per chunk
-constexpr int ST_STAGES = 4;
+constexpr int ST_STAGES = 6;
 constexpr int ST_REGION = ST_CH * 128;          // 4 KB: 32 rows x 128 B
 constexpr int ST_STAGE_BYTES = 8 * ST_REGION;   // k(kf), v(vb), khi, klo: 2 regions each
 constexpr int ST_RAW_BYTES = 4 * ST_REGION;     // what TMA writes per stage
-constexpr int ST_THREADS = 704;             // 2 + 16 transform + 4 epilogue warps
-constexpr int ST_TRANS_BYTES = 128 * 129 * 4;
+constexpr int ST_THREADS = 736;             // 2 + 16 transform + 4 epilogue + 1 beta warps
 constexpr int ST_NBAR = 3 * ST_STAGES + 2 * 2 + 1;
-constexpr size_t ST_SMEM = 1024 + ST_STAGES * ST_STAGE_BYTES + ST_TRANS_BYTES + ST_NBAR * 8 + 64;
+constexpr size_t ST_SMEM = 1024 + ST_STAGES * ST_STAGE_BYTES + ST_STAGES * ST_CH * 4 + ST_NBAR * 8 + 64;
+static_assert(ST_SMEM <= 232448, "shared memory per CTA");
 
 struct StatsParams {
   const uint16_t* beta;
@@ -88,8 +94,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
-  float* trans = reinterpret_cast<float*>(smem + ST_STAGES * ST_STAGE_BYTES);   // [128][129]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST_STAGES * ST_STAGE_BYTES + ST_TRANS_BYTES);
+  float* beta_s = reinterpret_cast<float*>(smem + ST_STAGES * ST_STAGE_BYTES);  // [stage][token]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(beta_s + ST_STAGES * ST_CH);
   uint64_t* full = bars;
   uint64_t* ready = full + ST_STAGES;
   uint64_t* empty = ready + ST_STAGES;
@@ -104,7 +110,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 
   if (tid == 0) {
     for (int s = 0; s < ST_STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);    // the producer (with the TMA bytes) and the beta warp
       mbar_init(&ready[s], 16);  // one arrival per transform warp
       mbar_init(&empty[s], 1);
     }
@@ -182,6 +188,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             const uint32_t acc = (c | ks) != 0;
             mma_bf16(acc_a, dhi, dkf, kIdesc, acc);
             mma_bf16(acc_a, dlo, dkf, kIdesc, 1);
+            mma_bf16(acc_a, dkf, dhi, kIdesc, 1);
+            mma_bf16(acc_a, dkf, dlo, kIdesc, 1);
             mma_bf16(acc_b, dvb, dkf, kIdesc, acc);
           }
           issued = true;
@@ -203,21 +211,16 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     const uint32_t row = t >> 4, e = t & 15, r = e >> 3, cc = e & 7;
     int g = 0;
     for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
-      const int f = item / p.H, h = item % p.H;
-      auto load_beta = [&](int c) -> float {
-        const int s = c * ST_CH + (int)row;
-        return s < p.S ? bf16_bits_to_f32(p.beta[(int64_t)f * p.b_sf + (int64_t)s * p.b_ss + (int64_t)h * p.b_sh])
-                       : 0.f;
-      };
       // One chunk: features, beta and the khi / klo split, in place in its stage.
       // Returns false when a wait gave up.
-      auto chunk = [&](float bt) -> bool {
+      auto chunk = [&]() -> bool {
         const int s = g % ST_STAGES;
         // Warp-uniform outcome: the warp's lanes meet again at the __syncwarp below.
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (g / ST_STAGES) & 1, abort_flag))) {
           return false;
         }
         uint8_t* st = stages + s * ST_STAGE_BYTES;
+        const float bt = beta_s[s * ST_CH + row];
         const uint32_t off = r * ST_REGION + swz(row, cc);
         float kv[8], vv[8];
         unpack8(*reinterpret_cast<const uint4*>(st + off), kv);
@@ -270,28 +273,31 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         ++g;
         return true;
       };
-      // beta of the next four chunks stays in four registers (each refilled four
-      // chunks ahead), so its global load latency hides behind four chunks of work
-      // (with one chunk of lead the load latency bounded the chunk rate).
-      float bq0 = load_beta(0), bq1 = nch > 1 ? load_beta(1) : 0.f;
-      float bq2 = nch > 2 ? load_beta(2) : 0.f, bq3 = nch > 3 ? load_beta(3) : 0.f;
       bool ok = true;
-      for (int c = 0; c < nch && ok; c += 4) {
-        float bt = bq0;
-        if (c + 4 < nch) bq0 = load_beta(c + 4);
-        ok = chunk(bt);
-        if (!ok || c + 1 >= nch) break;
-        bt = bq1;
-        if (c + 5 < nch) bq1 = load_beta(c + 5);
-        ok = chunk(bt);
-        if (!ok || c + 2 >= nch) break;
-        bt = bq2;
-        if (c + 6 < nch) bq2 = load_beta(c + 6);
-        ok = chunk(bt);
-        if (!ok || c + 3 >= nch) break;
-        bt = bq3;
-        if (c + 7 < nch) bq3 = load_beta(c + 7);
-        ok = chunk(bt);
+      for (int c = 0; c < nch && ok; ++c) ok = chunk();
+      if (!ok) break;
+    }
+  } else if (warp == 22) {
+    // ---------------------------------------------------------------- beta
+    // One lane per token: beta of a stage's 32 tokens into shared memory as soon as
+    // the stage is free (alongside the producer's k / v copies), then one arrival on
+    // the stage's full barrier.  The transform warps read it from there, so no global
+    // load sits in their loop.
+    int g = 0;
+    for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x) {
+      const int f = item / p.H, h = item % p.H;
+      const uint16_t* bcol = p.beta + (int64_t)f * p.b_sf + (int64_t)h * p.b_sh;
+      bool ok = true;
+      for (int c = 0; c < nch; ++c, ++g) {
+        const int s = g % ST_STAGES;
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ((g / ST_STAGES) & 1) ^ 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const int tok = c * ST_CH + lane;
+        beta_s[s * ST_CH + lane] = tok < p.S ? bf16_bits_to_f32(bcol[(int64_t)tok * p.b_ss]) : 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
       }
       if (!ok) break;
     }
@@ -305,6 +311,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       if (!bar_and(1, 128, mbar_wait(&acc_full[b], (k >> 1) & 1, abort_flag))) break;
       tc_fence_after();
       const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + b * 256;
+      float* a_out = p.A + ((int64_t)item * 128 + mrow) * 128;
       float* b_out = p.B + ((int64_t)item * 128 + mrow) * 128;
 #pragma unroll 1
       for (int cb = 0; cb < 4; ++cb) {
@@ -313,27 +320,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         tmem_ld_32x32b_x32(lane_base + 128 + cb * 32, vb);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) trans[mrow * 129 + cb * 32 + i] = __uint_as_float(va[i]);
-#pragma unroll
-        for (int i = 0; i < 32; i += 4)
+        for (int i = 0; i < 32; i += 4) {
+          *reinterpret_cast<float4*>(a_out + cb * 32 + i) =
+              make_float4(0.5f * __uint_as_float(va[i]), 0.5f * __uint_as_float(va[i + 1]),
+                          0.5f * __uint_as_float(va[i + 2]), 0.5f * __uint_as_float(va[i + 3]));
           *reinterpret_cast<float4*>(b_out + cb * 32 + i) =
               make_float4(round_bf16(__uint_as_float(vb[i])), round_bf16(__uint_as_float(vb[i + 1])),
                           round_bf16(__uint_as_float(vb[i + 2])), round_bf16(__uint_as_float(vb[i + 3])));
+        }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);                 // TMEM pair b may be refilled
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      float* a_out = p.A + ((int64_t)item * 128 + mrow) * 128;
-#pragma unroll 4
-      for (int cidx = 0; cidx < 128; cidx += 4) {
-        float4 o;
-        o.x = 0.5f * (trans[mrow * 129 + cidx] + trans[cidx * 129 + mrow]);
-        o.y = 0.5f * (trans[mrow * 129 + cidx + 1] + trans[(cidx + 1) * 129 + mrow]);
-        o.z = 0.5f * (trans[mrow * 129 + cidx + 2] + trans[(cidx + 2) * 129 + mrow]);
-        o.w = 0.5f * (trans[mrow * 129 + cidx + 3] + trans[(cidx + 3) * 129 + mrow]);
-        *reinterpret_cast<float4*>(a_out + cidx) = o;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // trans is free for the next item
     }
   }
   tc_fence_before();
