@@ -125,11 +125,11 @@ class ClockSampler:
 # (x 21 / 5).  Reported as roofline "traffic" with "traffic_source" saying so.
 NCU_TRAFFIC_BYTES = {
     "mxfp8_gemm_qkv": (104.2e6 + 97.6e6) * 32760 / 4096,
-    "statistics": 674.4e6 + 89.9e6,
-    "factors": None,
-    "scan": None,
-    "gather": 100.1e6 + 8.3e6,
-    "readout": 698.8e6 + 297.0e6,
+    "statistics": 167.2e6 * 21 / 5,
+    "factors": 13.2e6 * 21 / 5,
+    "scan": 32.9e6 * 21 / 5,
+    "gather": 15.8e6 * 21 / 5,
+    "readout": 213.6e6 * 21 / 5,
 }
 
 TRAFFIC_SOURCE = ("from a separate ncu capture of a small case of this kernel (profiles/), scaled to "
@@ -254,7 +254,9 @@ def bench_vda(args, torch, dist, rank, world):
 
     # Per-kernel device times of the five stage launches (same stream), on the regions of
     # the forward's own workspace (d = 128: A then the forward bank over it, B, the split
-    # inverses, the reverse bank, the gathered state).
+    # inverses, the reverse bank, the gathered state).  The scan is timed in the bf16-B
+    # form the forward runs (the statistics stage API writes fp32 B, so its bytes feed the
+    # scan as arbitrary bf16 values here: timing only).
     plane = F * H * d * d
     up = lambda b: (b + 255) // 256 * 256
     A = ws[: plane * 4].view(torch.float32)
@@ -270,7 +272,7 @@ def bench_vda(args, torch, dist, rank, world):
                                          S * beta.stride(0), beta.stride(0), beta.stride(1), 0, F, S, H,
                                          d, _lib.ptr(A), _lib.ptr(B), st)),
         ("factors", lambda: _lib.call("vdn_vda_factor_inverse", _lib.ptr(A), F * H, _lib.ptr(planes), st)),
-        ("scan", lambda: _lib.call("vdn_vda_scan_tc", _lib.ptr(planes), _lib.ptr(B), _lib.ptr(alpha), None, F, H,
+        ("scan", lambda: _lib.call("vdn_vda_scan_tc_bf16", _lib.ptr(planes), _lib.ptr(B), _lib.ptr(alpha), None, F, H,
                                    _lib.ptr(pre), _lib.ptr(suf), None, st)),
         ("gather", lambda: _lib.call("vdn_vda_gather", _lib.ptr(pre), _lib.ptr(suf), _lib.ptr(alpha), buf,
                                      None, 1, F, H, d, _lib.ptr(state), _lib.DTYPE_BF16, st)),

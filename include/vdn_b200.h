@@ -328,6 +328,11 @@ int vdn_vda_readout(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh,
 int vdn_vda_factor_inverse(const float* A, int64_t n, void* planes, cudaStream_t stream);
 int vdn_vda_scan_tc(const void* planes, const float* B, const float* alpha, const float* seed, int F, int H,
                     float* prefix, float* suffix, int* status, cudaStream_t stream);
+/* vdn_vda_scan_tc with B in bf16 [F, H, 128, 128] (the values the statistics produce are
+ * bf16 already): B_f reaches the kernel by TMA instead of per-thread loads.  The form
+ * vdn_vda_forward uses for d = 128. */
+int vdn_vda_scan_tc_bf16(const void* planes, const void* B, const float* alpha, const float* seed, int F,
+                         int H, float* prefix, float* suffix, int* status, cudaStream_t stream);
 
 /* Workspace bytes vdn_vda_forward needs for this geometry. */
 size_t vdn_vda_workspace_size(int F, int S, int H, int d);

@@ -82,8 +82,7 @@ def test_block_config3_stages_full_size(cuda, config3):
     qkv = torch.empty(T, 3 * hd, device=cuda, dtype=torch.bfloat16)
     block._gemm(q1, s1, block.qkv, T, qkv, bias=block.qkv.bias)
     g3 = block._gate_projections(y1)
-    og = block.output_gate
-    lgate = torch.sigmoid(F.linear(g3[:, 2 * H:], og.up.weight, og.up.bias))
+    lgate = block._linear_gate(g3[:, 2 * H:])
     q, k, v = (qkv[:, i * hd:(i + 1) * hd].view(T, H, d) for i in range(3))
     att = torch.empty(T, H, d, device=cuda, dtype=torch.bfloat16)
     window_softmax(q, k, v, g3[:, :H], frames, tokens, cfg.radius, out=att)

@@ -318,6 +318,25 @@ def test_scan_tc_vs_fp64(cuda, frames, text, decay):
     torch.testing.assert_close(suffix.double().cpu(), torch.from_numpy(osf), atol=3e-6, rtol=3e-5)
 
 
+@pytest.mark.parametrize("frames,heads,text", [(21, 4, False), (3, 1, True), (70, 2, False)])
+def test_scan_tc_bf16_b_equals_fp32_b(cuda, frames, heads, text):
+    """B in bf16 (staged by TMA, the forward's form) gives exactly the banks of the fp32-B
+    path fed the same bf16 values (the statistics produce bf16-valued B either way)."""
+    from vdn_b200.linear_attention import vda_factor_inverse, vda_scan_tc
+    g = torch.Generator().manual_seed(frames * 7 + heads)
+    k = F.normalize(torch.randn(frames, heads, 16, 128, generator=g), dim=-1)
+    a = (k.transpose(-1, -2) @ k).contiguous()
+    b = (torch.randn(a.shape, generator=g) * 0.1).bfloat16()
+    alpha = torch.rand(frames, heads, 128, generator=g) * 0.2 + 0.8
+    seed = torch.randn(heads, 128, 128, generator=g) * .3 if text else None
+    planes = vda_factor_inverse(a.to(cuda))
+    s = None if seed is None else seed.to(cuda)
+    p32, s32 = vda_scan_tc(planes, b.float().to(cuda), alpha.to(cuda), s)
+    p16, s16 = vda_scan_tc(planes, b.to(cuda), alpha.to(cuda), s)
+    torch.cuda.synchronize()
+    assert torch.equal(p16, p32) and torch.equal(s16, s32)
+
+
 @pytest.mark.parametrize("heads", [1, 5, 40, 80])
 def test_scan_tc_head_counts_and_long_recurrence(cuda, heads):
     """Every head count (one CTA per head and direction: 2 to 160 CTAs) and a long

@@ -67,6 +67,7 @@ SIGNATURES = {
                                _i32, _i32, _p, _p]),
     "vdn_vda_factor_inverse": (_i32, [_p, _i64, _p, _p]),
     "vdn_vda_scan_tc": (_i32, [_p, _p, _p, _p, _i32, _i32, _p, _p, _p, _p]),
+    "vdn_vda_scan_tc_bf16": (_i32, [_p, _p, _p, _p, _i32, _i32, _p, _p, _p, _p]),
     "vdn_vda_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
     "vdn_vda_forward": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _f32,
                                _p, _p, _i32, _i32, _i32, _i32, _i32, _p, _p, _sz, _p]),

@@ -575,7 +575,7 @@ bool tc_stats_supported(int d, const void* k, int64_t k_sf, int64_t k_ss, int64_
 int launch_stats_tc(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sf,
                     int64_t v_ss, int64_t v_sh, const void* beta, int64_t b_sf, int64_t b_ss,
                     int64_t b_sh, int features_applied, int F, int S, int H, float* A, float* B,
-                    int* status, cudaStream_t stream);
+                    int b_bf16, int* status, cudaStream_t stream);
 bool tc_readout_supported(int d, const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh,
                           const void* state, const void* gate, int64_t g_sf, int64_t g_ss, int64_t g_sh,
                           const void* out);
@@ -616,7 +616,7 @@ int launch_stats(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, const 
   VDN_CHECK_ARG(k && v && beta && A && B, "null pointer");
   if (tc_stats_supported(d, k, k_sf, k_ss, k_sh, v, v_sf, v_ss, v_sh))
     return launch_stats_tc(k, k_sf, k_ss, k_sh, v, v_sf, v_ss, v_sh, beta, b_sf, b_ss, b_sh,
-                           features_applied, F, S, H, A, B, nullptr, stream);
+                           features_applied, F, S, H, A, B, 0, nullptr, stream);
   const size_t smem = std::max<size_t>(3 * 32 * d, (size_t)d * d) * sizeof(float);
   const auto* kp = static_cast<const uint16_t*>(k);
   const auto* vp = static_cast<const uint16_t*>(v);
@@ -668,8 +668,8 @@ int launch_factor_split(const float* A, int64_t n, void* planes, cudaStream_t st
   return VDN_OK;
 }
 
-int launch_scan_tc(const void* inv_planes, const float* B, const float* alpha, const float* seed, int F,
-                   int H, float* prefix, float* suffix, int* status, cudaStream_t stream);
+int launch_scan_tc(const void* inv_planes, const float* B, int b_bf16, const float* alpha, const float* seed,
+                   int F, int H, float* prefix, float* suffix, int* status, cudaStream_t stream);
 
 int launch_scan(const float* T, const float* J, const float* seed, int F, int H, int d,
                 float* prefix, float* suffix, cudaStream_t stream) {
@@ -845,7 +845,13 @@ int vdn_vda_factor_inverse(const float* A, int64_t n, void* planes, cudaStream_t
 
 int vdn_vda_scan_tc(const void* planes, const float* B, const float* alpha, const float* seed, int F, int H,
                     float* prefix, float* suffix, int* status, cudaStream_t stream) {
-  return launch_scan_tc(planes, B, alpha, seed, F, H, prefix, suffix, status, stream);
+  return launch_scan_tc(planes, B, 0, alpha, seed, F, H, prefix, suffix, status, stream);
+}
+
+int vdn_vda_scan_tc_bf16(const void* planes, const void* B, const float* alpha, const float* seed, int F,
+                         int H, float* prefix, float* suffix, int* status, cudaStream_t stream) {
+  return launch_scan_tc(planes, static_cast<const float*>(B), 1, alpha, seed, F, H, prefix, suffix, status,
+                        stream);
 }
 
 size_t vdn_vda_workspace_size(int F, int S, int H, int d) {
@@ -871,13 +877,22 @@ int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss,
   float *A = w.A, *B = w.B, *prefix = w.prefix, *suffix = w.suffix;
   void* state = w.state;
   const int64_t sf = (int64_t)S * qkv_ss;
-  if (int rc = launch_stats(k, sf, qkv_ss, qkv_sh, v, sf, qkv_ss, qkv_sh, beta, (int64_t)S * b_ss,
-                            b_ss, b_sh, 0, F, S, H, d, A, B, stream))
+  // d = 128 with the tensor-core statistics: B leaves the statistics in bf16 (its values
+  // are bf16 either way) and reaches the scan by TMA.
+  const int b_bf16 = d == 128 && tc_stats_supported(d, k, sf, qkv_ss, qkv_sh, v, sf, qkv_ss, qkv_sh);
+  if (b_bf16) {
+    if (int rc = launch_stats_tc(k, sf, qkv_ss, qkv_sh, v, sf, qkv_ss, qkv_sh, beta, (int64_t)S * b_ss, b_ss, b_sh,
+                                 0, F, S, H, A, B, 1, nullptr, stream))
+      return rc;
+  } else if (int rc = launch_stats(k, sf, qkv_ss, qkv_sh, v, sf, qkv_ss, qkv_sh, beta, (int64_t)S * b_ss,
+                                   b_ss, b_sh, 0, F, S, H, d, A, B, stream)) {
     return rc;
+  }
   if (d == 128) {  // inverse only, then the tensor-core scan folds alpha and B into each step
     VDN_CHECK_ARG(aligned16(alpha) && (!seed || aligned16(seed)), "alpha and seed must be 16-byte aligned");
     if (int rc = launch_factor_split(A, (int64_t)F * H, w.planes, stream)) return rc;
-    if (int rc = launch_scan_tc(w.planes, B, alpha, seed, F, H, prefix, suffix, nullptr, stream)) return rc;
+    if (int rc = launch_scan_tc(w.planes, B, b_bf16, alpha, seed, F, H, prefix, suffix, nullptr, stream))
+      return rc;
   } else {
     if (int rc = launch_factors(A, B, alpha, (int64_t)F * H, d, A, B, stream)) return rc;
     if (int rc = launch_scan(A, B, seed, F, H, d, prefix, suffix, stream)) return rc;

@@ -20,11 +20,19 @@
 //                   in shared memory at the start, B requested before the wait for
 //                   the product) and write its three bf16 parts into the A operand
 //                   (128B-swizzled, K-major)
-// The copy of inverse f+1 lands while the rows of step f are formed.  Every wait
+// The copy of inverse f+1 lands while the rows of step f are formed.  With B in bf16
+// (the forward: the statistics round B to bf16 anyway) B_f arrives by TMA as a
+// 128B-swizzled 32 KB tile while the previous product runs, instead of 32 row-per-thread
+// loads per thread (whose 32-row access pattern, with L1 squeezed by the shared-memory
+// carve-out, kept the load queue throttled); alpha is then read from global (every lane
+// of a warp reads the same alpha values).  Every wait
 // is bounded (2 s); a timeout aborts all roles, lets copies and MMAs in flight
 // finish, frees TMEM and reports VDN_ERR_TIMEOUT through `status`.
 #include "common.cuh"
 #include "sm100.cuh"
+#include "tma_host.cuh"
+
+#include <cstring>
 
 namespace vdn {
 namespace vscan {
@@ -38,10 +46,13 @@ constexpr int ROW_WARPS = 16;               // four warps per TMEM lane quadrant
 constexpr int THREADS = 64 + 32 * ROW_WARPS;  // warp 0 producer, warp 1 MMA, warps 2-17 rows
 constexpr int ALPHA_FRAMES = 64;            // alpha of up to this many frames staged in shared memory
 constexpr size_t SMEM = 1024 + 2 * OPER + ALPHA_FRAMES * D * 4 + 256;
+constexpr int BTILE = D * D * 2;            // bf16 B_f: two 64-column halves of 128 rows x 128 B
+constexpr size_t SMEM_BH = 1024 + 2 * OPER + BTILE + 256;
+static_assert(SMEM <= 232448 && SMEM_BH <= 232448, "shared memory per CTA");
 
 struct Params {
   const uint8_t* inv;      // [F, H] split inverses, OPER bytes each
-  const float* B;          // [F, H, d, d] fp32 (B of the statistics)
+  const float* B;          // [F, H, d, d] fp32 (B of the statistics); unused on the bf16 path
   const float* alpha;      // [F, H, d] fp32
   const float* seed;       // [H, d, d] or null
   float* prefix;           // [F, H, d, d] forward states
@@ -56,19 +67,26 @@ __device__ __forceinline__ uint32_t oper_off(uint32_t r, uint32_t c) {
   return (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
 }
 
-__global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
+// BH: B_f in bf16 through a tensor map (tb: [F*H*128 rows, 128 cols], 64 x 128 boxes,
+// 128B swizzle), staged in shared memory by TMA.
+template <bool BH>
+__global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_constant__ CUtensorMap tb,
+                                                             const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sX = smem;                        // A operand: X_f parts
   uint8_t* sI = smem + OPER;                 // B operand: inv_f parts
-  float* sAlpha = reinterpret_cast<float*>(smem + 2 * OPER);   // [F][D] when F <= ALPHA_FRAMES
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * OPER + ALPHA_FRAMES * D * 4);
+  uint8_t* sB = smem + 2 * OPER;             // BH: B_f tile
+  float* sAlpha = reinterpret_cast<float*>(smem + 2 * OPER);   // !BH: [F][D] when F <= ALPHA_FRAMES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * OPER + (BH ? BTILE : ALPHA_FRAMES * D * 4));
   uint64_t* inv_full = bars;
   uint64_t* inv_empty = bars + 1;
   uint64_t* x_ready = bars + 2;
   uint64_t* acc_full = bars + 3;
   uint64_t* mma_drain = bars + 4;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 5);
+  uint64_t* b_full = bars + 5;
+  uint64_t* b_empty = bars + 6;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -79,13 +97,16 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
   if (tid == 0) {
     mbar_init(inv_full, 1);
     mbar_init(inv_empty, 1);
-    mbar_init(x_ready, 32 * ROW_WARPS);
+    mbar_init(x_ready, ROW_WARPS);  // one arrival per row warp
     mbar_init(acc_full, 1);
     mbar_init(mma_drain, 1);
+    mbar_init(b_full, 1);
+    mbar_init(b_empty, ROW_WARPS);  // one arrival per row warp once it has read B_f
     *abort_flag = 0;
     fence_barrier_init();
+    if (BH) prefetch_tensormap(&tb);
   }
-  const bool alpha_smem = F <= ALPHA_FRAMES;
+  const bool alpha_smem = !BH && F <= ALPHA_FRAMES;
   if (alpha_smem)
     for (int i = tid; i < F * D / 4; i += THREADS)
       reinterpret_cast<float4*>(sAlpha)[i] =
@@ -99,8 +120,16 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------- producer
-      int issued = 0;
+      int issued = 0, b_issued = 0;
       for (int step = 0; step < F && !*abort_flag; ++step) {
+        if (BH) {  // B_f as soon as the rows have read B_{f-1} (while the previous product runs)
+          if (!mbar_wait(b_empty, (step & 1) ^ 1, abort_flag)) break;
+          mbar_arrive_expect_tx(b_full, BTILE);
+          const int brow = (frame(step) * H + h) * D;
+          tma_load_2d(sB, &tb, b_full, 0, brow);
+          tma_load_2d(sB + BTILE / 2, &tb, b_full, 64, brow);
+          ++b_issued;
+        }
         if (!mbar_wait(inv_empty, (step & 1) ^ 1, abort_flag)) break;
         const uint8_t* src = p.inv + ((int64_t)frame(step) * H + h) * OPER;
         mbar_arrive_expect_tx(inv_full, OPER);
@@ -114,6 +143,11 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
       if (*abort_flag && issued) {  // the last copy must land before the CTA may exit
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(inv_full, (issued - 1) & 1) && globaltimer() - t0 < kWaitLimitNs) {
+        }
+      }
+      if (*abort_flag && b_issued) {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(b_full, (b_issued - 1) & 1) && globaltimer() - t0 < kWaitLimitNs) {
         }
       }
     }
@@ -182,7 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
     for (int step = 0; step <= F; ++step) {
       const int fr = frame(step < F ? step : F - 1);
       float4 bq[QC / 4];
-      if (step < F) {
+      if (!BH && step < F) {
         const float4* b4 = reinterpret_cast<const float4*>(p.B + (((int64_t)fr * H + h) * D + row) * D + col0);
 #pragma unroll
         for (int i = 0; i < QC / 4; ++i) bq[i] = b4[i];
@@ -204,6 +238,21 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
         for (int i = 0; i < QC / 4; ++i) dst[i] = make_uint4(prev[4 * i], prev[4 * i + 1], prev[4 * i + 2], prev[4 * i + 3]);
       }
       if (step == F) break;
+      if (BH) {  // this thread's 32 values of B_f's row from the staged tile
+        if (!__all_sync(0xffffffffu, mbar_wait(b_full, step & 1, abort_flag))) break;
+#pragma unroll
+        for (int j = 0; j < QC / 8; ++j) {
+          const int chunk = col0 / 8 + j;    // 16-byte chunk of the row (8 bf16)
+          const uint4 w = *reinterpret_cast<const uint4*>(sB + (chunk >> 3) * (BTILE / 2) + row * 128 +
+                                                          (((chunk & 7) ^ (row & 7)) << 4));
+          float f8[8];
+          unpack8(w, f8);
+          bq[2 * j] = make_float4(f8[0], f8[1], f8[2], f8[3]);
+          bq[2 * j + 1] = make_float4(f8[4], f8[5], f8[6], f8[7]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(b_empty);
+      }
       // X = P diag(alpha_f) + B_f, split into three bf16 parts in the A operand.
       const float* al = alpha_smem ? sAlpha + fr * D + col0 : p.alpha + ((int64_t)fr * H + h) * D + col0;
 #pragma unroll
@@ -227,7 +276,8 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
           *reinterpret_cast<uint4*>(sX + part * PLANE + off) = make_uint4(w[part][0], w[part][1], w[part][2], w[part][3]);
       }
       fence_proxy_async_smem();
-      mbar_arrive(x_ready);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(x_ready);
     }
   }
 
@@ -241,23 +291,41 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const Params p) {
   if (tid == 0 && *abort_flag && p.status) atomicExch(p.status, VDN_ERR_TIMEOUT);
 }
 
+
 }  // namespace vscan
 
-int launch_scan_tc(const void* inv_planes, const float* B, const float* alpha, const float* seed, int F,
-                   int H, float* prefix, float* suffix, int* status, cudaStream_t stream) {
+// B: fp32 [F, H, d, d]; or, with b_bf16, the same values in bf16 [F, H, d, d].
+int launch_scan_tc(const void* inv_planes, const float* B, int b_bf16, const float* alpha, const float* seed,
+                   int F, int H, float* prefix, float* suffix, int* status, cudaStream_t stream) {
   using namespace vscan;
   VDN_CHECK_ARG(F >= 1 && H >= 1, "positive F and H required");
   VDN_CHECK_ARG(inv_planes && B && alpha && prefix && suffix, "null pointer");
   VDN_CHECK_ARG(aligned16(inv_planes) && aligned16(B) && aligned16(alpha) && aligned16(prefix) &&
                     aligned16(suffix) && (!seed || aligned16(seed)),
                 "scan operands must be 16-byte aligned");
-  static bool attr_set = false;
-  if (!attr_set) {
-    VDN_CUDA_TRY(cudaFuncSetAttribute(scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM));
-    attr_set = true;
-  }
+  static bool attr_set[2] = {false, false};
   Params p{static_cast<const uint8_t*>(inv_planes), B, alpha, seed, prefix, suffix, F, H, status};
-  scan_tc_kernel<<<2 * H, THREADS, SMEM, stream>>>(p);
+  CUtensorMap tb;
+  if (b_bf16) {
+    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)F * H * D};
+    cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)D};
+    if (int rc = encode_map(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, dims, strides, box)) return rc;
+    if (!attr_set[1]) {
+      VDN_CUDA_TRY(cudaFuncSetAttribute(scan_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)SMEM_BH));
+      attr_set[1] = true;
+    }
+    scan_tc_kernel<true><<<2 * H, THREADS, SMEM_BH, stream>>>(tb, p);
+    VDN_LAUNCH_CHECK("vda scan (tcgen05, bf16 B)");
+    return VDN_OK;
+  }
+  std::memset(&tb, 0, sizeof(tb));
+  if (!attr_set[0]) {
+    VDN_CUDA_TRY(cudaFuncSetAttribute(scan_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM));
+    attr_set[0] = true;
+  }
+  scan_tc_kernel<false><<<2 * H, THREADS, SMEM, stream>>>(tb, p);
   VDN_LAUNCH_CHECK("vda scan (tcgen05)");
   return VDN_OK;
 }

@@ -82,7 +82,8 @@ struct StatsParams {
   const uint16_t* beta;
   int64_t b_sf, b_ss, b_sh;
   float* A;
-  float* B;
+  float* B;                // fp32 [items][128][128], or bf16 when b_bf16 (its values are bf16 either way)
+  int b_bf16;
   int S, H, items;
   int* status;
 };
@@ -313,6 +314,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + b * 256;
       float* a_out = p.A + ((int64_t)item * 128 + mrow) * 128;
       float* b_out = p.B + ((int64_t)item * 128 + mrow) * 128;
+      uint16_t* bh_out = reinterpret_cast<uint16_t*>(p.B) + ((int64_t)item * 128 + mrow) * 128;
 #pragma unroll 1
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t va[32], vb[32];
@@ -320,13 +322,24 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         tmem_ld_32x32b_x32(lane_base + 128 + cb * 32, vb);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
+        for (int i = 0; i < 32; i += 4)
           *reinterpret_cast<float4*>(a_out + cb * 32 + i) =
               make_float4(0.5f * __uint_as_float(va[i]), 0.5f * __uint_as_float(va[i + 1]),
                           0.5f * __uint_as_float(va[i + 2]), 0.5f * __uint_as_float(va[i + 3]));
-          *reinterpret_cast<float4*>(b_out + cb * 32 + i) =
-              make_float4(round_bf16(__uint_as_float(vb[i])), round_bf16(__uint_as_float(vb[i + 1])),
-                          round_bf16(__uint_as_float(vb[i + 2])), round_bf16(__uint_as_float(vb[i + 3])));
+        if (p.b_bf16) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float f8[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f8[j] = __uint_as_float(vb[i + j]);
+            *reinterpret_cast<uint4*>(bh_out + cb * 32 + i) = pack8(f8);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(b_out + cb * 32 + i) =
+                make_float4(round_bf16(__uint_as_float(vb[i])), round_bf16(__uint_as_float(vb[i + 1])),
+                            round_bf16(__uint_as_float(vb[i + 2])), round_bf16(__uint_as_float(vb[i + 3])));
         }
       }
       tc_fence_before();
@@ -687,12 +700,12 @@ bool tc_stats_supported(int d, const void* k, int64_t k_sf, int64_t k_ss, int64_
 int launch_stats_tc(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sf,
                     int64_t v_ss, int64_t v_sh, const void* beta, int64_t b_sf, int64_t b_ss,
                     int64_t b_sh, int features_applied, int F, int S, int H, float* A, float* B,
-                    int* status, cudaStream_t stream) {
+                    int b_bf16, int* status, cudaStream_t stream) {
   using namespace vtc;
   CUtensorMap mk, mv;
   if (int rc = map_tokens(&mk, k, k_sf, k_ss, k_sh, F, S, H, ST_CH)) return rc;
   if (int rc = map_tokens(&mv, v, v_sf, v_ss, v_sh, F, S, H, ST_CH)) return rc;
-  StatsParams p{static_cast<const uint16_t*>(beta), b_sf, b_ss, b_sh, A, B, S, H, F * H, status};
+  StatsParams p{static_cast<const uint16_t*>(beta), b_sf, b_ss, b_sh, A, B, b_bf16, S, H, F * H, status};
   int dev = 0, sms = 148;
   VDN_CUDA_TRY(cudaGetDevice(&dev));
   VDN_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

@@ -209,10 +209,12 @@ def split_inverse_values(planes):
 def vda_scan_tc(planes, B, alpha, seed=None):
     """Forward / reverse banks [F, H, 128, 128] fp32 from split inverses [F, H, 98304],
     B [F, H, 128, 128] and alpha [F, H, 128]: P_f = (P_{f-1} diag(alpha_f) + B_f) inv_f
-    on the tensor cores (the d = 128 scan of vda_forward)."""
+    on the tensor cores (the d = 128 scan of vda_forward).  B fp32, or bf16 (the form
+    the forward passes: B_f then reaches the kernel by TMA)."""
     f, h = B.shape[:2]
-    if B.shape != (f, h, 128, 128) or B.dtype != torch.float32 or planes.shape != (f, h, SPLIT_INVERSE_BYTES):
-        raise ValueError("B must be fp32 [F,H,128,128] and planes uint8 [F,H,98304]")
+    if (B.shape != (f, h, 128, 128) or B.dtype not in (torch.float32, torch.bfloat16)
+            or planes.shape != (f, h, SPLIT_INVERSE_BYTES)):
+        raise ValueError("B must be fp32 or bf16 [F,H,128,128] and planes uint8 [F,H,98304]")
     if alpha.shape != (f, h, 128):
         raise ValueError("alpha must be [F,H,128]")
     _lib.require_device(B)
@@ -220,10 +222,11 @@ def vda_scan_tc(planes, B, alpha, seed=None):
         seed = seed.float().contiguous()
         if seed.shape != (h, 128, 128):
             raise ValueError("seed must be fp32 [H,128,128]")
-    prefix = torch.empty_like(B)
-    suffix = torch.empty_like(B)
+    prefix = torch.empty(B.shape, dtype=torch.float32, device=B.device)
+    suffix = torch.empty_like(prefix)
     status = torch.zeros(1, dtype=torch.int32, device=B.device)
-    _lib.call("vdn_vda_scan_tc", _lib.ptr(planes.contiguous()), _lib.ptr(B.contiguous()),
+    entry = "vdn_vda_scan_tc_bf16" if B.dtype == torch.bfloat16 else "vdn_vda_scan_tc"
+    _lib.call(entry, _lib.ptr(planes.contiguous()), _lib.ptr(B.contiguous()),
               _lib.ptr(alpha.float().contiguous()), _lib.ptr(seed), f, h, _lib.ptr(prefix), _lib.ptr(suffix),
               _lib.ptr(status), _lib.stream_of(B.device))
     if int(status.item()):
