@@ -324,7 +324,8 @@ int vdn_vda_readout(const void* q, int64_t q_sf, int64_t q_ss, int64_t q_sh,
  * directions (forward into prefix, reverse into suffix, [F, H, 128, 128] fp32), from
  * the planes of [F, H] inverses, B [F, H, 128, 128] fp32, alpha [F, H, 128] fp32 and an
  * optional seed [H, 128, 128]; status (optional int32) receives VDN_ERR_TIMEOUT if a
- * bounded wait gave up. */
+ * bounded wait gave up.  Operands 16-byte aligned; prefix and suffix 32-byte aligned
+ * (the banks leave in 32-byte stores). */
 int vdn_vda_factor_inverse(const float* A, int64_t n, void* planes, cudaStream_t stream);
 int vdn_vda_scan_tc(const void* planes, const float* B, const float* alpha, const float* seed, int F, int H,
                     float* prefix, float* suffix, int* status, cudaStream_t stream);
@@ -342,7 +343,8 @@ size_t vdn_vda_workspace_size(int F, int S, int H, int d);
  * q, k, v [F*S, H, d] bf16 with token stride qkv_ss and head stride qkv_sh
  * (shared by the three), beta [F*S, H] bf16 (b_ss, b_sh), gate [F*S, H, d] bf16
  * (g_ss, g_sh), alpha fp32 [F, H, d] contiguous, norm_weight fp32 [d], bounds
- * host int32 [F][2], seed fp32 [H, d, d] or NULL, out bf16 [F*S, H*d].
+ * host int32 [F][2], seed fp32 [H, d, d] or NULL, out bf16 [F*S, H*d]; workspace
+ * (vdn_vda_workspace_size bytes) 32-byte aligned.
  * Replaces BidirectionalLinearBranch._readout / _readout_inference / paper_readout,
  * src/models/linear_attention/branch.py:404-563, paper_stack.py:266-318. */
 int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss, int64_t qkv_sh,

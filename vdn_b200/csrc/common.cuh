@@ -38,6 +38,7 @@ void clear_error();
   } while (0)
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+inline bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31) == 0; }
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
   return __uint_as_float(bits16 << 16);
@@ -114,20 +115,23 @@ __device__ __forceinline__ float sigmoid_nr(float x) {
 
 // Exact three-way bf16 split of eight fp32 values: x = x1 + x2 + x3 with each part
 // the round-to-nearest bf16 of what the earlier parts leave (every subtraction is
-// exact in fp32, and the three 8-bit significands cover fp32's 24).  w[p] holds
-// part p of the eight values as packed bf16 pairs (element 2i in the low half).
+// exact in fp32, and the three 8-bit significands cover fp32's 24).  What the first
+// two parts leave has at most 8 significant bits, so the third part is that residual
+// itself (its rounding would be exact): two conversions per pair, not three.  w[p]
+// holds part p of the eight values as packed bf16 pairs (element 2i in the low half).
 __device__ __forceinline__ void split3_bf16x8(const float* x, uint32_t (&w)[3][4]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     float a = x[2 * i], b = x[2 * i + 1];
 #pragma unroll
-    for (int p = 0; p < 3; ++p) {
+    for (int p = 0; p < 2; ++p) {
       float ra = a, rb = b;
       round_bf16_pair(ra, rb);
       w[p][i] = pack_exact2(ra, rb);
       a -= ra;
       b -= rb;
     }
+    w[2][i] = pack_exact2(a, b);
   }
 }
 

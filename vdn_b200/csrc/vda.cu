@@ -870,7 +870,7 @@ int vdn_vda_forward(const void* q, const void* k, const void* v, int64_t qkv_ss,
   VDN_CHECK_ARG(q && k && v && beta && gate && alpha && norm_weight && out, "null pointer");
   const size_t need = vdn_vda_workspace_size(F, S, H, d);
   VDN_CHECK_ARG(workspace && workspace_bytes >= need, "workspace too small: need %zu bytes", need);
-  VDN_CHECK_ARG(aligned16(workspace), "workspace must be 16-byte aligned");
+  VDN_CHECK_ARG(aligned32(workspace), "workspace must be 32-byte aligned");
   FrameBounds fb;
   if (int rc = fill_bounds(bounds, F, &fb)) return rc;
   const VdaWorkspace w = vda_workspace(workspace, F, H, d);

@@ -15,17 +15,17 @@
 //   warp 1          TMEM allocation; lane 0 issues the 48 MMAs of a step (each
 //                   64-deep K half into its own 128 columns)
 //   warps 2-17      a quarter row of the state per thread (thread = TMEM lane x 32
-//                   columns): read P_{f-1} from TMEM, store it to the frame's bank
-//                   row, form X_f = P_{f-1} alpha_f + B_f (alpha of the chain staged
-//                   in shared memory at the start, B requested before the wait for
-//                   the product) and write its three bf16 parts into the A operand
-//                   (128B-swizzled, K-major)
+//                   columns): read P_{f-1} from TMEM, form X_f = P_{f-1} alpha_f + B_f
+//                   and write its three bf16 parts into the A operand (128B-swizzled,
+//                   K-major); then, while the tensor cores compute P_f, store P_{f-1}
+//                   to its bank (whole 128-byte lines after an in-warp transpose)
 // The copy of inverse f+1 lands while the rows of step f are formed.  With B in bf16
 // (the forward: the statistics round B to bf16 anyway) B_f arrives by TMA as a
-// 128B-swizzled 32 KB tile while the previous product runs, instead of 32 row-per-thread
-// loads per thread (whose 32-row access pattern, with L1 squeezed by the shared-memory
-// carve-out, kept the load queue throttled); alpha is then read from global (every lane
-// of a warp reads the same alpha values).  Every wait
+// 128B-swizzled 32 KB tile, and alpha_f (512 bytes) by a bulk copy on the same
+// barrier, while the previous product runs; the fp32-B form reads B row by row, and
+// alpha from global memory or (up to 64 frames) a copy staged at the start.  A step is the
+// product (48 MMAs, ~3.2k cycles) plus the rows' TMEM read and X formation; the bank
+// stores, issued after X, overlap the product.  Every wait
 // is bounded (2 s); a timeout aborts all roles, lets copies and MMAs in flight
 // finish, frees TMEM and reports VDN_ERR_TIMEOUT through `status`.
 #include "common.cuh"
@@ -47,7 +47,7 @@ constexpr int THREADS = 64 + 32 * ROW_WARPS;  // warp 0 producer, warp 1 MMA, wa
 constexpr int ALPHA_FRAMES = 64;            // alpha of up to this many frames staged in shared memory
 constexpr size_t SMEM = 1024 + 2 * OPER + ALPHA_FRAMES * D * 4 + 256;
 constexpr int BTILE = D * D * 2;            // bf16 B_f: two 64-column halves of 128 rows x 128 B
-constexpr size_t SMEM_BH = 1024 + 2 * OPER + BTILE + 256;
+constexpr size_t SMEM_BH = 1024 + 2 * OPER + BTILE + D * 4 + 256;  // + alpha_f, staged with B_f
 static_assert(SMEM <= 232448 && SMEM_BH <= 232448, "shared memory per CTA");
 
 struct Params {
@@ -67,6 +67,32 @@ __device__ __forceinline__ uint32_t oper_off(uint32_t r, uint32_t c) {
   return (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
 }
 
+// Stores a warp's 32 state rows x 32 columns (lane = row quad*32 + lane, holding
+// columns col0..col0+31 in v) to the bank [D, D].  Row-per-lane stores would touch 32
+// rows (32 partial lines) per instruction; instead a 4 x 4 transpose of 32-byte chunks
+// inside each group of four lanes (two xor-shuffle rounds) leaves lane (a, b) = (lane / 4,
+// lane % 4) holding chunk b of rows 4a .. 4a + 3, so each of the four 32-byte stores
+// writes eight whole 128-byte lines.  v is clobbered.  The bank must be 32-byte aligned.
+__device__ __forceinline__ void store_bank_rows(float* bank, uint32_t (&v)[D / 4], int quad, int lane, int col0) {
+#pragma unroll
+  for (int m = 1; m < 4; m <<= 1) {
+    const bool up = lane & m;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j & m) continue;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // lane with bit m clear sends chunk j^m, the other chunk j
+        const uint32_t send = up ? v[8 * j + c] : v[8 * (j ^ m) + c];
+        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, m);
+        if (up) v[8 * j + c] = recv; else v[8 * (j ^ m) + c] = recv;
+      }
+    }
+  }
+  float* base = bank + (quad * 32 + (lane >> 2) * 4) * D + col0 + (lane & 3) * 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) st_global_v8(base + i * D, v + 8 * i);
+}
+
 // BH: B_f in bf16 through a tensor map (tb: [F*H*128 rows, 128 cols], 64 x 128 boxes,
 // 128B swizzle), staged in shared memory by TMA.
 template <bool BH>
@@ -78,7 +104,8 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
   uint8_t* sI = smem + OPER;                 // B operand: inv_f parts
   uint8_t* sB = smem + 2 * OPER;             // BH: B_f tile
   float* sAlpha = reinterpret_cast<float*>(smem + 2 * OPER);   // !BH: [F][D] when F <= ALPHA_FRAMES
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * OPER + (BH ? BTILE : ALPHA_FRAMES * D * 4));
+  float* sAl = reinterpret_cast<float*>(smem + 2 * OPER + BTILE);  // BH: alpha_f
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * OPER + (BH ? BTILE + D * 4 : ALPHA_FRAMES * D * 4));
   uint64_t* inv_full = bars;
   uint64_t* inv_empty = bars + 1;
   uint64_t* x_ready = bars + 2;
@@ -122,12 +149,13 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
       // ---------------------------------------------------------- producer
       int issued = 0, b_issued = 0;
       for (int step = 0; step < F && !*abort_flag; ++step) {
-        if (BH) {  // B_f as soon as the rows have read B_{f-1} (while the previous product runs)
+        if (BH) {  // B_f and alpha_f once the rows have formed X_{f-1} (while the previous product runs)
           if (!mbar_wait(b_empty, (step & 1) ^ 1, abort_flag)) break;
-          mbar_arrive_expect_tx(b_full, BTILE);
+          mbar_arrive_expect_tx(b_full, BTILE + D * 4);
           const int brow = (frame(step) * H + h) * D;
           tma_load_2d(sB, &tb, b_full, 0, brow);
           tma_load_2d(sB + BTILE / 2, &tb, b_full, 64, brow);
+          bulk_load(sAl, p.alpha + ((int64_t)frame(step) * H + h) * D, D * 4, b_full);
           ++b_issued;
         }
         if (!mbar_wait(inv_empty, (step & 1) ^ 1, abort_flag)) break;
@@ -233,11 +261,11 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
         tc_fence_before();
 #pragma unroll
         for (int i = 0; i < QC; ++i) prev[i] = __float_as_uint(__uint_as_float(prev[i]) + __uint_as_float(hi[i]));
-        uint4* dst = reinterpret_cast<uint4*>(banks + (((int64_t)frame(step - 1) * H + h) * D + row) * D + col0);
-#pragma unroll
-        for (int i = 0; i < QC / 4; ++i) dst[i] = make_uint4(prev[4 * i], prev[4 * i + 1], prev[4 * i + 2], prev[4 * i + 3]);
       }
-      if (step == F) break;
+      if (step == F) {
+        store_bank_rows(banks + ((int64_t)frame(step - 1) * H + h) * D * D, prev, quad, lane, col0);
+        break;
+      }
       if (BH) {  // this thread's 32 values of B_f's row from the staged tile
         if (!__all_sync(0xffffffffu, mbar_wait(b_full, step & 1, abort_flag))) break;
 #pragma unroll
@@ -250,11 +278,9 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
           bq[2 * j] = make_float4(f8[0], f8[1], f8[2], f8[3]);
           bq[2 * j + 1] = make_float4(f8[4], f8[5], f8[6], f8[7]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(b_empty);
       }
       // X = P diag(alpha_f) + B_f, split into three bf16 parts in the A operand.
-      const float* al = alpha_smem ? sAlpha + fr * D + col0 : p.alpha + ((int64_t)fr * H + h) * D + col0;
+      const float* al = BH ? sAl + col0 : alpha_smem ? sAlpha + fr * D + col0 : p.alpha + ((int64_t)fr * H + h) * D + col0;
 #pragma unroll
       for (int c = 0; c < QC / 8; ++c) {
         const float4 al0 = *reinterpret_cast<const float4*>(al + 8 * c);
@@ -277,7 +303,12 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(x_ready);
+      if (lane == 0) {
+        mbar_arrive(x_ready);
+        if (BH) mbar_arrive(b_empty);  // done with B_f and alpha_f
+      }
+      // P_{f-1} to its bank while the tensor cores compute P_f.
+      if (step > 0) store_bank_rows(banks + ((int64_t)frame(step - 1) * H + h) * D * D, prev, quad, lane, col0);
     }
   }
 
@@ -300,9 +331,9 @@ int launch_scan_tc(const void* inv_planes, const float* B, int b_bf16, const flo
   using namespace vscan;
   VDN_CHECK_ARG(F >= 1 && H >= 1, "positive F and H required");
   VDN_CHECK_ARG(inv_planes && B && alpha && prefix && suffix, "null pointer");
-  VDN_CHECK_ARG(aligned16(inv_planes) && aligned16(B) && aligned16(alpha) && aligned16(prefix) &&
-                    aligned16(suffix) && (!seed || aligned16(seed)),
+  VDN_CHECK_ARG(aligned16(inv_planes) && aligned16(B) && aligned16(alpha) && (!seed || aligned16(seed)),
                 "scan operands must be 16-byte aligned");
+  VDN_CHECK_ARG(aligned32(prefix) && aligned32(suffix), "scan banks must be 32-byte aligned");
   static bool attr_set[2] = {false, false};
   Params p{static_cast<const uint8_t*>(inv_planes), B, alpha, seed, prefix, suffix, F, H, status};
   CUtensorMap tb;
