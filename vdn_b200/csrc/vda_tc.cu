@@ -50,11 +50,25 @@ __device__ __forceinline__ bool bar_and(uint32_t id, uint32_t count, bool pred) 
   return out != 0;
 }
 
-// x * sigmoid(x) with the fast exponential and divide (two MUFU operations).  The
-// reciprocal on the FMA pipe instead (sigmoid_nr) measured slower here (statistics
-// 0.37 -> 0.45 ms, readout 0.26 -> 0.33 ms): these transforms are bound by issue, not by
-// the MUFU pipe.
-__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+// x * sigmoid(x) for two values: x0 / a and x1 / b with a = 1 + 2^(-x0 log2 e), b
+// likewise, both reciprocals from one MUFU reciprocal of a * b (1/a = b / (a b)); the
+// products run as f32x2 pairs.  a and b are capped at 2^63 so that a * b stays a
+// normal fp32 value: for x below -43.6, where |silu(x)| < 6e-18, the result is
+// x * 2^-63 instead.  The transforms that use it are bound by issue slots and by
+// the MUFU pipe together (a Newton reciprocal on the FMA pipe, or the pair trick in
+// scalar arithmetic, measured slower); this form takes three MUFU operations and
+// five issue slots of arithmetic for the pair.
+__device__ __forceinline__ void silu_pair(float& x0, float& x1) {
+  const f2 xx = f2_pack(x0, x1);
+  float e0, e1;
+  f2_unpack(f2_mul(xx, f2_pack(-1.4426950408889634f, -1.4426950408889634f)), e0, e1);
+  float a, b;
+  f2_unpack(f2_add(f2_pack(ex2_approx(e0), ex2_approx(e1)), f2_pack(1.0f, 1.0f)), a, b);
+  a = fminf(a, 0x1p63f);
+  b = fminf(b, 0x1p63f);
+  const float r = rcp_approx(a * b);
+  f2_unpack(f2_mul(xx, f2_mul(f2_pack(b, a), f2_pack(r, r))), x0, x1);
+}
 
 // ------------------------------------------------------------------ statistics
 // Persistent, warp-specialised: grid = min(F*H, SMs), one CTA per SM walking
@@ -226,43 +240,54 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         float kv[8], vv[8];
         unpack8(*reinterpret_cast<const uint4*>(st + off), kv);
         unpack8(*reinterpret_cast<const uint4*>(st + 2 * ST_REGION + off), vv);
+        // Features in f32x2 pairs: bf16(silu), the L2 norm (its square root and
+        // reciprocal approximate, within fp32 ulps of the exact ones and then rounded
+        // to bf16 or applied before a bf16 rounding), bf16(x / norm).
         if (FEATURES) {
-          float ss = 0.f;
+          f2 ss2 = f2_pack(0.f, 0.f);
 #pragma unroll
           for (int i = 0; i < 8; i += 2) {
-            kv[i] = silu_fast(kv[i]);
-            kv[i + 1] = silu_fast(kv[i + 1]);
+            silu_pair(kv[i], kv[i + 1]);
             round_bf16_pair(kv[i], kv[i + 1]);
-            ss = fmaf(kv[i], kv[i], ss);
-            ss = fmaf(kv[i + 1], kv[i + 1], ss);
-            vv[i] = silu_fast(vv[i]);
-            vv[i + 1] = silu_fast(vv[i + 1]);
+            const f2 k2 = f2_pack(kv[i], kv[i + 1]);
+            ss2 = f2_fma(k2, k2, ss2);
+            silu_pair(vv[i], vv[i + 1]);
             round_bf16_pair(vv[i], vv[i + 1]);
           }
+          float s0, s1;
+          f2_unpack(ss2, s0, s1);
+          float ss = s0 + s1;
           ss += __shfl_xor_sync(0xffffffffu, ss, 1);
           ss += __shfl_xor_sync(0xffffffffu, ss, 2);
           ss += __shfl_xor_sync(0xffffffffu, ss, 4);
           ss += __shfl_xor_sync(0xffffffffu, ss, 8);
-          const float nrm = fmaxf(round_bf16(sqrtf(ss)), round_bf16(1e-6f));
-          const float inv = __fdiv_rn(1.0f, nrm);
+          const float nrm = fmaxf(round_bf16(sqrt_approx(ss)), round_bf16(1e-6f));
+          const float inv = rcp_approx(nrm);
+          const f2 inv2 = f2_pack(inv, inv);
 #pragma unroll
           for (int i = 0; i < 8; i += 2) {
-            kv[i] *= inv;
-            kv[i + 1] *= inv;
+            f2_unpack(f2_mul(f2_pack(kv[i], kv[i + 1]), inv2), kv[i], kv[i + 1]);
             round_bf16_pair(kv[i], kv[i + 1]);
           }
         }
-        // kf * beta is exact in fp32 (two bf16 factors, 16 significant bits); its
-        // bf16 rounding hi leaves a residual that is itself exactly a bf16 value.
+        // kf * beta is exact in fp32 (two bf16 factors, 16 significant bits): its upper
+        // half (bf16 truncation, hi) and the residual (itself a bf16 value) split it.
         uint32_t hi2[4], lo2[4], vb2[4];
+        const f2 bt2 = f2_pack(bt, bt), m1 = f2_pack(-1.f, -1.f);
 #pragma unroll
         for (int i = 0; i < 8; i += 2) {
-          const float p0 = kv[i] * bt, p1 = kv[i + 1] * bt;
-          float h0 = p0, h1 = p1;
-          round_bf16_pair(h0, h1);
-          hi2[i / 2] = pack_exact2(h0, h1);
-          lo2[i / 2] = pack_exact2(p0 - h0, p1 - h1);
-          vb2[i / 2] = pack_bf16x2(vv[i] * bt, vv[i + 1] * bt);
+          const f2 p2 = f2_mul(f2_pack(kv[i], kv[i + 1]), bt2);
+          float p0, p1;
+          f2_unpack(p2, p0, p1);
+          const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFF0000u);
+          const float h1 = __uint_as_float(__float_as_uint(p1) & 0xFFFF0000u);
+          hi2[i / 2] = pack_exact2(p0, p1);
+          float l0, l1;
+          f2_unpack(f2_fma(f2_pack(h0, h1), m1, p2), l0, l1);
+          lo2[i / 2] = pack_exact2(l0, l1);
+          float w0, w1;
+          f2_unpack(f2_mul(f2_pack(vv[i], vv[i + 1]), bt2), w0, w1);
+          vb2[i / 2] = pack_bf16x2(w0, w1);
         }
         *reinterpret_cast<uint4*>(st + off) = pack_exact8(kv);
         *reinterpret_cast<uint4*>(st + 2 * ST_REGION + off) = make_uint4(vb2[0], vb2[1], vb2[2], vb2[3]);
@@ -546,7 +571,7 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
         }
         uint8_t* region = q_s + s * RO_TILE + half * (RO_TILE / 2);
         // Pass 1: bf16(silu) written back in place, sum of squares; pass 2: / norm.
-        float ssum = 0.f;
+        f2 ss2 = f2_pack(0.f, 0.f);
 #pragma unroll 4
         for (int c = 0; c < 8; ++c) {
           uint4* ptr = reinterpret_cast<uint4*>(region + swz(row, c));
@@ -554,24 +579,26 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
           unpack8(*ptr, x);
 #pragma unroll
           for (int kk = 0; kk < 8; kk += 2) {
-            x[kk] = silu_fast(x[kk]);
-            x[kk + 1] = silu_fast(x[kk + 1]);
+            silu_pair(x[kk], x[kk + 1]);
             round_bf16_pair(x[kk], x[kk + 1]);
-            ssum = fmaf(x[kk], x[kk], ssum);
-            ssum = fmaf(x[kk + 1], x[kk + 1], ssum);
+            const f2 x2 = f2_pack(x[kk], x[kk + 1]);
+            ss2 = f2_fma(x2, x2, ss2);
           }
           *ptr = pack_exact8(x);
         }
+        float s0, s1;
+        f2_unpack(ss2, s0, s1);
+        float ssum = s0 + s1;
         ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);
-        const float nrm = fmaxf(round_bf16(sqrtf(ssum)), round_bf16(1e-6f));
-        const float inv = __fdiv_rn(1.0f, nrm);
+        const float nrm = fmaxf(round_bf16(sqrt_approx(ssum)), round_bf16(1e-6f));
+        const float inv = rcp_approx(nrm);
 #pragma unroll 4
         for (int c = 0; c < 8; ++c) {
           uint4* ptr = reinterpret_cast<uint4*>(region + swz(row, c));
           float x[8];
           unpack8(*ptr, x);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) x[kk] *= inv;
+          for (int kk = 0; kk < 8; kk += 2) f2_unpack(f2_mul(f2_pack(x[kk], x[kk + 1]), f2_pack(inv, inv)), x[kk], x[kk + 1]);
           *ptr = pack8(x);
         }
         fence_proxy_async_smem();
