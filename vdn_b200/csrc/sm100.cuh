@@ -131,6 +131,49 @@ __device__ __forceinline__ void st_global_v8(void* dst, const uint32_t* v) {
                : "memory");
 }
 
+// Stores a warp's 32 x 32 block of 32-bit words (lane = row, v = that row's 32
+// consecutive words) to rows 0..31 of dst (row pitch ld words; dst and ld * 4 bytes
+// 32-byte aligned).  Row-per-lane stores would touch 32 rows (32 partial lines) per
+// instruction; instead a 4 x 4 transpose of 32-byte chunks inside each group of four
+// lanes (two xor-shuffle rounds) leaves lane (a, b) = (lane / 4, lane % 4) holding
+// chunk b of rows 4a .. 4a + 3, so each of the four 32-byte stores writes eight whole
+// 128-byte lines.  v is clobbered.
+__device__ __forceinline__ void store_warp_rows_32x32(uint32_t* dst, int64_t ld, uint32_t (&v)[32], int lane) {
+#pragma unroll
+  for (int m = 1; m < 4; m <<= 1) {
+    const bool up = lane & m;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j & m) continue;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // the lane with bit m clear sends chunk j^m, the other chunk j
+        const uint32_t send = up ? v[8 * j + c] : v[8 * (j ^ m) + c];
+        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, m);
+        if (up) v[8 * j + c] = recv; else v[8 * (j ^ m) + c] = recv;
+      }
+    }
+  }
+  uint32_t* base = dst + (int64_t)((lane >> 2) * 4) * ld + (lane & 3) * 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) st_global_v8(base + i * ld, v + 8 * i);
+}
+
+// The same for a 32 x 16 block (32 rows of 16 words, e.g. 32 bf16 values): one xor
+// round leaves lane (a, b) = (lane / 2, lane % 2) holding chunk b of rows 2a, 2a + 1,
+// so each of the two 32-byte stores writes 64 contiguous bytes of 16 rows.
+__device__ __forceinline__ void store_warp_rows_32x16(uint32_t* dst, int64_t ld, uint32_t (&v)[16], int lane) {
+  const bool up = lane & 1;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint32_t send = up ? v[c] : v[8 + c];
+    const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+    if (up) v[c] = recv; else v[8 + c] = recv;
+  }
+  uint32_t* base = dst + (int64_t)((lane >> 1) * 2) * ld + (lane & 1) * 8;
+  st_global_v8(base, v);
+  st_global_v8(base + ld, v + 8);
+}
+
 // Untiled bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

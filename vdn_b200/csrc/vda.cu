@@ -614,7 +614,7 @@ int launch_stats(const void* k, int64_t k_sf, int64_t k_ss, int64_t k_sh, const 
   if (int rc = check_d(d)) return rc;
   VDN_CHECK_ARG(F >= 1 && S >= 1 && H >= 1, "positive F, S, H required");
   VDN_CHECK_ARG(k && v && beta && A && B, "null pointer");
-  if (tc_stats_supported(d, k, k_sf, k_ss, k_sh, v, v_sf, v_ss, v_sh))
+  if (tc_stats_supported(d, k, k_sf, k_ss, k_sh, v, v_sf, v_ss, v_sh) && aligned32(A) && aligned32(B))
     return launch_stats_tc(k, k_sf, k_ss, k_sh, v, v_sf, v_ss, v_sh, beta, b_sf, b_ss, b_sh,
                            features_applied, F, S, H, A, B, 0, nullptr, stream);
   const size_t smem = std::max<size_t>(3 * 32 * d, (size_t)d * d) * sizeof(float);

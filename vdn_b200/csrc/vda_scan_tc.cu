@@ -67,32 +67,6 @@ __device__ __forceinline__ uint32_t oper_off(uint32_t r, uint32_t c) {
   return (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
 }
 
-// Stores a warp's 32 state rows x 32 columns (lane = row quad*32 + lane, holding
-// columns col0..col0+31 in v) to the bank [D, D].  Row-per-lane stores would touch 32
-// rows (32 partial lines) per instruction; instead a 4 x 4 transpose of 32-byte chunks
-// inside each group of four lanes (two xor-shuffle rounds) leaves lane (a, b) = (lane / 4,
-// lane % 4) holding chunk b of rows 4a .. 4a + 3, so each of the four 32-byte stores
-// writes eight whole 128-byte lines.  v is clobbered.  The bank must be 32-byte aligned.
-__device__ __forceinline__ void store_bank_rows(float* bank, uint32_t (&v)[D / 4], int quad, int lane, int col0) {
-#pragma unroll
-  for (int m = 1; m < 4; m <<= 1) {
-    const bool up = lane & m;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (j & m) continue;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {  // lane with bit m clear sends chunk j^m, the other chunk j
-        const uint32_t send = up ? v[8 * j + c] : v[8 * (j ^ m) + c];
-        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, m);
-        if (up) v[8 * j + c] = recv; else v[8 * (j ^ m) + c] = recv;
-      }
-    }
-  }
-  float* base = bank + (quad * 32 + (lane >> 2) * 4) * D + col0 + (lane & 3) * 8;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) st_global_v8(base + i * D, v + 8 * i);
-}
-
 // BH: B_f in bf16 through a tensor map (tb: [F*H*128 rows, 128 cols], 64 x 128 boxes,
 // 128B swizzle), staged in shared memory by TMA.
 template <bool BH>
@@ -229,6 +203,10 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
     const int col0 = quarter * QC;
     const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + col0;
     float* const banks = dir == 0 ? p.prefix : p.suffix;
+    // This warp's 32 rows x 32 columns of the bank of step s's frame.
+    auto bank_rows = [&](int s) {
+      return reinterpret_cast<uint32_t*>(banks + (((int64_t)frame(s) * H + h) * D + quad * 32) * D + col0);
+    };
     uint32_t prev[QC];                         // this quarter row of the state, fp32 bits
     if (p.seed) {
       const uint4* s4 = reinterpret_cast<const uint4*>(p.seed + ((int64_t)h * D + row) * D + col0);
@@ -263,7 +241,7 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
         for (int i = 0; i < QC; ++i) prev[i] = __float_as_uint(__uint_as_float(prev[i]) + __uint_as_float(hi[i]));
       }
       if (step == F) {
-        store_bank_rows(banks + ((int64_t)frame(step - 1) * H + h) * D * D, prev, quad, lane, col0);
+        store_warp_rows_32x32(bank_rows(step - 1), D, prev, lane);
         break;
       }
       if (BH) {  // this thread's 32 values of B_f's row from the staged tile
@@ -308,7 +286,7 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
         if (BH) mbar_arrive(b_empty);  // done with B_f and alpha_f
       }
       // P_{f-1} to its bank while the tensor cores compute P_f.
-      if (step > 0) store_bank_rows(banks + ((int64_t)frame(step - 1) * H + h) * D * D, prev, quad, lane, col0);
+      if (step > 0) store_warp_rows_32x32(bank_rows(step - 1), D, prev, lane);
     }
   }
 

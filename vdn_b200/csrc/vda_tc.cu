@@ -78,7 +78,9 @@ __device__ __forceinline__ void silu_pair(float& x0, float& x1) {
 // khi / klo split; warp 1 lane 0 issues A2 += khi.kf^T + klo.kf^T + kf.khi^T +
 // kf.klo^T and B += vb.kf^T into one of two TMEM accumulator pairs (512 columns);
 // warps 18-21 drain an item's A = A2 / 2 and B (bf16-rounded) while the next item
-// streams.  A stage is held from its TMA load until its MMAs complete, and the
+// streams, in whole-line stores after an in-warp transpose (row-per-thread stores, 32
+// rows per instruction, held up the transform warps' shared-memory traffic for ~6k
+// cycles at every item boundary).  A stage is held from its TMA load until its MMAs complete, and the
 // load alone takes ~3.2k cycles, so the ring depth sets the chunk rate: the
 // symmetrisation moved onto the tensor cores to free the 66 KB transpose buffer
 // for two more stages.
@@ -330,16 +332,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;                   // warps 18..21 -> quadrants 2,3,0,1
-    const int mrow = quad * 32 + lane;
     int k = 0;
     for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x, ++k) {
       const int b = k & 1;
       if (!bar_and(1, 128, mbar_wait(&acc_full[b], (k >> 1) & 1, abort_flag))) break;
       tc_fence_after();
       const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + b * 256;
-      float* a_out = p.A + ((int64_t)item * 128 + mrow) * 128;
-      float* b_out = p.B + ((int64_t)item * 128 + mrow) * 128;
-      uint16_t* bh_out = reinterpret_cast<uint16_t*>(p.B) + ((int64_t)item * 128 + mrow) * 128;
+      // This warp's 32 rows of the item's A and B; each 32-column block leaves through
+      // an in-warp transpose as whole-line stores.
+      const int64_t row0 = (int64_t)item * 128 + quad * 32;
+      uint32_t* a_out = reinterpret_cast<uint32_t*>(p.A + row0 * 128);
+      uint32_t* b_out = reinterpret_cast<uint32_t*>(p.B) + row0 * (p.b_bf16 ? 64 : 128);
 #pragma unroll 1
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t va[32], vb[32];
@@ -347,24 +350,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         tmem_ld_32x32b_x32(lane_base + 128 + cb * 32, vb);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(a_out + cb * 32 + i) =
-              make_float4(0.5f * __uint_as_float(va[i]), 0.5f * __uint_as_float(va[i + 1]),
-                          0.5f * __uint_as_float(va[i + 2]), 0.5f * __uint_as_float(va[i + 3]));
+        for (int i = 0; i < 32; ++i) va[i] = __float_as_uint(0.5f * __uint_as_float(va[i]));
+        store_warp_rows_32x32(a_out + cb * 32, 128, va, lane);
         if (p.b_bf16) {
+          uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float f8[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) f8[j] = __uint_as_float(vb[i + j]);
-            *reinterpret_cast<uint4*>(bh_out + cb * 32 + i) = pack8(f8);
-          }
+          for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(__uint_as_float(vb[2 * i]), __uint_as_float(vb[2 * i + 1]));
+          store_warp_rows_32x16(b_out + cb * 16, 64, w, lane);
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(b_out + cb * 32 + i) =
-                make_float4(round_bf16(__uint_as_float(vb[i])), round_bf16(__uint_as_float(vb[i + 1])),
-                            round_bf16(__uint_as_float(vb[i + 2])), round_bf16(__uint_as_float(vb[i + 3])));
+          for (int i = 0; i < 32; ++i) vb[i] = __float_as_uint(round_bf16(__uint_as_float(vb[i])));
+          store_warp_rows_32x32(b_out + cb * 32, 128, vb, lane);
         }
       }
       tc_fence_before();
