@@ -21,6 +21,7 @@ from vdn_b200.block import BlockConfig, HybridBlock  # noqa: E402
 from vdn_b200.ulysses import UlyssesRuntime, init_ulysses  # noqa: E402
 
 
+@torch.no_grad()
 def main():
     rt = init_ulysses("nccl", timeout_seconds=60)
     dev = rt.device
