@@ -253,6 +253,18 @@ int vdn_mxfp8_quantize_scatter(const void* src, int64_t rows, int heads_local, i
 int vdn_sepconv(const void* x, int64_t x_ld, int F, int gh, int gw, int C, const void* w_spatial,
                 const void* w_temporal, void* scratch, void* out, int64_t out_ld, cudaStream_t stream);
 
+/* Per-frame column sums of bf16 rows: out [frames, width] fp32, out[f, c] = (sum of
+ * x[r, c] over r in [bounds[f], bounds[f + 1])) / divisor, in a fixed summation order
+ * (the same result on every run).  x [rows, width] bf16 with row stride ld (elements;
+ * width and ld multiples of 8, x 16-byte aligned); bounds host int32 [frames + 1],
+ * nondecreasing within [0, rows] (an empty range gives zeros); frames <= 1024.
+ * divisor = tokens per frame gives the frame mean, 1 the sums of a sequence shard.
+ * Replaces the frame mean of BidirectionalLinearBranch, src/models/linear_attention/
+ * branch.py:450-452, and UlyssesRuntime._local_video_frame_sums,
+ * src/inference/utils/ulysses_runtime.py:606-635. */
+int vdn_frame_sums(const void* x, int64_t ld, int64_t rows, int64_t width, const int32_t* bounds, int frames,
+                   float divisor, float* out, cudaStream_t stream);
+
 /* FrameKDAAlpha: alpha [F, heads, d] fp32 = exp(-exp(a_log[h]) * softplus(
  * (frame_mean @ down_w^T) @ up_w^T + dt_bias)), softplus threshold 20.
  * frame_mean [F, hidden], down_w [r, hidden], up_w [heads*d, r], dt_bias

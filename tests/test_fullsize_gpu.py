@@ -62,7 +62,7 @@ def config3(cuda):
 
 @torch.no_grad()
 def test_block_config3_stages_full_size(cuda, config3):
-    from vdn_b200.linear_attention import vda_forward, window_bounds
+    from vdn_b200.linear_attention import frame_sums, vda_forward, window_bounds
     from vdn_b200.mxfp8_kernels import launch_prenorm_quantize
     from vdn_b200.mxfp8_quant import quantize_activation
     from vdn_b200.window import window_softmax
@@ -86,7 +86,7 @@ def test_block_config3_stages_full_size(cuda, config3):
     q, k, v = (qkv[:, i * hd:(i + 1) * hd].view(T, H, d) for i in range(3))
     att = torch.empty(T, H, d, device=cuda, dtype=torch.bfloat16)
     window_softmax(q, k, v, g3[:, :H], frames, tokens, cfg.radius, out=att)
-    frame_mean = y1.view(frames, tokens, hd).mean(1, dtype=torch.float32)
+    frame_mean = frame_sums(y1, [f * tokens for f in range(frames + 1)], tokens)
     alpha = block.alpha.forward_native(frame_mean)
     bounds = window_bounds(frames, cfg.radius)
     lin = vda_forward(q, k, v, g3[:, H:2 * H], lgate.view(T, H, d), alpha, bounds, frames, tokens, block.vda_norm)

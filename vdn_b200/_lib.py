@@ -58,6 +58,7 @@ SIGNATURES = {
                                 _i64, _i64, _p, _p, _p]),
     "vdn_sepconv": (_i32, [_p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _i64, _p]),
     "vdn_frame_alpha": (_i32, [_p, _i32, _i32, _p, _i32, _p, _p, _p, _i32, _i32, _p, _p, _p]),
+    "vdn_frame_sums": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _f32, _p, _p]),
     "vdn_delta_factors": (_i32, [_p, _p, _p, _i64, _i32, _p, _p, _p]),
     "vdn_vda_statistics": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                   _i32, _i32, _i32, _i32, _i32, _p, _p, _p]),

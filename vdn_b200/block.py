@@ -37,7 +37,7 @@ from torch import nn
 
 from . import _lib
 from .gates import gate_gemm
-from .linear_attention import FrameKDAAlpha, OutputGate, window_bounds
+from .linear_attention import FrameKDAAlpha, OutputGate, frame_sums, window_bounds
 from .mxfp8_kernels import launch_prenorm_quantize
 from .mxfp8_quant import quantize_cpu, quantize_activation
 from .window import window_softmax
@@ -256,7 +256,7 @@ class HybridBlock(nn.Module):
             return self._forward_general(x, temb, frames, tokens, text_rows)
         ev = runtime.profile_start() if runtime is not None else None
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self._adaln(temb)
-        idx = torch.zeros(rows, dtype=torch.int64, device=dev)
+        idx = self._row_index(rows, dev)
         y1, q1, s1, _ = launch_prenorm_quantize(x, self.norm1, cfg.eps, scale_msa.view(1, hd),
                                                 shift_msa.view(1, hd), idx, write_bf16=True)
         if runtime is not None:
@@ -285,7 +285,7 @@ class HybridBlock(nn.Module):
             og = self.output_gate
             lgate = self._linear_gate(g3[:, 2 * H:])                      # [rows, H*d]
             if runtime is None:
-                frame_mean = y1.view(frames, tokens, hd).mean(1, dtype=torch.float32)
+                frame_mean = frame_sums(y1, [f * tokens for f in range(frames + 1)], tokens)
                 first, second = self._attention(qkv, sgate, beta, lgate, frame_mean, frames, tokens,
                                                 heads=slice(0, H))
             else:
@@ -295,6 +295,15 @@ class HybridBlock(nn.Module):
         self._gemm(first[0], first[1], self.o, rows, x1, second=(second, self.ol),
                    bias=self.o_bias, resid=x, gate=gate_msa.contiguous())
         return self._ffn(x1, shift_mlp, scale_mlp, gate_mlp, idx)
+
+    def _row_index(self, rows, dev):
+        """The AdaLN row -> modulation-row map (all rows use row 0: one timestep per
+        call), cached per row count so a forward launches no fill for it."""
+        cache = self.__dict__.setdefault("_row_index_cache", {})
+        idx = cache.get((rows, dev))
+        if idx is None:
+            idx = cache[(rows, dev)] = torch.zeros(rows, dtype=torch.int64, device=dev)
+        return idx
 
     def _adaln(self, temb):
         hd = self.cfg.hidden
@@ -338,7 +347,7 @@ class HybridBlock(nn.Module):
         n = x.shape[0]
         dev = x.device
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self._adaln(temb)
-        idx = torch.zeros(n, dtype=torch.int64, device=dev)
+        idx = self._row_index(n, dev)
         y1, q1, s1, _ = launch_prenorm_quantize(x, self.norm1, cfg.eps, scale_msa.view(1, hd),
                                                 shift_msa.view(1, hd), idx, write_bf16=True)
         qkv = torch.empty(n, 3 * hd, device=dev, dtype=torch.bfloat16)
@@ -350,7 +359,7 @@ class HybridBlock(nn.Module):
             k = qkv[:, hd:2 * hd].view(n, H, d)
             v = qkv[:, 2 * hd:].view(n, H, d)
             lgate = self._linear_gate(g3[L:, 2 * H:]).view(T, H, d)
-            frame_mean = y1[L:].view(frames, tokens, hd).mean(1, dtype=torch.float32)
+            frame_mean = frame_sums(y1[L:], [f * tokens for f in range(frames + 1)], tokens)
             att = torch.empty(n, H, d, device=dev, dtype=torch.bfloat16)
             lin_q = self._layout_branches(q, k, v, g3[:, :H], g3[:, H:2 * H], lgate, frame_mean, frames,
                                           tokens, L, slice(0, H), att, quantize_lin=True)

@@ -58,9 +58,87 @@ __global__ void __launch_bounds__(256) alpha_up_kernel(const float* __restrict__
   out[g] = expf(-expf(a_log[o / d]) * sp);
 }
 
+// ----------------------------------------------------------------- frame sums
+// Per-frame fp32 column sums of bf16 rows, the input of FrameKDAAlpha (the
+// reference's frame mean, branch.py:450-452, and the sequence-parallel frame sums,
+// ulysses_runtime.py:606-635): out[f, c] = (sum of x[r, c] over rows r in
+// [bounds[f], bounds[f + 1])) / divisor.  grid (width / 256, frames), 256 threads =
+// 32 column lanes (8 columns each: one 16-byte load per row, a warp reads 512
+// contiguous bytes) x 8 row groups (rows g, g + 8, ...; four rows in flight per
+// thread).  The row groups are added in a fixed order, so the sums are the same on
+// every run (the reference replaced an atomic reduction for that reason).
+constexpr int kFrameSumsMax = 1024;
+struct FrameRows {
+  int32_t b[kFrameSumsMax + 1];
+};
+
+__global__ void __launch_bounds__(256) frame_sums_kernel(const uint16_t* __restrict__ x, int64_t ld,
+                                                         int64_t width, const __grid_constant__ FrameRows fr,
+                                                         float divisor, float* __restrict__ out) {
+  __shared__ __align__(16) float part[8][256];
+  const int f = blockIdx.y;
+  const int lc = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int64_t c0 = (int64_t)blockIdx.x * 256;
+  const int64_t col = c0 + lc * 8;
+  const int r1 = fr.b[f + 1];
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  auto add = [&](const uint4& v) {
+    float e[8];
+    unpack8(v, e);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] += e[k];
+  };
+  if (col < width) {
+    const uint16_t* px = x + col;
+    int r = fr.b[f] + g;
+    for (; r + 24 < r1; r += 32) {
+      const uint4 v0 = __ldg(reinterpret_cast<const uint4*>(px + (int64_t)r * ld));
+      const uint4 v1 = __ldg(reinterpret_cast<const uint4*>(px + (int64_t)(r + 8) * ld));
+      const uint4 v2 = __ldg(reinterpret_cast<const uint4*>(px + (int64_t)(r + 16) * ld));
+      const uint4 v3 = __ldg(reinterpret_cast<const uint4*>(px + (int64_t)(r + 24) * ld));
+      add(v0);
+      add(v1);
+      add(v2);
+      add(v3);
+    }
+    for (; r < r1; r += 8) add(__ldg(reinterpret_cast<const uint4*>(px + (int64_t)r * ld)));
+  }
+  float4* dst = reinterpret_cast<float4*>(&part[g][lc * 8]);
+  dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  __syncthreads();
+  const int64_t c = c0 + threadIdx.x;
+  if (c < width) {
+    float s = part[0][threadIdx.x];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) s += part[k][threadIdx.x];
+    out[(int64_t)f * width + c] = __fdiv_rn(s, divisor);
+  }
+}
+
 }  // namespace vdn
 
 using namespace vdn;
+
+extern "C" int vdn_frame_sums(const void* x, int64_t ld, int64_t rows, int64_t width, const int32_t* bounds,
+                              int frames, float divisor, float* out, cudaStream_t stream) {
+  VDN_CHECK_ARG(frames >= 1 && frames <= kFrameSumsMax, "frames must lie in [1, %d]", kFrameSumsMax);
+  VDN_CHECK_ARG(rows >= 0 && rows < (1ll << 31) && width > 0, "bad extents");
+  VDN_CHECK_ARG(bounds && out && (x || rows == 0), "null pointer");
+  VDN_CHECK_ARG(width % 8 == 0 && ld % 8 == 0 && ld >= width && aligned16(x),
+                "x must be 16-byte aligned with width and row stride multiples of 8 elements");
+  VDN_CHECK_ARG(divisor != 0.0f, "divisor must be nonzero");
+  FrameRows fr;
+  for (int f = 0; f <= frames; ++f) {
+    VDN_CHECK_ARG(bounds[f] >= 0 && bounds[f] <= rows && (f == 0 || bounds[f] >= bounds[f - 1]),
+                  "bounds must be nondecreasing row offsets within [0, rows]");
+    fr.b[f] = bounds[f];
+  }
+  frame_sums_kernel<<<dim3((unsigned)((width + 255) / 256), (unsigned)frames), 256, 0, stream>>>(
+      static_cast<const uint16_t*>(x), ld, width, fr, divisor, out);
+  VDN_LAUNCH_CHECK("frame sums");
+  return VDN_OK;
+}
 
 extern "C" int vdn_frame_alpha(const float* frame_mean, int F, int hidden, const float* down_w, int r,
                                const float* up_w, const float* dt_bias, const float* a_log, int heads,

@@ -76,6 +76,26 @@ class OutputGate(nn.Module):
         return gate.view(-1, self.num_heads, self.head_dim or 1)
 
 
+def frame_sums(x, bounds, divisor=1.0, out=None):
+    """Per-frame fp32 column sums of bf16 rows x [rows, W] over the row ranges
+    [bounds[f], bounds[f + 1]) (host ints, nondecreasing), divided by `divisor`:
+    [len(bounds) - 1, W] fp32, in a fixed order (reproducible run to run).  divisor =
+    tokens per frame gives the frame mean (branch.py:450-452); 1 the sums of a sequence
+    shard (ulysses_runtime.py:606-635).  One native launch (vdn_frame_sums)."""
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be bf16 [rows, W] with unit column stride")
+    frames = len(bounds) - 1
+    if out is None:
+        out = torch.empty(frames, x.shape[1], device=x.device, dtype=torch.float32)
+    if out.shape != (frames, x.shape[1]) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("out must be contiguous fp32 [frames, W]")
+    _lib.require_device(x)
+    buf = (_lib.C.c_int32 * (frames + 1))(*[int(b) for b in bounds])
+    _lib.call("vdn_frame_sums", _lib.ptr(x), x.stride(0), x.shape[0], x.shape[1], buf, frames, float(divisor),
+              _lib.ptr(out), _lib.stream_of(x.device))
+    return out
+
+
 class FrameKDAAlpha(nn.Module):
     """alpha = exp(-exp(A_log) * softplus(up(down(mean)) + dt_bias)), fp32 (layers.py:12-69)."""
 

@@ -29,6 +29,8 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
+from .linear_attention import frame_sums
+
 __all__ = ["sequence_splits", "balanced_splits", "ShardPlan", "UlyssesRuntime", "init_ulysses",
            "install_ulysses"]
 
@@ -428,22 +430,17 @@ class UlyssesRuntime:
                          video_start: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
         """Per-frame fp32 sums of this rank's rows, one contiguous slice per frame
         (deterministic; ulysses_runtime.py:606-635).  `out` [num_frames, W] fp32."""
-        if out is None:
-            sums = torch.zeros(num_frames, local_x.shape[-1], device=local_x.device, dtype=torch.float32)
-        else:
-            sums = out
-            sums.zero_()
-        v0, v1 = video_start, video_start + num_frames * tokens_per_frame
-        lo, hi = max(self.local_start, v0), min(self.local_end, v1)
-        if hi <= lo:
-            return sums
-        first = (lo - v0) // tokens_per_frame
-        last = (hi - 1 - v0) // tokens_per_frame
-        for frame in range(first, last + 1):
-            a = max(lo, v0 + frame * tokens_per_frame)
-            b = min(hi, v0 + (frame + 1) * tokens_per_frame)
-            torch.sum(local_x[a - self.local_start:b - self.local_start], 0, dtype=torch.float32,
-                      out=sums[frame])
+        v0 = video_start
+        lo, hi = self.local_start, self.local_end
+        # Frame f's rows clipped to this rank's shard, as offsets into local_x; frames
+        # outside the shard get empty ranges (zero sums).
+        bounds = [min(max(v0 + f * tokens_per_frame, lo), hi) - lo for f in range(num_frames + 1)]
+        if local_x.is_cuda:
+            return frame_sums(local_x, bounds, 1.0, out=out)
+        # Host tensors (gloo process groups): one torch sum per frame slice.
+        sums = out if out is not None else torch.empty(num_frames, local_x.shape[-1], dtype=torch.float32)
+        for f in range(num_frames):
+            torch.sum(local_x[bounds[f]:bounds[f + 1]], 0, dtype=torch.float32, out=sums[f])
         return sums
 
     def video_frame_mean_async(self, local_x, num_frames, tokens_per_frame, video_start=0):
