@@ -125,11 +125,11 @@ class ClockSampler:
 # (x 21 / 5).  Reported as roofline "traffic" with "traffic_source" saying so.
 NCU_TRAFFIC_BYTES = {
     "mxfp8_gemm_qkv": (104.2e6 + 97.6e6) * 32760 / 4096,
-    "statistics": 167.2e6 * 21 / 5,
+    "statistics": 164.4e6 * 21 / 5,
     "factors": 13.2e6 * 21 / 5,
-    "scan": 32.9e6 * 21 / 5,
+    "scan": 26.4e6 * 21 / 5,
     "gather": 15.8e6 * 21 / 5,
-    "readout": 213.6e6 * 21 / 5,
+    "readout": 215.9e6 * 21 / 5,
 }
 
 TRAFFIC_SOURCE = ("from a separate ncu capture of a small case of this kernel (profiles/), scaled to "
@@ -529,6 +529,9 @@ def bench_block(args, torch, dist, rank, world):
         ms = time_steps(torch, step, args.steps, args.warmup, dist, stream)
     per_step_ms = ms / args.steps
     value = T / (per_step_ms * 1e-3)
+    # This library's kernels per forward, counted on one eager forward (every rank runs
+    # it: the sharded forward has collectives); the graph replays the same launches.
+    launches = count_launches(lambda: block(x, temb, F, S, runtime))
     flops = 2 * T * BLOCK_CFG["hidden"] * (3 * BLOCK_CFG["hidden"] + 2 * BLOCK_CFG["hidden"]
                                            + 2 * BLOCK_CFG["ffn"])
 
@@ -594,7 +597,7 @@ def bench_block(args, torch, dist, rank, world):
                 "h2d_bytes_per_step": x_host[0].numel() * 2, "d2h_bytes_per_step": out_host[0].numel() * 2,
                 "steps": e2e_steps, "copies": "per step; overlapped with neighbouring steps"
                 if not args.eager else "per step; serial"},
-        "gpu_launches": block.launches_per_forward(world, runtime) * args.steps,
+        "gpu_launches": launches * args.steps,
         "launch": "eager" if args.eager else "cuda_graph",
         "roofline": {"bound": "tensor", "kernel": "mxfp8_gemm (QKV, %d x 15360 x 5120)" % rows,
                      "achieved": round(achieved, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",

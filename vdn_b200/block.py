@@ -211,21 +211,6 @@ class HybridBlock(nn.Module):
             return out
         return join
 
-    def launches_per_forward(self, world_size=1, runtime=None):
-        """Kernels of this library launched per block forward (for bench accounting)."""
-        # Every layout: prenorm, QKV GEMM, output GEMM, prenorm, FFN up (+GELU
-        # quantise), FFN down.  Window softmax: the merge (the attention legs are
-        # cuDNN).  VDA: alpha (2), statistics, factors, scans, gather, readout.
-        common, softmax, vda = 6, 1, 7
-        if world_size == 1:
-            return common + softmax + vda + 1                  # + quantise the VDA output
-        if runtime is not None and runtime.branch_parallel:    # one branch per rank, 2 quantisers
-            return common + (softmax if runtime.branch_kind == "softmax" else vda) + 2
-        if runtime is not None and runtime.exchange_mode != "peer":
-            return common + softmax + vda + 2                  # NCCL all-to-alls, 2 quantisers
-        # peer exchange: two scatter quantisers, two side-input broadcasts, two fences
-        return common + softmax + vda + 6
-
     # ---------------------------------------------------------------- forward
     @torch.no_grad()
     def forward(self, x, temb, frames, tokens, runtime=None, text_rows=0):
