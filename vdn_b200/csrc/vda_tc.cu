@@ -50,22 +50,36 @@ __device__ __forceinline__ bool bar_and(uint32_t id, uint32_t count, bool pred) 
   return out != 0;
 }
 
-// x * sigmoid(x) for two values: x0 / a and x1 / b with a = 1 + 2^(-x0 log2 e), b
-// likewise, both reciprocals from one MUFU reciprocal of a * b (1/a = b / (a b)); the
-// products run as f32x2 pairs.  a and b are capped at 2^63 so that a * b stays a
-// normal fp32 value: for x below -43.6, where |silu(x)| < 6e-18, the result is
-// x * 2^-63 instead.  The transforms that use it are bound by issue slots and by
-// the MUFU pipe together (a Newton reciprocal on the FMA pipe, or the pair trick in
-// scalar arithmetic, measured slower); this form takes three MUFU operations and
-// five issue slots of arithmetic for the pair.
+// bf16 pair helpers: unpack a packed pair, and the round-to-nearest product of two
+// bf16 pairs (exact product, one rounding: the bf16 multiply of the eager body).
+__device__ __forceinline__ void unpack2(uint32_t w, float& lo, float& hi) {
+  lo = __uint_as_float(w << 16);
+  hi = __uint_as_float(w & 0xFFFF0000u);
+}
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// SiLU inputs arrive as packed bf16 pairs; values below -43.5 (bf16 0xC22E) are raised
+// to it, where |silu(x)| < 6e-18 (compare the unsigned 16-bit patterns: every negative
+// value below -43.5, -inf included, has a larger pattern than 0xC22E, every positive
+// value a smaller one).  This bounds 1 + e^-x by 8e18 for silu_pair.
+__device__ __forceinline__ uint32_t clamp_silu_in(uint32_t w) { return __vminu2(w, 0xC22EC22Eu); }
+
+// x * sigmoid(x) for two values clamped by clamp_silu_in: x0 / a and x1 / b with
+// a = 1 + 2^(-x0 log2 e), b likewise, both reciprocals from one MUFU reciprocal of
+// a * b (< 2^126: 1/a = b / (a b)); the products run as f32x2 pairs.  The transforms
+// that use it are bound by issue slots and the MUFU pipe together (a Newton reciprocal
+// on the FMA pipe, or the pair trick in scalar arithmetic, measured slower): this form
+// takes three MUFU operations and five issue slots of arithmetic for the pair.
 __device__ __forceinline__ void silu_pair(float& x0, float& x1) {
   const f2 xx = f2_pack(x0, x1);
   float e0, e1;
   f2_unpack(f2_mul(xx, f2_pack(-1.4426950408889634f, -1.4426950408889634f)), e0, e1);
   float a, b;
   f2_unpack(f2_add(f2_pack(ex2_approx(e0), ex2_approx(e1)), f2_pack(1.0f, 1.0f)), a, b);
-  a = fminf(a, 0x1p63f);
-  b = fminf(b, 0x1p63f);
   const float r = rcp_approx(a * b);
   f2_unpack(f2_mul(xx, f2_mul(f2_pack(b, a), f2_pack(r, r))), x0, x1);
 }
@@ -239,22 +253,30 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         uint8_t* st = stages + s * ST_STAGE_BYTES;
         const float bt = beta_s[s * ST_CH + row];
         const uint32_t off = r * ST_REGION + swz(row, cc);
-        float kv[8], vv[8];
-        unpack8(*reinterpret_cast<const uint4*>(st + off), kv);
-        unpack8(*reinterpret_cast<const uint4*>(st + 2 * ST_REGION + off), vv);
+        const uint4 kin = *reinterpret_cast<const uint4*>(st + off);
+        const uint4 vin = *reinterpret_cast<const uint4*>(st + 2 * ST_REGION + off);
+        uint32_t kfw[4] = {kin.x, kin.y, kin.z, kin.w};   // kf as packed bf16 pairs
+        uint32_t vsw[4] = {vin.x, vin.y, vin.z, vin.w};   // bf16(silu(v)) (or v) pairs
+        float kv[8];
         // Features in f32x2 pairs: bf16(silu), the L2 norm (its square root and
         // reciprocal approximate, within fp32 ulps of the exact ones and then rounded
-        // to bf16 or applied before a bf16 rounding), bf16(x / norm).
+        // to bf16 or applied before a bf16 rounding), bf16(x / norm); each bf16 result
+        // stays packed as the conversion writes it and is unpacked only where fp32
+        // arithmetic needs it.
         if (FEATURES) {
           f2 ss2 = f2_pack(0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) {
-            silu_pair(kv[i], kv[i + 1]);
-            round_bf16_pair(kv[i], kv[i + 1]);
-            const f2 k2 = f2_pack(kv[i], kv[i + 1]);
+          for (int i = 0; i < 4; ++i) {
+            float a, b;
+            unpack2(clamp_silu_in(kfw[i]), a, b);
+            silu_pair(a, b);
+            kfw[i] = pack_bf16x2(a, b);
+            unpack2(kfw[i], kv[2 * i], kv[2 * i + 1]);
+            const f2 k2 = f2_pack(kv[2 * i], kv[2 * i + 1]);
             ss2 = f2_fma(k2, k2, ss2);
-            silu_pair(vv[i], vv[i + 1]);
-            round_bf16_pair(vv[i], vv[i + 1]);
+            unpack2(clamp_silu_in(vsw[i]), a, b);
+            silu_pair(a, b);
+            vsw[i] = pack_bf16x2(a, b);
           }
           float s0, s1;
           f2_unpack(ss2, s0, s1);
@@ -267,31 +289,36 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
           const float inv = rcp_approx(nrm);
           const f2 inv2 = f2_pack(inv, inv);
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) {
-            f2_unpack(f2_mul(f2_pack(kv[i], kv[i + 1]), inv2), kv[i], kv[i + 1]);
-            round_bf16_pair(kv[i], kv[i + 1]);
+          for (int i = 0; i < 4; ++i) {
+            float a, b;
+            f2_unpack(f2_mul(f2_pack(kv[2 * i], kv[2 * i + 1]), inv2), a, b);
+            kfw[i] = pack_bf16x2(a, b);
+            unpack2(kfw[i], kv[2 * i], kv[2 * i + 1]);
           }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) unpack2(kfw[i], kv[2 * i], kv[2 * i + 1]);
         }
         // kf * beta is exact in fp32 (two bf16 factors, 16 significant bits): its upper
         // half (bf16 truncation, hi) and the residual (itself a bf16 value) split it.
+        // vb = bf16(v * beta) is one bf16 pair multiply (exact product, one rounding).
         uint32_t hi2[4], lo2[4], vb2[4];
         const f2 bt2 = f2_pack(bt, bt), m1 = f2_pack(-1.f, -1.f);
+        const uint32_t bb = __float_as_uint(bt) >> 16, btb = bb | (bb << 16);   // (beta, beta) bf16x2
 #pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          const f2 p2 = f2_mul(f2_pack(kv[i], kv[i + 1]), bt2);
+        for (int i = 0; i < 4; ++i) {
+          const f2 p2 = f2_mul(f2_pack(kv[2 * i], kv[2 * i + 1]), bt2);
           float p0, p1;
           f2_unpack(p2, p0, p1);
           const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFF0000u);
           const float h1 = __uint_as_float(__float_as_uint(p1) & 0xFFFF0000u);
-          hi2[i / 2] = pack_exact2(p0, p1);
+          hi2[i] = pack_exact2(p0, p1);
           float l0, l1;
           f2_unpack(f2_fma(f2_pack(h0, h1), m1, p2), l0, l1);
-          lo2[i / 2] = pack_exact2(l0, l1);
-          float w0, w1;
-          f2_unpack(f2_mul(f2_pack(vv[i], vv[i + 1]), bt2), w0, w1);
-          vb2[i / 2] = pack_bf16x2(w0, w1);
+          lo2[i] = pack_exact2(l0, l1);
+          vb2[i] = mul_bf16x2(vsw[i], btb);
         }
-        *reinterpret_cast<uint4*>(st + off) = pack_exact8(kv);
+        *reinterpret_cast<uint4*>(st + off) = make_uint4(kfw[0], kfw[1], kfw[2], kfw[3]);
         *reinterpret_cast<uint4*>(st + 2 * ST_REGION + off) = make_uint4(vb2[0], vb2[1], vb2[2], vb2[3]);
         *reinterpret_cast<uint4*>(st + 4 * ST_REGION + off) = make_uint4(hi2[0], hi2[1], hi2[2], hi2[3]);
         *reinterpret_cast<uint4*>(st + 6 * ST_REGION + off) = make_uint4(lo2[0], lo2[1], lo2[2], lo2[3]);
@@ -571,16 +598,19 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
 #pragma unroll 4
         for (int c = 0; c < 8; ++c) {
           uint4* ptr = reinterpret_cast<uint4*>(region + swz(row, c));
-          float x[8];
-          unpack8(*ptr, x);
+          const uint4 w4 = *ptr;
+          uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-          for (int kk = 0; kk < 8; kk += 2) {
-            silu_pair(x[kk], x[kk + 1]);
-            round_bf16_pair(x[kk], x[kk + 1]);
-            const f2 x2 = f2_pack(x[kk], x[kk + 1]);
+          for (int i = 0; i < 4; ++i) {
+            float a, b;
+            unpack2(clamp_silu_in(ww[i]), a, b);
+            silu_pair(a, b);
+            ww[i] = pack_bf16x2(a, b);
+            unpack2(ww[i], a, b);
+            const f2 x2 = f2_pack(a, b);
             ss2 = f2_fma(x2, x2, ss2);
           }
-          *ptr = pack_exact8(x);
+          *ptr = make_uint4(ww[0], ww[1], ww[2], ww[3]);
         }
         float s0, s1;
         f2_unpack(ss2, s0, s1);
