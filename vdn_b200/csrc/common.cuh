@@ -163,19 +163,20 @@ __device__ __forceinline__ float sigmoid_nr(float x) {
 // the round-to-nearest bf16 of what the earlier parts leave (every subtraction is
 // exact in fp32, and the three 8-bit significands cover fp32's 24).  What the first
 // two parts leave has at most 8 significant bits, so the third part is that residual
-// itself (its rounding would be exact): two conversions per pair, not three.  w[p]
-// holds part p of the eight values as packed bf16 pairs (element 2i in the low half).
+// itself (its rounding would be exact): two conversions per pair, not three.  Each
+// conversion's packed output is the part itself; the residuals are taken in f32x2
+// pairs.  w[p] holds part p of the eight values as packed bf16 pairs (element 2i in
+// the low half).
 __device__ __forceinline__ void split3_bf16x8(const float* x, uint32_t (&w)[3][4]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     float a = x[2 * i], b = x[2 * i + 1];
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
-      float ra = a, rb = b;
-      round_bf16_pair(ra, rb);
-      w[p][i] = pack_exact2(ra, rb);
-      a -= ra;
-      b -= rb;
+      const uint32_t pk = pack_bf16x2(a, b);
+      w[p][i] = pk;
+      const f2 r = f2_pack(__uint_as_float(pk << 16), __uint_as_float(pk & 0xFFFF0000u));
+      f2_unpack(f2_fma(r, f2_pack(-1.0f, -1.0f), f2_pack(a, b)), a, b);
     }
     w[2][i] = pack_exact2(a, b);
   }

@@ -238,7 +238,13 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
         tmem_ld_wait();
         tc_fence_before();
 #pragma unroll
-        for (int i = 0; i < QC; ++i) prev[i] = __float_as_uint(__uint_as_float(prev[i]) + __uint_as_float(hi[i]));
+        for (int i = 0; i < QC; i += 2) {
+          float s0, s1;
+          f2_unpack(f2_add(f2_pack(__uint_as_float(prev[i]), __uint_as_float(prev[i + 1])),
+                           f2_pack(__uint_as_float(hi[i]), __uint_as_float(hi[i + 1]))), s0, s1);
+          prev[i] = __float_as_uint(s0);
+          prev[i + 1] = __float_as_uint(s1);
+        }
       }
       if (step == F) {
         store_warp_rows_32x32(bank_rows(step - 1), D, prev, lane);
@@ -264,14 +270,14 @@ __global__ void __launch_bounds__(THREADS, 1) scan_tc_kernel(const __grid_consta
         const float4 al0 = *reinterpret_cast<const float4*>(al + 8 * c);
         const float4 al1 = *reinterpret_cast<const float4*>(al + 8 * c + 4);
         const float4 b0 = bq[2 * c], b1 = bq[2 * c + 1];
-        const float x[8] = {fmaf(__uint_as_float(prev[8 * c]), al0.x, b0.x),
-                            fmaf(__uint_as_float(prev[8 * c + 1]), al0.y, b0.y),
-                            fmaf(__uint_as_float(prev[8 * c + 2]), al0.z, b0.z),
-                            fmaf(__uint_as_float(prev[8 * c + 3]), al0.w, b0.w),
-                            fmaf(__uint_as_float(prev[8 * c + 4]), al1.x, b1.x),
-                            fmaf(__uint_as_float(prev[8 * c + 5]), al1.y, b1.y),
-                            fmaf(__uint_as_float(prev[8 * c + 6]), al1.z, b1.z),
-                            fmaf(__uint_as_float(prev[8 * c + 7]), al1.w, b1.w)};
+        const float alv[8] = {al0.x, al0.y, al0.z, al0.w, al1.x, al1.y, al1.z, al1.w};
+        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        float x[8];
+#pragma unroll
+        for (int k = 0; k < 8; k += 2)
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(prev[8 * c + k]), __uint_as_float(prev[8 * c + k + 1])),
+                           f2_pack(alv[k], alv[k + 1]), f2_pack(bv[k], bv[k + 1])),
+                    x[k], x[k + 1]);
         uint32_t w[3][4];
         split3_bf16x8(x, w);
         const uint32_t off = oper_off(row, quarter * (QC / 8) + c);

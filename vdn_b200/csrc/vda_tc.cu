@@ -653,7 +653,7 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + b * 128;
-        float ss = 0.f;
+        f2 ss2 = f2_pack(0.f, 0.f);
 #pragma unroll 1
         for (int cb = 0; cb < 4; ++cb) {
           uint32_t v[32];
@@ -661,14 +661,18 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
           tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
-            round_bf16_pair(x0, x1);
-            ss = fmaf(x0, x0, ss);
-            ss = fmaf(x1, x1, ss);
+            float x0, x1;
+            unpack2(pack_bf16x2(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), x0, x1);
+            const f2 x2 = f2_pack(x0, x1);
+            ss2 = f2_fma(x2, x2, ss2);
           }
         }
+        float s0, s1;
+        f2_unpack(ss2, s0, s1);
+        const float ss = s0 + s1;
         const float nrm = sqrtf(ss);
         const float inv = round_bf16(__fdiv_rn(1.0f, sqrtf(nrm * nrm / 128.0f + p.eps)));
+        const uint32_t ib = __float_as_uint(inv) >> 16, inv2 = ib | (ib << 16);
         uint8_t* gt = g_s + gs * RO_TILE;
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb) {
@@ -679,23 +683,21 @@ __global__ void __launch_bounds__(RO_THREADS, 1)
           for (int e4 = 0; e4 < 4; ++e4) {
             const int col = cb * 32 + 8 * e4;  // 8 columns in one 16-byte chunk of a 64-column half
             uint4* cell = reinterpret_cast<uint4*>(gt + (col >> 6) * (RO_TILE / 2) + swz(erow, (col & 63) >> 3));
-            float gf[8], y[8];
-            unpack8(*cell, gf);
+            const uint4 g4 = *cell;
+            const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+            uint32_t yw[4];
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              const int c = 8 * e4 + e;
-              float r0 = __uint_as_float(v[c]), r1 = __uint_as_float(v[c + 1]);
-              round_bf16_pair(r0, r1);
-              r0 *= inv;
-              r1 *= inv;
-              round_bf16_pair(r0, r1);
-              r0 *= w_s[cb * 32 + c];
-              r1 *= w_s[cb * 32 + c + 1];
-              round_bf16_pair(r0, r1);
-              y[e] = r0 * gf[e];
-              y[e + 1] = r1 * gf[e + 1];
+            for (int j = 0; j < 4; ++j) {
+              const int c = 8 * e4 + 2 * j;
+              uint32_t rp = pack_bf16x2(__uint_as_float(v[c]), __uint_as_float(v[c + 1]));  // bf16(readout)
+              rp = mul_bf16x2(rp, inv2);                                                     // bf16(. / rms)
+              float a, b;
+              unpack2(rp, a, b);
+              const float2 wv = *reinterpret_cast<const float2*>(w_s + cb * 32 + c);
+              f2_unpack(f2_mul(f2_pack(a, b), f2_pack(wv.x, wv.y)), a, b);
+              yw[j] = mul_bf16x2(pack_bf16x2(a, b), gw[j]);                                  // bf16(bf16(. * w) * gate)
             }
-            *cell = pack8(y);
+            *cell = make_uint4(yw[0], yw[1], yw[2], yw[3]);
           }
         }
         tc_fence_before();
