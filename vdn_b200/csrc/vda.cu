@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* __restrict__ p
                                                      const float* __restrict__ alpha,
                                                      const float* __restrict__ seed, int bridge,
                                                      int F, int H, const FrameBounds bounds,
-                                                     OutT* __restrict__ out) {
+                                                     OutT* __restrict__ out, int vec) {
   constexpr int R = 16;
   __shared__ float dec_b[D], dec_a[D];
   const int t = blockIdx.x, h = blockIdx.y, rb = blockIdx.z;
@@ -466,6 +466,38 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* __restrict__ p
   }
   __syncthreads();
   const int64_t plane = (int64_t)D * D;
+  if (vec) {
+    // Eight consecutive elements per thread: 32-byte loads of each bank row, one 16-byte
+    // (bf16) or 32-byte (fp32) store; every load of the thread is issued before the sums.
+    for (int e = threadIdx.x * 8; e < R * D; e += blockDim.x * 8) {
+      const int r = rb * R + e / D, kk = e % D;
+      const int64_t off = (int64_t)r * D + kk;
+      float sd[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, left[8], right[8];
+      auto load8 = [](const float* src, float* dst) {
+        const float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
+        dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
+        dst[4] = b.x; dst[5] = b.y; dst[6] = b.z; dst[7] = b.w;
+      };
+      if (seed) load8(seed + h * plane + off, sd);
+      if (has_b) load8(prefix + ((int64_t)(lo - 1) * H + h) * plane + off, left);
+      else
+        for (int i = 0; i < 8; ++i) left[i] = sd[i];
+      if (has_a) load8(suffix + ((int64_t)(hi + 1) * H + h) * plane + off, right);
+      else
+        for (int i = 0; i < 8; ++i) right[i] = sd[i];
+      float val[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) val[i] = left[i] * dec_b[kk + i] + right[i] * dec_a[kk + i];
+      const int64_t o = ((int64_t)t * H + h) * plane + off;
+      if constexpr (sizeof(OutT) == 2) {
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + o) = pack8(val);
+      } else {
+        *reinterpret_cast<float4*>(out + o) = make_float4(val[0], val[1], val[2], val[3]);
+        *reinterpret_cast<float4*>(out + o + 4) = make_float4(val[4], val[5], val[6], val[7]);
+      }
+    }
+    return;
+  }
   for (int e = threadIdx.x; e < R * D; e += blockDim.x) {
     const int r = rb * R + e / D, kk = e % D;
     const int64_t off = (int64_t)r * D + kk;
@@ -714,14 +746,15 @@ int launch_gather(const float* prefix, const float* suffix, const float* alpha,
   FrameBounds fb;
   if (int rc = fill_bounds(bounds, F, &fb)) return rc;
   const dim3 grid(F, H, d / 16);
+  const int vec = aligned16(prefix) && aligned16(suffix) && (!seed || aligned16(seed)) && aligned16(out);
   if (out_dtype == VDN_DTYPE_BF16) {
     auto* o = static_cast<__nv_bfloat16*>(out);
-    if (d == 128) gather_kernel<128, __nv_bfloat16><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o);
-    else gather_kernel<64, __nv_bfloat16><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o);
+    if (d == 128) gather_kernel<128, __nv_bfloat16><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o, vec);
+    else gather_kernel<64, __nv_bfloat16><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o, vec);
   } else if (out_dtype == VDN_DTYPE_F32) {
     auto* o = static_cast<float*>(out);
-    if (d == 128) gather_kernel<128, float><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o);
-    else gather_kernel<64, float><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o);
+    if (d == 128) gather_kernel<128, float><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o, vec);
+    else gather_kernel<64, float><<<grid, 256, 0, stream>>>(prefix, suffix, alpha, seed, bridge, F, H, fb, o, vec);
   } else {
     return set_error(VDN_ERR_TYPE, "out_dtype must be fp32 or bf16");
   }
