@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(256) stats_kernel(
 // 128B-swizzled K-major operand layout of the tensor-core scan (two 64-column
 // halves of 128 rows x 128 B per plane, 96 KB per matrix at `Tout` bytes).
 template <int D, bool SPLIT = false>
-__global__ void __launch_bounds__(256, 2) factor_kernel(const float* A, const float* B,
+__global__ void __launch_bounds__(256, 1) factor_kernel(const float* A, const float* B,
                                                         const float* __restrict__ alpha,
                                                         float* Tout, float* Jout) {
   constexpr int T = D / 16;

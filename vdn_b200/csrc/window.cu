@@ -9,7 +9,9 @@
 // the output-projection GEMM consumes directly -- the gated softmax output is
 // never materialised in bf16 on the single-GPU path.
 // One thread per 32-element block of the [T, H*d] output; lanes 4i..4i+3 pack
-// their scale bytes into one 32-bit store, as in the quantiser.
+// their scale bytes into one 32-bit store, as in the quantiser.  Capped at 64
+// registers (four CTAs, 32 warps per SM): with 90 registers two CTAs fit and the
+// loads in flight fell short of HBM (config 3: 0.232 -> 0.160 ms).
 // Reference: window_softmax_reference / decomposed window softmax and
 // apply_softmax_gate (ec-jt/vdn src/models/softmax_attention/window.py:56-111,
 // decomposed.py, hybrid_attention.py:217-222).
@@ -34,7 +36,7 @@ __device__ __forceinline__ uint16_t e4m3x2_w(float hi, float lo) {
   return r;
 }
 
-__global__ void __launch_bounds__(256) window_merge_kernel(
+__global__ void __launch_bounds__(256, 4) window_merge_kernel(
     const Partials P, int F, int S, int H, int d, const uint16_t* __restrict__ gate, int64_t g_ss,
     int64_t g_sh, uint16_t* __restrict__ out, int64_t out_ld, int64_t out_hs, uint8_t* __restrict__ q,
     uint8_t* __restrict__ s, int64_t rows_pad) {
