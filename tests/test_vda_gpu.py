@@ -84,6 +84,32 @@ def test_statistics_raw_features_vs_oracle(cuda, s):
     assert rel_l2(b.cpu().numpy(), ob) < 4e-3
 
 
+@torch.no_grad()
+def test_statistics_raw_features_extreme_inputs(cuda):
+    """SiLU inputs far below zero (the kernel raises them to -43.5 on the packed bf16
+    pair, where |silu| < 6e-18 either way) and large positive ones: A and B still
+    match the oracle, with no inf or NaN."""
+    from vdn_b200.linear_attention import vda_statistics
+    g = torch.Generator(device="cpu").manual_seed(3)
+    raw_k = torch.randn(2, 96, 2, 128, generator=g)
+    raw_v = torch.randn(2, 96, 2, 128, generator=g)
+    mask = torch.rand(raw_k.shape, generator=g) < 0.05
+    raw_k[mask] = -90.0
+    raw_v[mask] = -300.0
+    raw_k[..., 5] = 60.0
+    raw_v[..., 7] = -1e4
+    raw_k, raw_v = raw_k.bfloat16(), raw_v.bfloat16()
+    beta = torch.rand(2, 96, 2, generator=g).bfloat16()
+    a, b = vda_statistics(raw_k.to(cuda).permute(0, 2, 1, 3), raw_v.to(cuda).permute(0, 2, 1, 3),
+                          beta.to(cuda).permute(0, 2, 1), features_applied=False)
+    assert bool(torch.isfinite(a).all()) and bool(torch.isfinite(b).all())
+    kf = ovda.features(raw_k.float().numpy(), True).transpose(0, 2, 1, 3)
+    vf = ovda.features(raw_v.float().numpy(), False).transpose(0, 2, 1, 3)
+    oa, ob = ovda.frame_statistics(kf, vf, beta.float().numpy().transpose(0, 2, 1))
+    assert rel_l2(a.cpu().numpy(), oa) < 2e-3
+    assert rel_l2(b.cpu().numpy(), ob) < 4e-3
+
+
 def _stats_inputs(frames, heads, tokens, beta_scale=1.0, seed=0, d=128):
     g = torch.Generator(device="cpu").manual_seed(seed)
     shape = (frames, heads, tokens, d)
