@@ -145,9 +145,9 @@ __device__ __forceinline__ f2 f2_fma(f2 a, f2 b, f2 c) {
 // (0, 1].  The exponential is one MUFU operation; the divisor y = 1 + t lies in (1, 2],
 // so its reciprocal is taken on the FMA pipe: Newton-Raphson division from the textbook
 // linear seed 48/17 - 32/17 D for D = y / 2 in (1/2, 1] (relative error <= 1/17, squared
-// by each of three steps: below fp32 rounding).  For kernels whose MUFU / conversion pipe
-// is the limit (the gate GEMM's epilogue), this halves its load against exp + a hardware
-// reciprocal; kernels bound by issue are better off with the hardware reciprocal.
+// by each of three steps: below fp32 rounding).  It halves the MUFU / conversion load
+// against exp + a hardware reciprocal, at the price of issue slots; the gate GEMM keeps
+// it for single columns and takes full chunks in pairs that share one reciprocal.
 __device__ __forceinline__ float sigmoid_nr(float x) {
   const float t = __expf(-fabsf(x));
   const float d = 0.5f * (1.0f + t);
