@@ -125,11 +125,11 @@ class ClockSampler:
 # (x 21 / 5).  Reported as roofline "traffic" with "traffic_source" saying so.
 NCU_TRAFFIC_BYTES = {
     "mxfp8_gemm_qkv": (104.2e6 + 97.6e6) * 32760 / 4096,
-    "statistics": 164.4e6 * 21 / 5,
+    "statistics": 164.3e6 * 21 / 5,
     "factors": 13.2e6 * 21 / 5,
     "scan": 26.4e6 * 21 / 5,
     "gather": 15.8e6 * 21 / 5,
-    "readout": 215.9e6 * 21 / 5,
+    "readout": 213.6e6 * 21 / 5,
 }
 
 TRAFFIC_SOURCE = ("from a separate ncu capture of a small case of this kernel (profiles/), scaled to "
