@@ -163,7 +163,9 @@ __device__ __forceinline__ float sigmoid_nr(float x) {
 // the round-to-nearest bf16 of what the earlier parts leave (every subtraction is
 // exact in fp32, and the three 8-bit significands cover fp32's 24).  What the first
 // two parts leave has at most 8 significant bits, so the third part is that residual
-// itself (its rounding would be exact): two conversions per pair, not three.  Each
+// itself (its rounding would be exact; for |x| < 2^-103 the residual is an fp32
+// denormal and the part keeps its upper half, an error below 2^-133): two conversions
+// per pair, not three.  Each
 // conversion's packed output is the part itself; the residuals are taken in f32x2
 // pairs.  w[p] holds part p of the eight values as packed bf16 pairs (element 2i in
 // the low half).
